@@ -1,0 +1,175 @@
+/*
+ * pck_b200 — C ABI of the B200-native checked decode path (sm_100a).
+ *
+ * These entry points replace the pybind11 module `pck_kernels` of the reference project
+ * r7919/proof-carrying-kernels (src/pck/cuda/csrc/bindings.cpp:302-335) and its internal
+ * launchers (bindings.cpp:15-38). Every function takes plain device pointers, sizes and a
+ * CUDA stream (`void*` holding a cudaStream_t; NULL is the legacy default stream), launches
+ * asynchronously on that stream, and returns PCK_OK or an error code; the message of the
+ * last failing call on this host thread is available from pck_last_error().
+ *
+ * Conventions shared by all entry points:
+ *   - bfloat16 and E4M3 data are passed as untyped pointers to their bit patterns;
+ *   - matrices are row-major and contiguous; W (m, n) holds output rows;
+ *   - inputs are only read; outputs are written; scratch buffers named as such must stay
+ *     untouched by other work while a call that uses them is in flight (one stream);
+ *   - a call with m == 0 (or rows == 0) launches nothing and succeeds.
+ */
+#ifndef PCK_B200_H
+#define PCK_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PCK_OK 0
+#define PCK_ERR_ARGUMENT 1    /* a size, pointer, alignment or option is invalid */
+#define PCK_ERR_CUDA 2        /* a CUDA runtime call failed; see pck_last_error() */
+#define PCK_ERR_UNSUPPORTED 3 /* valid input this build does not handle */
+
+#define PCK_WEIGHTS_BF16 0
+#define PCK_WEIGHTS_E4M3 1
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* pck_last_error(void);
+
+/* ABI version of this library (increases when a declaration here changes). */
+int pck_abi_version(void);
+
+/*
+ * Device status word shared by every kernel of the library: bit 0 = a bounded wait gave up
+ * (the result of that launch is not valid). Synchronizes the current device, stores the
+ * word in *status and, if `clear`, resets it.
+ */
+int pck_device_status(unsigned int* status, int clear);
+
+/* ------------------------------------------------------------------------------------ */
+/* GEMV: y = W x with binary32 accumulation in the reference's summation tree.           */
+
+/*
+ * Naive tree: thread t of `threads` (a power of two in [1, 1024]) sums the contiguous
+ * columns [t*ceil(n/threads), ...) in order, then a pairwise tree (t += t + stride).
+ * Bit-exact with the reference model `emulate_gemv` (src/pck/gemv.py:14-57).
+ * Replaces bindings.cpp:73-75 / gemv_kernel.cu:204-211 (`gemv_naive`).
+ */
+int pck_gemv_naive(const void* W, const void* x, float* y, int64_t m, int64_t n, int threads,
+                   void* stream);
+
+/*
+ * Coalesced tree: chain t (threads a power of two in [32, 1024]) owns the 8-column vectors
+ * t, t + threads, ...; chains are halved within groups of 32, then across groups.
+ * Bit-exact with `emulate_gemv_coalesced(W, x, threads, 8)` (src/pck/gemv.py:71-101).
+ * Replaces bindings.cpp:77-79 / gemv_kernel.cu:182-191 (`gemv_coalesced`).
+ */
+int pck_gemv_coalesced(const void* W, const void* x, float* y, int64_t m, int64_t n,
+                       int threads, void* stream);
+
+/*
+ * E4M3 weights Q (m, n), bfloat16 x: z = Q x with the coalesced tree over 16-column
+ * vectors, bit-exact with `emulate_gemv_coalesced(Q, x, threads, 16)`. The per-row scales
+ * of the quantisation are applied by the caller afterwards (y = s * z).
+ * Replaces bindings.cpp:81-83 / gemv_kernel.cu:193-202 (`gemv_fp8`).
+ */
+int pck_gemv_fp8(const void* Q, const void* x, float* z, int64_t m, int64_t n, int threads,
+                 void* stream);
+
+/*
+ * Batched coalesced GEMV: Y (batch, m) = X (batch, n) W^T, every column of the batch
+ * bit-exact with the single-vector tree above (vec 8 for bfloat16, 16 for E4M3),
+ * batch in [1, 16]. The reference has no library counterpart; its diagnostic
+ * harness/csrc/batched_gemv.cu:25-82 computes the same product for batch <= 8.
+ */
+int pck_gemv_batched(int weight_format, const void* W, const void* X, float* Y, int64_t m,
+                     int64_t n, int64_t batch, int threads, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Blocked checksum checker (the trusted check of y = W x).                               */
+
+/*
+ * One GEMV output to check, with the bank built at weight load (src/pck/cuda/checker.py:
+ * 72-129). For every column b of the batch, check k and row block beta:
+ *   rho = c[k,beta] . x_b - r[k,beta] . y_b[beta]             (binary64, exact products)
+ *   s   = a[beta] . |x_b|                                       (binary64, rounded up)
+ *   tau = coef*s + geps*((1+u32) s + sum |y_b[beta]|) + tau_floor   (rounded up)
+ *   passed = every y in the block finite && tau finite && |rho| <= tau
+ * (the decision rule of src/pck/cuda/csrc/checker_kernel.cu:87-185). Mirrors the
+ * reference's `CheckDesc` (src/pck/cuda/csrc/checker.h:13-34), extended by a batch.
+ */
+typedef struct pck_check_desc {
+  const float* c;       /* (checks, num_blocks, n) binary32 checksums r^T W_beta        */
+  const void* a;        /* (num_blocks, n) bfloat16, rounded up                          */
+  const int8_t* r;      /* (checks, num_blocks, block) signs, +-1                        */
+  const void* x;        /* (batch, n) bfloat16                                            */
+  const float* y;       /* (batch, num_blocks*block) binary32 output to check            */
+  double* partial_cx;   /* scratch (batch, checks, num_blocks, segments)                 */
+  double* partial_s;    /* scratch (batch, num_blocks, segments)                         */
+  uint32_t* counters;   /* scratch (num_blocks,), zero between calls; left zero          */
+  uint8_t* passed;      /* out (batch, checks, num_blocks), 1 = passed                   */
+  double* rho;          /* out (batch, checks, num_blocks)                               */
+  double* tau;          /* out (batch, checks, num_blocks)                               */
+  int64_t n;
+  int32_t block;
+  int32_t num_blocks;
+  int32_t checks;
+  int32_t segments;     /* column segments per bank row, in [1, n]                        */
+  int32_t batch;        /* columns of x and y, in [1, 16]                                 */
+  int32_t reserved;
+  double coef;          /* >= gamma_h + u32, rounded up                                   */
+  double geps;          /* >= the checker's own rounding constant, rounded up             */
+  double tau_floor;     /* >= n 2^-148, rounded up                                        */
+} pck_check_desc;
+
+#define PCK_MAX_JOBS 16
+
+/*
+ * Checks up to PCK_MAX_JOBS GEMV outputs in one launch (the standalone check, run after the
+ * producing kernel has finished). Replaces bindings.cpp:221-256 (`blocked_check`) and
+ * checker_kernel.cu:189-196; the reference batches at most 8.
+ */
+int pck_blocked_check(const pck_check_desc* descs, int count, void* stream);
+
+/*
+ * One GEMV, optionally checked in the same launch.
+ * weight_format: PCK_WEIGHTS_BF16 (vec 8) or PCK_WEIGHTS_E4M3 (vec 16).
+ * If `check` is not NULL, its x and y must equal this job's X and Y; the verdict of each
+ * row block is computed in the same kernel, by the last unit of that block to finish,
+ * from the y values as stored in memory (fused production mode).
+ */
+typedef struct pck_gemv_job {
+  const void* W;                /* (m, n) weights                                         */
+  const void* X;                /* (batch, n) bfloat16                                    */
+  float* Y;                     /* (batch, m) binary32                                    */
+  int64_t m;
+  int64_t n;
+  int32_t batch;                /* [1, 16]                                                */
+  int32_t threads;              /* tree parameter, power of two in [32, 1024]             */
+  int32_t weight_format;
+  int32_t reserved;
+  const pck_check_desc* check;  /* NULL: unchecked                                        */
+} pck_gemv_job;
+
+/*
+ * Up to PCK_MAX_JOBS independent GEMVs (each optionally checked) in one persistent launch:
+ * e.g. the q, k, v projections of a decode layer with their checks. No reference
+ * counterpart: the reference launches each GEMV and the check separately.
+ */
+int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream);
+
+/*
+ * Builds a checker's bank on the device from bfloat16 W (m, n) and signs r
+ * (checks, m/block, block): c[k,beta,j] = fl32(sum_i r[k,beta,i] W[beta*block+i, j])
+ * (binary64 sum over i in order, then rounded to nearest binary32) and
+ * a[beta,j] = round_up_bf16(next_up(fl64(sum_i |W_ij|) * sum_up_factor)), where
+ * `sum_up_factor` is passed by the caller. Replaces the weight-load arithmetic of
+ * src/pck/cuda/checker.py:94-107 (torch einsum and `round_up_bf16`, :29-43).
+ */
+int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m, int64_t n,
+                   int block, int checks, double sum_up_factor, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PCK_B200_H */

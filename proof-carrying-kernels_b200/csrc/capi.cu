@@ -1,0 +1,392 @@
+// extern "C" entry points of libpck_b200.so (declared in include/pck_b200.h): argument
+// validation, launch planning and dispatch. Messages of rejected calls follow the
+// reference bindings' wording (src/pck/cuda/csrc/bindings.cpp) so callers can match them.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "pck_b200.h"
+#include "stream_plan.h"
+
+namespace pck {
+cudaError_t launch_gemv_naive(const void* W, const void* x, float* y, int64_t m, int64_t n,
+                              int threads, int sms, cudaStream_t stream);
+cudaError_t status_stream_bf16(unsigned int* value, bool clear);
+cudaError_t status_stream_e4m3(unsigned int* value, bool clear);
+cudaError_t launch_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t n,
+                              int block, int num_blocks, int checks, double factor,
+                              cudaStream_t stream);
+}  // namespace pck
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+int cuda_fail(const char* what, cudaError_t err) {
+  return fail(PCK_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(err));
+}
+
+int ok() {
+  g_error.clear();
+  return PCK_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool power_of_two(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v < 1) v = 148;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+// One job of a streaming launch, as requested by the caller.
+struct Spec {
+  const void* W;
+  const void* X;
+  float* Y;
+  int64_t m;
+  int64_t n;
+  int batch;
+  int threads;
+  int wfmt;
+  bool has_w;
+  const pck_check_desc* check;
+};
+
+int validate_check(const pck_check_desc* d) {
+  if (!d) return fail(PCK_ERR_ARGUMENT, "check descriptor is NULL");
+  if (!d->c || !d->a || !d->r || !d->x || !d->y || !d->partial_cx || !d->partial_s ||
+      !d->counters || !d->passed || !d->rho || !d->tau) {
+    return fail(PCK_ERR_ARGUMENT, "check descriptor has a NULL pointer");
+  }
+  if (d->checks < 1 || d->num_blocks < 1 || d->n < 1 || d->block < 1) {
+    return fail(PCK_ERR_ARGUMENT, "empty checker");
+  }
+  if (d->segments < 1 || d->segments > d->n) {
+    return fail(PCK_ERR_ARGUMENT, "segments must be in [1, n], got %d", d->segments);
+  }
+  if (d->batch < 1 || d->batch > pck::kMaxBatch) {
+    return fail(PCK_ERR_ARGUMENT, "check batch must be in [1, %d], got %d", pck::kMaxBatch, d->batch);
+  }
+  if (!(d->coef > 0) || !(d->geps > 0) || !(d->tau_floor > 0)) {
+    return fail(PCK_ERR_ARGUMENT, "coef, geps and floor must be positive");
+  }
+  return PCK_OK;
+}
+
+// Plans and launches the streaming kernel for `specs` (all validated by the caller except
+// for the checks done here).
+int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
+  if (specs.empty() || specs.size() > static_cast<size_t>(pck::kMaxJobs)) {
+    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %zu", pck::kMaxJobs, specs.size());
+  }
+  int wfmt = -1, threads = -1, batch = -1;
+  for (const Spec& s : specs) {
+    if (s.has_w) {
+      if (wfmt < 0) {
+        wfmt = s.wfmt;
+        threads = s.threads;
+        batch = s.batch;
+      } else if (s.wfmt != wfmt || s.threads != threads || s.batch != batch) {
+        return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share weight format, threads and batch");
+      }
+    }
+  }
+  if (wfmt < 0) {  // checks only: the tree parameters are unused
+    wfmt = pck::kWeightsBf16;
+    threads = 256;
+    batch = 1;
+  }
+  const int vec = wfmt == pck::kWeightsBf16 ? 8 : 16;
+  const int esize = wfmt == pck::kWeightsBf16 ? 2 : 1;
+
+  pck::Plan plan{};
+  bool tma = true;
+  int64_t x_bytes = 0, stage_bytes = 0;
+  std::vector<int64_t> bytes;
+  int nj = 0;
+  for (const Spec& s : specs) {
+    pck::JobPlan jb{};
+    jb.W = s.W;
+    jb.X = static_cast<const uint16_t*>(s.has_w ? s.X : s.check->x);
+    jb.Y = s.Y;
+    jb.has_w = s.has_w ? 1 : 0;
+    jb.has_check = s.check ? 1 : 0;
+    if (s.check) {
+      const pck_check_desc* d = s.check;
+      jb.m = static_cast<int64_t>(d->num_blocks) * d->block;
+      jb.n = d->n;
+      jb.batch = d->batch;
+    } else {
+      jb.m = s.m;
+      jb.n = s.n;
+      jb.batch = s.batch;
+    }
+    if (jb.m == 0) continue;
+    jb.row_bytes = jb.n * esize;
+    if (s.has_w) {
+      if (!aligned16(s.W) || !aligned16(s.X) || jb.n % vec != 0) tma = false;
+    }
+    if (s.check) {
+      const pck_check_desc* d = s.check;
+      jb.block = d->block;
+      jb.num_blocks = d->num_blocks;
+      jb.checks = d->checks;
+      jb.seg_alloc = d->segments;
+      int64_t len = (d->n + d->segments - 1) / d->segments;
+      len = (len + 7) / 8 * 8;
+      jb.seg_len = len;
+      jb.segs = static_cast<int32_t>((d->n + len - 1) / len);
+      jb.c = d->c;
+      jb.a = static_cast<const uint16_t*>(d->a);
+      jb.r = d->r;
+      jb.y_check = d->y;
+      jb.partial_cx = d->partial_cx;
+      jb.partial_s = d->partial_s;
+      jb.counters = d->counters;
+      jb.passed = d->passed;
+      jb.rho = d->rho;
+      jb.tau = d->tau;
+      jb.coef = d->coef;
+      jb.geps = d->geps;
+      jb.tau_floor = d->tau_floor;
+      const int64_t bw = s.has_w ? d->block : 0;
+      jb.period_units = bw + static_cast<int64_t>(d->checks + 1) * jb.segs;
+      jb.period_bytes = bw * jb.row_bytes + (4LL * d->checks + 2) * d->n;
+      jb.units = jb.period_units * d->num_blocks;
+      jb.total_bytes = jb.period_bytes * d->num_blocks;
+      if (!aligned16(d->c) || !aligned16(d->a) || !aligned16(d->x) || d->n % 8 != 0) tma = false;
+      stage_bytes = std::max<int64_t>(stage_bytes, 4 * len);
+    } else {
+      jb.period_units = 1;
+      jb.period_bytes = jb.row_bytes;
+      jb.units = jb.m;
+      jb.total_bytes = jb.m * jb.row_bytes;
+    }
+    if (s.has_w) stage_bytes = std::max<int64_t>(stage_bytes, jb.row_bytes);
+    x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 2);
+    plan.jobs[nj++] = jb;
+    bytes.push_back(jb.total_bytes);
+  }
+  if (nj == 0) return ok();
+
+  // Shared memory: activations, then as many stages as fit (at least two).
+  x_bytes = (x_bytes + 127) / 128 * 128;
+  stage_bytes = (stage_bytes + 127) / 128 * 128;
+  int stages = 0;
+  if (tma) {
+    const int64_t room = pck::kSmemCap - x_bytes - 8 * (2 * pck::kMaxStages + 2) - 64;
+    stages = room > 0 ? static_cast<int>(std::min<int64_t>(pck::kMaxStages, room / stage_bytes)) : 0;
+    if (stages < 2) tma = false;
+  }
+  size_t smem = 0;
+  if (tma) {
+    smem = static_cast<size_t>(x_bytes + stages * stage_bytes + 8 * (2 * stages + 2) + 16);
+    plan.stages = stages;
+    plan.stage_bytes = static_cast<int32_t>(stage_bytes);
+    plan.x_bytes = static_cast<int32_t>(x_bytes);
+  }
+
+  // CTAs: one per SM in total (two without shared-memory staging), split between the jobs
+  // in proportion to their bytes, at least one each and never more than their units.
+  const int sms = sm_count();
+  int64_t total_units = 0, total_bytes = 0;
+  for (int j = 0; j < nj; ++j) {
+    total_units += plan.jobs[j].units;
+    total_bytes += bytes[j];
+  }
+  const int64_t want = std::min<int64_t>(tma ? sms : 2LL * sms, total_units);
+  std::vector<int64_t> cnt(nj);
+  int64_t assigned = 0;
+  for (int j = 0; j < nj; ++j) {
+    const double share = static_cast<double>(want) * static_cast<double>(bytes[j]) / static_cast<double>(total_bytes);
+    cnt[j] = std::min<int64_t>(std::max<int64_t>(1, static_cast<int64_t>(share)), plan.jobs[j].units);
+    assigned += cnt[j];
+  }
+  // Remaining CTAs go, one at a time, to the job whose CTAs carry the most bytes.
+  while (assigned < want) {
+    int best = -1;
+    double load = -1.0;
+    for (int j = 0; j < nj; ++j) {
+      const double l = static_cast<double>(bytes[j]) / static_cast<double>(cnt[j]);
+      if (cnt[j] < plan.jobs[j].units && l > load) {
+        best = j;
+        load = l;
+      }
+    }
+    if (best < 0) break;
+    ++cnt[best];
+    ++assigned;
+  }
+  int64_t begin = 0;
+  for (int j = 0; j < nj; ++j) {
+    plan.jobs[j].cta_begin = static_cast<int32_t>(begin);
+    plan.jobs[j].cta_count = static_cast<int32_t>(cnt[j]);
+    begin += cnt[j];
+  }
+  plan.njobs = nj;
+  plan.threads = threads;
+
+  const int nv = threads / 32;
+  int bg = 1;
+  if (tma) {
+    const int limit = std::min(8, 64 / nv);
+    while (bg * 2 <= limit && bg * 2 <= batch) bg *= 2;
+  }
+  const unsigned grid = static_cast<unsigned>(begin);
+  const cudaError_t err = wfmt == pck::kWeightsBf16
+                              ? pck::launch_stream_bf16(plan, nv, bg, tma, grid, smem, stream)
+                              : pck::launch_stream_e4m3(plan, nv, bg, tma, grid, smem, stream);
+  if (err != cudaSuccess) return cuda_fail("streaming kernel", err);
+  return ok();
+}
+
+int check_gemv_args(const void* W, const void* x, const float* y, int64_t m, int64_t n,
+                    int threads, int min_threads) {
+  if (m < 0 || n < 0) return fail(PCK_ERR_ARGUMENT, "expected W of shape (m, n) with m, n >= 0");
+  if (threads < min_threads || threads > 1024 || !power_of_two(threads)) {
+    return fail(PCK_ERR_ARGUMENT, "threads must be a power of two in [%d, 1024], got %d", min_threads, threads);
+  }
+  if (m > 0 && n < 1) return fail(PCK_ERR_ARGUMENT, "n must be positive");
+  if (m > 0 && (!W || !x || !y)) return fail(PCK_ERR_ARGUMENT, "W, x and y must not be NULL");
+  return PCK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pck_last_error(void) { return g_error.c_str(); }
+
+int pck_abi_version(void) { return 1; }
+
+int pck_device_status(unsigned int* status, int clear) {
+  if (!status) return fail(PCK_ERR_ARGUMENT, "status must not be NULL");
+  cudaError_t err = cudaDeviceSynchronize();
+  if (err != cudaSuccess) return cuda_fail("device synchronize", err);
+  unsigned int total = 0;
+  for (auto* reader : {pck::status_stream_bf16, pck::status_stream_e4m3}) {
+    unsigned int v = 0;
+    err = reader(&v, clear != 0);
+    if (err != cudaSuccess) return cuda_fail("status read", err);
+    total |= v;
+  }
+  *status = total;
+  return ok();
+}
+
+int pck_gemv_naive(const void* W, const void* x, float* y, int64_t m, int64_t n, int threads,
+                   void* stream) {
+  if (int rc = check_gemv_args(W, x, y, m, n, threads, 1)) return rc;
+  if (m == 0) return ok();
+  const cudaError_t err = pck::launch_gemv_naive(W, x, y, m, n, threads, sm_count(),
+                                                 static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail("gemv kernel", err);
+  return ok();
+}
+
+int pck_gemv_batched(int weight_format, const void* W, const void* X, float* Y, int64_t m,
+                     int64_t n, int64_t batch, int threads, void* stream) {
+  if (weight_format != PCK_WEIGHTS_BF16 && weight_format != PCK_WEIGHTS_E4M3) {
+    return fail(PCK_ERR_ARGUMENT, "unknown weight format %d", weight_format);
+  }
+  if (int rc = check_gemv_args(W, X, Y, m, n, threads, 32)) return rc;
+  if (batch < 1 || batch > pck::kMaxBatch) {
+    return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %lld", pck::kMaxBatch, static_cast<long long>(batch));
+  }
+  if (m == 0) return ok();
+  std::vector<Spec> specs{{W, X, Y, m, n, static_cast<int>(batch), threads, weight_format, true, nullptr}};
+  return run_stream(specs, static_cast<cudaStream_t>(stream));
+}
+
+int pck_gemv_coalesced(const void* W, const void* x, float* y, int64_t m, int64_t n,
+                       int threads, void* stream) {
+  return pck_gemv_batched(PCK_WEIGHTS_BF16, W, x, y, m, n, 1, threads, stream);
+}
+
+int pck_gemv_fp8(const void* Q, const void* x, float* z, int64_t m, int64_t n, int threads,
+                 void* stream) {
+  return pck_gemv_batched(PCK_WEIGHTS_E4M3, Q, x, z, m, n, 1, threads, stream);
+}
+
+int pck_blocked_check(const pck_check_desc* descs, int count, void* stream) {
+  if (count < 1 || count > PCK_MAX_JOBS || !descs) {
+    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", PCK_MAX_JOBS, count);
+  }
+  std::vector<Spec> specs;
+  for (int i = 0; i < count; ++i) {
+    if (int rc = validate_check(descs + i)) return rc;
+    specs.push_back(Spec{nullptr, nullptr, nullptr, 0, descs[i].n, descs[i].batch, 256,
+                         PCK_WEIGHTS_BF16, false, descs + i});
+  }
+  return run_stream(specs, static_cast<cudaStream_t>(stream));
+}
+
+int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream) {
+  if (count < 1 || count > PCK_MAX_JOBS || !jobs) {
+    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", PCK_MAX_JOBS, count);
+  }
+  std::vector<Spec> specs;
+  for (int i = 0; i < count; ++i) {
+    const pck_gemv_job& jb = jobs[i];
+    if (jb.weight_format != PCK_WEIGHTS_BF16 && jb.weight_format != PCK_WEIGHTS_E4M3) {
+      return fail(PCK_ERR_ARGUMENT, "unknown weight format %d", jb.weight_format);
+    }
+    if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, jb.threads, 32)) return rc;
+    if (jb.batch < 1 || jb.batch > pck::kMaxBatch) {
+      return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %d", pck::kMaxBatch, jb.batch);
+    }
+    if (jb.check) {
+      const pck_check_desc* d = jb.check;
+      if (int rc = validate_check(d)) return rc;
+      if (d->x != jb.X || d->y != jb.Y || d->n != jb.n || d->batch != jb.batch ||
+          static_cast<int64_t>(d->num_blocks) * d->block != jb.m) {
+        return fail(PCK_ERR_ARGUMENT, "a fused check must cover the job's own x, y and shape");
+      }
+    }
+    specs.push_back(Spec{jb.W, jb.X, jb.Y, jb.m, jb.n, jb.batch, jb.threads, jb.weight_format,
+                         true, jb.check});
+  }
+  return run_stream(specs, static_cast<cudaStream_t>(stream));
+}
+
+int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m, int64_t n,
+                   int block, int checks, double sum_up_factor, void* stream) {
+  if (!W || !r || !c || !a) return fail(PCK_ERR_ARGUMENT, "W, r, c and a must not be NULL");
+  if (block < 1 || m < 1 || m % block != 0) {
+    return fail(PCK_ERR_ARGUMENT, "block=%d must be positive and divide m=%lld", block, static_cast<long long>(m));
+  }
+  if (checks < 1) return fail(PCK_ERR_ARGUMENT, "checks must be positive, got %d", checks);
+  if (n < 1) return fail(PCK_ERR_ARGUMENT, "n must be positive");
+  const int64_t nb = m / block;
+  if (nb > 65535) return fail(PCK_ERR_UNSUPPORTED, "too many row blocks (%lld > 65535)", static_cast<long long>(nb));
+  const cudaError_t err = pck::launch_bank_build(W, r, c, a, n, block, static_cast<int>(nb), checks,
+                                                 sum_up_factor, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail("bank kernel", err);
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,57 @@
+// Instantiation and launch of the streaming kernel for one weight format (included by
+// stream_bf16.cu and stream_e4m3.cu, which nvcc compiles in parallel).
+#pragma once
+
+#include "stream_kernel.cuh"
+
+namespace pck {
+
+template <int WFMT, int NV, int BG, bool kTma>
+cudaError_t launch_variant(const Plan& plan, unsigned grid, size_t smem, cudaStream_t stream) {
+  auto* fn = stream_kernel<WFMT, NV, BG, kTma>;
+  if (kTma) {
+    // The opt-in shared-memory size is a per-device function attribute: set it once per
+    // device to the largest size this library ever asks for.
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+      err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap);
+      if (err != cudaSuccess) return err;
+      configured[dev] = 1;
+    }
+  }
+  fn<<<grid, kTma ? kTmaThreads : kPlainThreads, smem, stream>>>(plan);
+  return cudaGetLastError();
+}
+
+template <int WFMT, int NV>
+cudaError_t launch_nv(const Plan& plan, int bg, bool tma, unsigned grid, size_t smem,
+                      cudaStream_t stream) {
+  if (!tma) return launch_variant<WFMT, NV, 1, false>(plan, grid, smem, stream);
+  switch (bg) {
+    case 1: return launch_variant<WFMT, NV, 1, true>(plan, grid, smem, stream);
+    case 2: return launch_variant<WFMT, NV, (NV <= 32 ? 2 : 1), true>(plan, grid, smem, stream);
+    case 4: return launch_variant<WFMT, NV, (NV <= 16 ? 4 : 1), true>(plan, grid, smem, stream);
+    case 8: return launch_variant<WFMT, NV, (NV <= 8 ? 8 : 1), true>(plan, grid, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int WFMT>
+cudaError_t launch_format(const Plan& plan, int nv, int bg, bool tma, unsigned grid, size_t smem,
+                          cudaStream_t stream) {
+  switch (nv) {
+    case 1: return launch_nv<WFMT, 1>(plan, bg, tma, grid, smem, stream);
+    case 2: return launch_nv<WFMT, 2>(plan, bg, tma, grid, smem, stream);
+    case 4: return launch_nv<WFMT, 4>(plan, bg, tma, grid, smem, stream);
+    case 8: return launch_nv<WFMT, 8>(plan, bg, tma, grid, smem, stream);
+    case 16: return launch_nv<WFMT, 16>(plan, bg, tma, grid, smem, stream);
+    case 32: return launch_nv<WFMT, 32>(plan, bg, tma, grid, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace pck

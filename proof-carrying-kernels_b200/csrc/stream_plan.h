@@ -1,0 +1,91 @@
+// Launch plan of the persistent streaming kernel (host and device view).
+//
+// A launch processes up to kMaxJobs jobs. A job is a GEMV over W (m, n) with its
+// activations X (batch, n) and outputs Y (batch, m), a check of one GEMV output against
+// its checksum bank, or both (a checked GEMV). Its work is a sequence of "units", each a
+// contiguous byte range that one warp reduces against the activations:
+//   - a W row (n weights)                         -> y[b, row] for every column b
+//   - a segment of a checksum row c[k, beta, :]   -> partial c . x_b (binary64)
+//   - a segment of a bound row a[beta, :]         -> partial a . |x_b| (binary64, up)
+// For a checked job the units of row block beta are laid out contiguously:
+//   [block W rows (fused only)] [checks x segments c-segments] [segments a-segments]
+// and the last unit of the block to finish (an atomic ticket) computes the verdict.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace pck {
+
+constexpr int kMaxJobs = 16;
+constexpr int kConsumerWarps = 8;
+constexpr int kTmaThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kPlainThreads = kConsumerWarps * 32;
+constexpr int kMaxStages = 32;
+constexpr int kSmemCap = 232448;  // 227 KB: the opt-in dynamic shared memory per CTA
+constexpr int kMaxBatch = 16;
+constexpr int kWeightsBf16 = 0;
+constexpr int kWeightsE4m3 = 1;
+
+struct JobPlan {
+  // GEMV part (has_w): W (m, n) rows are units.
+  const void* W;
+  const uint16_t* X;  // (batch, n) bfloat16 bits
+  float* Y;           // (batch, m)
+  int64_t m;
+  int64_t n;
+  int64_t row_bytes;  // n * element size
+  int32_t batch;
+  int32_t has_w;
+  // check part (has_check)
+  int32_t has_check;
+  int32_t block;
+  int32_t num_blocks;
+  int32_t checks;
+  int32_t seg_alloc;  // segment stride of the scratch arrays
+  int32_t segs;       // effective segments (seg_len-aligned)
+  int64_t seg_len;    // columns per segment (multiple of 8)
+  const float* c;
+  const uint16_t* a;
+  const int8_t* r;
+  const float* y_check;  // (batch, m) the output whose blocks are checked
+  double* partial_cx;
+  double* partial_s;
+  uint32_t* counters;
+  uint8_t* passed;
+  double* rho;
+  double* tau;
+  double coef;
+  double geps;
+  double tau_floor;
+  // partition
+  int64_t units;         // total units
+  int64_t period_units;  // units per row block (checked) or 1 (unchecked)
+  int64_t period_bytes;  // bytes per period
+  int64_t total_bytes;
+  int32_t cta_begin;
+  int32_t cta_count;
+  int32_t x_fp8_fma;     // host hint unused by the kernel (kept zero)
+  int32_t pad;
+};
+
+struct Plan {
+  JobPlan jobs[kMaxJobs];
+  int32_t njobs;
+  int32_t stages;
+  int32_t stage_bytes;
+  int32_t x_bytes;
+  int32_t threads;      // tree parameter T (all W jobs share it)
+  int32_t per_pad;
+};
+
+// Host-side launch of one instantiation family (stream_bf16.cu, stream_e4m3.cu). nv is
+// threads / 32, bg the batch columns reduced together, tma the staged path.
+cudaError_t launch_stream_bf16(const Plan& plan, int nv, int bg, bool tma, unsigned grid,
+                               size_t smem, cudaStream_t stream);
+cudaError_t launch_stream_e4m3(const Plan& plan, int nv, int bg, bool tma, unsigned grid,
+                               size_t smem, cudaStream_t stream);
+
+}  // namespace pck

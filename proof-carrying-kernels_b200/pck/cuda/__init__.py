@@ -1,0 +1,32 @@
+"""GPU entry points (the drop-in for the reference's `pck.cuda`, src/pck/cuda/__init__.py)."""
+
+from pck.cuda._lib import device_status
+from pck.cuda.checker import (
+    DEFAULT_BLOCK,
+    CheckResult,
+    GpuBlockedChecker,
+    PendingCheck,
+    SideStreamChecker,
+    check_many,
+    checked_gemvs,
+    gemv_checked,
+    round_up_bf16,
+)
+from pck.cuda.gemv import gemv_coalesced, gemv_fp8, gemv_naive, quantize_fp8
+
+__all__ = [
+    "DEFAULT_BLOCK",
+    "CheckResult",
+    "GpuBlockedChecker",
+    "PendingCheck",
+    "SideStreamChecker",
+    "check_many",
+    "checked_gemvs",
+    "device_status",
+    "gemv_checked",
+    "gemv_coalesced",
+    "gemv_fp8",
+    "gemv_naive",
+    "quantize_fp8",
+    "round_up_bf16",
+]
