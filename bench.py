@@ -1,0 +1,432 @@
+"""Checked decode-layer benchmark (the driver's contract: one JSON line from rank 0).
+
+Workload: the Llama-3-8B decode-layer GEMV set (q 4096x4096, k/v 1024x4096, o 4096x4096,
+gate/up 14336x4096, down 4096x14336), bfloat16 weights ~N(0, 0.02^2), activations ~N(0, 1)
+with 1% outlier channels x20, every output checked by the trusted blocked checker
+(b = 128, K = 1). A step is one decode layer: four launches of the persistent streaming
+kernel (q/k/v share their input, o, gate/up share theirs, down), each with its checks
+fused, captured in a CUDA graph. With N GPUs every matrix is row-sharded by whole checker
+blocks and one NCCL all-gather per step assembles the outputs and verdict bits.
+
+metric: checked-GEMV HBM throughput = algorithmic bytes of the step (weights, activations,
+outputs, checksum bank, verdicts) / device time, GB/s, over all ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "proof-carrying-kernels_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "checked GEMV HBM GB/s (Llama-3-8B decode layer, b=128 blocks, K=1)"
+UNIT = "GB/s"
+L2_BYTES = 126 * 2**20
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text())
+        except ValueError:
+            pass
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per launch of the streaming kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "stream_kernel_decode_layer.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_step:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")  # fmt: skip
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"pck_clocks_{os.getpid()}.csv"
+
+    def __enter__(self) -> "ClockSampler":
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index)],
+                stdout=self.path.open("w"), stderr=subprocess.DEVNULL,
+            )  # fmt: skip
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in self.path.read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}  # fmt: skip
+
+
+def outlier_x(n: int, batch: int, gen: torch.Generator) -> torch.Tensor:
+    x = torch.randn(batch, n, generator=gen)
+    for b in range(batch):
+        idx = torch.randperm(n, generator=gen)[: max(1, n // 100)]
+        x[b, idx] *= 20.0
+    return x.bfloat16()
+
+
+def build_layer(args, rank: int, world: int, device: torch.device):
+    """Sharded weights, inputs, checkers and the launch objects of one decode layer."""
+    from pck.cuda import GpuBlockedChecker
+    from pck.cuda.plan import LLAMA3_8B_GROUPS, GemvLaunch
+    from pck.cuda.sharded import PackedOutputs, shard_rows
+    from pck.fp import tree_height
+
+    names = [p for g in LLAMA3_8B_GROUPS for p in g]
+    ys = PackedOutputs([m for _, m, _ in names], args.block, world, rank, device, batch=args.batch)
+    vs = PackedOutputs([m // args.block for _, m, _ in names], 1, world, rank, device, batch=args.checks,
+                       dtype=torch.bool)  # fmt: skip
+    gen = torch.Generator().manual_seed(0)
+    groups, plain, xs, j = [], [], [], 0
+    for group in LLAMA3_8B_GROUPS:
+        n = group[0][2]
+        x = outlier_x(n, args.batch, gen).to(device)
+        x = x[0].contiguous() if args.batch == 1 else x.contiguous()
+        xs.append(x)
+        items, items_plain, y_views, p_views = [], [], [], []
+        for _name, m, nn in group:
+            shard = shard_rows(m, args.block, world, rank)
+            dgen = torch.Generator(device=device).manual_seed(1000 + j)
+            W = (torch.randn(m, nn, generator=dgen, device=device) * 0.02).bfloat16()
+            W = W[shard.row0 : shard.row1].contiguous()
+            checker = GpuBlockedChecker(W, args.block, tree_height(nn, args.threads, 8), checks=args.checks,
+                                        generator=torch.Generator().manual_seed(2000 + j))  # fmt: skip
+            items.append((W, x, checker))
+            items_plain.append((W, x, None))
+            y_views.append(ys.local_view(j))
+            p_views.append(vs.local_view(j))
+            j += 1
+        groups.append(GemvLaunch(items, args.threads, ys=y_views, passed=p_views))
+        plain.append(GemvLaunch(items_plain, args.threads))
+    torch.cuda.synchronize()
+    return groups, plain, xs, ys, vs
+
+
+def cuda_graph(fn) -> torch.cuda.CUDAGraph:
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def timed(graph: torch.cuda.CUDAGraph, steps: int, warmup: int, world: int) -> float:
+    """Seconds per step: max over ranks of the CUDA-event time of ``steps`` replays."""
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms / 1e3 / steps
+
+
+def e2e_step_time(groups, xs, ys, vs, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
+    """The public launch API with host buffers: every step copies the layer's activations
+    from pinned host memory, launches, gathers and copies outputs and verdicts back."""
+    hx = [x.cpu().pin_memory() for x in xs]
+    hy = torch.empty(ys.gathered.shape, dtype=ys.gathered.dtype, pin_memory=True)
+    hv = torch.empty(vs.gathered.shape, dtype=vs.gathered.dtype, pin_memory=True)
+
+    def step() -> None:
+        for x, h in zip(xs, hx, strict=True):
+            x.copy_(h, non_blocking=True)
+        for g in groups:
+            g.launch()
+        if world > 1:
+            ys.gather()
+            vs.gather()
+        else:
+            ys.gathered.copy_(ys.local)
+            vs.gathered.copy_(vs.local)
+        hy.copy_(ys.gathered, non_blocking=True)
+        hv.copy_(vs.gathered, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    h2d = sum(h.numel() * h.element_size() for h in hx)
+    d2h = hy.numel() * hy.element_size() + hv.numel() * hv.element_size()
+    return ms / 1e3 / steps, h2d, d2h
+
+
+def host_layer(args, gpu_groups=None):
+    """The layer on the host for the CPU legs: same seeds, same checker banks (copied from
+    the GPU when it exists, built on the CPU otherwise)."""
+    from oracle.checker import gpu_bank
+    from oracle.cpu_baseline import HostMatrix
+    from pck.cuda.plan import LLAMA3_8B_GROUPS
+    from pck.fp import tree_height
+
+    gen = torch.Generator().manual_seed(0)
+    mats, j = [], 0
+    for gi, group in enumerate(LLAMA3_8B_GROUPS):
+        n = group[0][2]
+        x = outlier_x(n, 1, gen)[0]
+        for k, (_name, m, nn) in enumerate(group):
+            if gpu_groups is not None:
+                W, _, ch = gpu_groups[gi].items[k]
+                Wc = W.cpu()
+                c, a, r = ch.c.cpu().numpy(), ch.a.float().cpu().numpy(), ch.r.cpu().numpy()
+                coef, geps, floor = ch.coef, ch.geps, ch.tau_floor
+            else:
+                Wc = (torch.randn(m, nn, generator=torch.Generator().manual_seed(1000 + j)) * 0.02).bfloat16()
+                bank = gpu_bank(Wc, args.block, tree_height(nn, args.threads, 8), args.checks,
+                                torch.Generator().manual_seed(2000 + j), segments=1)  # fmt: skip
+                c, a, r = bank["c"].numpy(), bank["a"].float().numpy(), bank["r"].numpy()
+                coef, geps, floor = bank["coef"], bank["geps"], bank["tau_floor"]
+            mats.append(HostMatrix(Wc.view(torch.uint16).numpy(), x.view(torch.uint16).numpy(),
+                                   c.astype(np.float64), a.astype(np.float64), r.astype(np.float64),
+                                   coef, geps, floor))  # fmt: skip
+            j += 1
+    return mats
+
+
+def layer_bytes(mats) -> int:
+    total = 0
+    for mat in mats:
+        m, n = mat.W_bits.shape
+        K, nb, _ = mat.c.shape
+        total += 2 * m * n + 2 * n + 4 * m + K * nb * n * 4 + nb * n * 2 + mat.r.size + K * nb * 17
+    return total
+
+
+def run_reference(args) -> None:
+    """The reference arm: the reference's CPU path (the oracle port) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle.cpu_baseline import checked_step
+    from oracle.gemv import host_threads
+
+    mats = host_layer(args)
+    cores = host_threads()
+    step_bytes = layer_bytes(mats)
+    for _ in range(max(1, args.warmup)):
+        checked_step(mats, args.threads, cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        checked_step(mats, args.threads, cores)
+    per_step = (time.perf_counter() - t0) / args.steps
+    value = step_bytes / per_step / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; weights N(0,0.02^2), activations N(0,1) with 1% outliers x20)",
+        "config": {"workload": "llama3-8b decode layer GEMV set + blocked check (reference CPU path)",
+                   "batch": 1, "block": args.block, "checks": args.checks, "threads": args.threads},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"the whole checked layer, {args.steps} steps (oracle/gemv_ref.c + NumPy check)"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }  # fmt: skip
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=2000)
+    parser.add_argument("--warmup", type=int, default=50)
+    parser.add_argument("--impl", choices=["pck", "reference"], default="pck")
+    parser.add_argument("--batch", type=int, default=1)
+    parser.add_argument("--block", type=int, default=128)
+    parser.add_argument("--checks", type=int, default=1)
+    parser.add_argument("--threads", type=int, default=256)
+    parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=device)  # fmt: skip
+
+    groups, plain, xs, ys, vs = build_layer(args, rank, world, device)
+    step_bytes_local = sum(g.algorithmic_bytes for g in groups)
+
+    def checked_step() -> None:
+        for g in groups:
+            g.launch()
+        if world > 1:
+            ys.gather()
+            vs.gather()
+
+    def plain_step() -> None:
+        for g in plain:
+            g.launch()
+
+    graph_checked = cuda_graph(checked_step)
+    graph_plain = cuda_graph(plain_step)
+    # correctness of the timed path: every block of the honest layer passes
+    graph_checked.replay()
+    torch.cuda.synchronize()
+    all_passed = bool(vs.local.all()) if world == 1 else None
+
+    gpu_index = local
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if visible:
+        try:
+            gpu_index = int(visible.split(",")[local])
+        except (ValueError, IndexError):
+            pass
+    with ClockSampler(gpu_index) as clocks:
+        t_checked = timed(graph_checked, args.steps, args.warmup, world)
+        t_plain = timed(graph_plain, args.steps, args.warmup, world)
+    clock = clocks.summary()
+    t_e2e, h2d, d2h = e2e_step_time(groups, xs, ys, vs, max(20, args.steps // 10), args.warmup, world)
+
+    total_bytes = torch.tensor([float(step_bytes_local)], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(total_bytes)
+    step_bytes = float(total_bytes.item())
+    value = step_bytes / t_checked / 1e9
+    peaks = measured_peaks()
+    peak = float(peaks["hbm_gbs"])
+    traffic = profile_traffic()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.cpu_baseline import time_checked_layer
+
+        mats = host_layer(args, groups)
+        timing = time_checked_layer(mats, args.threads, min_seconds=args.cpu_seconds)
+        cpu_value = layer_bytes(mats) * timing["steps"] / timing["seconds"] / 1e9
+        cpu = {"value": round(cpu_value, 3), "unit": UNIT, "cores": timing["cores"], "kind": "port",
+               "sample": f"{timing['steps']} whole checked layers in {timing['seconds']:.1f} s "
+                         "(oracle/gemv_ref.c over all host threads + NumPy check)"}  # fmt: skip
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_checked * 1e3, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; weights N(0,0.02^2), activations N(0,1) with 1% outliers x20)",
+            "config": {
+                "workload": "llama3-8b decode layer GEMV set (q,k,v,o,gate,up,down) + fused blocked check",
+                "batch": args.batch, "block": args.block, "checks": args.checks, "threads": args.threads,
+                "launches_per_step": len(groups), "parallelism": f"row-shard x{world}" if world > 1 else "single",
+                "l2": "inputs larger than L2 (436 MB of weights per step, 126 MB L2)",
+                "graph": "CUDA graph of one step, replayed",
+            },
+            "checker_overhead_pct": round((t_checked / t_plain - 1) * 100, 2),
+            "unchecked_ms_per_step": round(t_plain * 1e3, 5),
+            "all_blocks_passed": all_passed,
+            "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(value / world / peak, 4),
+                         "traffic": traffic,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"},
+            "e2e": {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e * 1e3, 4)},
+            "gpu_launches": len(groups) * args.steps,
+            "clocks": clock,
+            "cpu_baseline": cpu,
+        }  # fmt: skip
+        print(json.dumps(line), flush=True)
+    del graph_checked, graph_plain
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -12,7 +12,9 @@ Three restatements of the reference:
    87-185) evaluated with exact arithmetic: rho is the correctly rounded exact residual
    c.x - r.y; the parts of tau that the kernel bounds from above (a.|x| and sum |y|) are
    replaced by the smallest binary64 upper bounds of their exact values; tau then follows
-   checker_kernel.cu:176-183 with every operation rounded upward. Any sound GPU
+   checker_kernel.cu:176-183 with every operation rounded upward; when a.|x| exceeds the
+   binary32 range, where the reference's binary32 bound sums overflow, tau is infinite
+   and the block fails closed (reference tests/gpu/test_checker_cuda.py:241-252). Any sound GPU
    implementation returns a tau at least this large and a rho within its own rounding of
    this one, so verdicts agree except within that rounding of |rho| = tau.
 """
@@ -205,6 +207,7 @@ def _ru_add(a: float, b: float) -> float:
 
 
 ONE_PLUS_U32 = 1.0 + U32  # exact in binary64
+FLOAT_MAX = float(np.finfo(np.float32).max)
 
 
 def gpu_verdict(c: np.ndarray, a: np.ndarray, r: np.ndarray, x: np.ndarray, y: np.ndarray,
@@ -238,6 +241,10 @@ def gpu_verdict(c: np.ndarray, a: np.ndarray, r: np.ndarray, x: np.ndarray, y: n
         cabs = _ru_mul(ONE_PLUS_U32, s)
         eps = _ru_mul(geps, _ru_add(cabs, yabs))
         t = _ru_add(_ru_add(_ru_mul(coef, s), eps), tau_floor)
+        if not s <= FLOAT_MAX:
+            # a.|x| beyond binary32: the checked kernel's no-overflow hypothesis fails, and the
+            # reference's binary32 bound sums overflow to inf: fail closed
+            t = math.inf
         for k in range(K):
             cx = c[k, beta].astype(np.float64) * x64  # binary32 * bfloat16: exact in binary64
             if finite[beta]:

@@ -392,6 +392,7 @@ static __device__ __noinline__ void merge_block(const JobPlan& jb, int64_t beta,
   const int64_t nb = jb.num_blocks;
   const int64_t ldy = jb.m;
   constexpr double kOnePlusU32 = 1.0 + 0x1p-24;
+  constexpr double kFloatMax = 3.4028234663852886e38;
   for (int col = 0; col < jb.batch; ++col) {
     const float* yb = jb.y_check + col * ldy + beta * blk;
     double yabs = 0.0;
@@ -424,7 +425,10 @@ static __device__ __noinline__ void merge_block(const JobPlan& jb, int64_t beta,
         const double rho = __dsub_rn(cx, ry);
         const double cabs = __dmul_ru(kOnePlusU32, s_total);
         const double eps = __dmul_ru(jb.geps, __dadd_ru(cabs, yabs));
-        const double tau = __dadd_ru(__dadd_ru(__dmul_ru(jb.coef, s_total), eps), jb.tau_floor);
+        double tau = __dadd_ru(__dadd_ru(__dmul_ru(jb.coef, s_total), eps), jb.tau_floor);
+        // Beyond the binary32 range of a.|x| the checked kernel's rounding model (no
+        // overflow) cannot hold: the threshold is unbounded and the block fails closed.
+        if (!(s_total <= kFloatMax)) tau = __longlong_as_double(0x7ff0000000000000LL);
         const int64_t o = (static_cast<int64_t>(col) * jb.checks + k) * nb + beta;
         jb.passed[o] = (!bad && isfinite(tau) && fabs(rho) <= tau) ? 1 : 0;
         jb.rho[o] = rho;

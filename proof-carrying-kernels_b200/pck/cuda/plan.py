@@ -1,0 +1,103 @@
+"""Pre-validated launches for a decode loop: the tensors of a group of checked GEMVs are
+fixed once, their C descriptors built once, and `launch()` issues the single
+`pck_gemv_checked` call — cheap enough per token, and capturable in a CUDA graph.
+
+`CheckedLayer` strings such launches into a transformer decode layer's projections
+(q/k/v share an input, o, gate/up share an input, down), each group one persistent
+launch with its checks fused.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections.abc import Sequence
+
+import torch
+
+from pck.cuda import _lib
+from pck.cuda._ext import extension, on_device, stream_handle
+from pck.cuda.checker import CheckResult, GpuBlockedChecker
+
+
+class GemvLaunch:
+    """One launch of up to 16 GEMVs y_i = W_i x_i, each optionally checked.
+
+    ``items``: (W, x, checker or None). W all bfloat16 or all E4M3, x (n,) or (B, n)
+    bfloat16. ``ys`` may give preallocated outputs (e.g. views into one packed buffer);
+    otherwise they are allocated. The results are rewritten by every launch.
+    """
+
+    def __init__(self, items: Sequence[tuple[torch.Tensor, torch.Tensor, GpuBlockedChecker | None]],
+                 threads: int = 256, ys: Sequence[torch.Tensor] | None = None,
+                 passed: Sequence[torch.Tensor | None] | None = None) -> None:  # fmt: skip
+        if not 1 <= len(items) <= _lib.MAX_JOBS:
+            raise ValueError(f"a launch holds 1 to {_lib.MAX_JOBS} GEMVs, got {len(items)}")
+        W0 = items[0][0]
+        self.device = W0.device
+        self.fmt = _lib.PCK_WEIGHTS_E4M3 if W0.dtype == torch.float8_e4m3fn else _lib.PCK_WEIGHTS_BF16
+        want = torch.float8_e4m3fn if self.fmt == _lib.PCK_WEIGHTS_E4M3 else torch.bfloat16
+        ext = extension()
+        self.lib = ext.lib
+        self.count = len(items)
+        self._descs = (_lib.CheckDesc * self.count)()
+        self._jobs = (_lib.GemvJob * self.count)()
+        self.items = list(items)
+        self.ys: list[torch.Tensor] = []
+        self.results: list[CheckResult | None] = []
+        for g, (W, x, ch) in enumerate(items):
+            if W.dtype != want or x.dtype != torch.bfloat16 or W.device != self.device or x.device != self.device:
+                raise RuntimeError("W must share one format and device with the others, x bfloat16")
+            if not (W.is_contiguous() and x.is_contiguous()) or x.size(-1) != W.size(1):
+                raise RuntimeError("expected contiguous W (m, n) and x (n,) or (B, n)")
+            shape = (*x.shape[:-1], W.size(0))
+            y = ys[g] if ys is not None else torch.empty(shape, dtype=torch.float32, device=self.device)
+            if tuple(y.shape) != shape or y.dtype != torch.float32 or not y.is_contiguous():
+                raise RuntimeError(f"y must be a contiguous float32 tensor of shape {shape}")
+            self.ys.append(y)
+            job = self._jobs[g]
+            job.W, job.X, job.Y = W.data_ptr(), x.data_ptr(), y.data_ptr()
+            job.m, job.n = W.size(0), W.size(1)
+            job.batch = x.size(0) if x.dim() == 2 else 1
+            job.threads, job.weight_format = threads, self.fmt
+            if ch is None:
+                job.check = None
+                self.results.append(None)
+                continue
+            c, a, r, pcx, ps, ctr, coef, geps, floor = ch.check_args(x)
+            out = ext.describe(c, a, r, x, y, pcx, ps, ctr, coef, geps, floor, self.device, self._descs[g])
+            p = passed[g] if passed is not None else None
+            if p is not None:  # write the verdict bits into the caller's buffer
+                if p.numel() != out[0].numel() or p.dtype != torch.bool or not p.is_contiguous():
+                    raise RuntimeError("passed must be a contiguous bool tensor of the check's size")
+                self._descs[g].passed = p.data_ptr()
+                out = (p.view(out[0].shape), out[1], out[2])
+            self.results.append(CheckResult(*out))
+            job.check = ctypes.pointer(self._descs[g])
+
+    def launch(self) -> None:
+        """Issue the launch on the current stream."""
+        with on_device(self.device):
+            rc = self.lib.pck_gemv_checked(self._jobs, self.count, stream_handle(self.device))
+        _lib.check(rc, "checked gemv kernel")
+
+    @property
+    def algorithmic_bytes(self) -> int:
+        """Bytes the launch must move at least: W, x, y and, for checked items, the bank
+        (c, a, r) and the verdict outputs."""
+        total = 0
+        for (W, x, ch), y, res in zip(self.items, self.ys, self.results, strict=True):
+            total += W.numel() * W.element_size() + x.numel() * 2 + y.numel() * 4
+            if ch is not None:
+                total += ch.c.numel() * 4 + ch.a.numel() * 2 + ch.r.numel()
+                total += res.passed.numel() * (1 + 8 + 8)
+        return total
+
+
+# Llama-3-8B decode-layer projections: (name, m, n) with hidden 4096, 8 KV heads of 128,
+# MLP 14336; the groups share one input and form one launch each.
+LLAMA3_8B_GROUPS: list[list[tuple[str, int, int]]] = [
+    [("q", 4096, 4096), ("k", 1024, 4096), ("v", 1024, 4096)],
+    [("o", 4096, 4096)],
+    [("gate", 14336, 4096), ("up", 14336, 4096)],
+    [("down", 4096, 14336)],
+]

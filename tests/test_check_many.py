@@ -1,0 +1,185 @@
+"""Batched checks and the fused checked GEMV (the reference's tests/gpu/test_check_many.py
+and tests/gpu/test_side_stream.py, plus the one-launch GEMV + check of this build)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import checker as ochk
+from oracle.fp import tree_height
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
+
+THREADS = 128
+CONFIGS = [  # (m, n, block, checks, segments)
+    (512, 4096, 64, 1, None),
+    (1024, 512, 32, 2, 1),
+    (256, 14336, 128, 4, 7),
+    (64, 1000, 8, 1, 3),
+    (2048, 4096, 256, 2, None),
+]
+
+
+def make(m: int, n: int, block: int, checks: int, segments, seed: int):
+    from pck.cuda import GpuBlockedChecker, gemv_coalesced
+
+    gen = torch.Generator().manual_seed(seed)
+    W = (torch.randn(m, n, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+    x = torch.randn(n, generator=gen).to(torch.bfloat16).cuda()
+    checker = GpuBlockedChecker(W, block, tree_height(n, THREADS, vec=8), checks=checks, generator=gen,
+                                segments=segments)  # fmt: skip
+    return checker, x, gemv_coalesced(W, x, THREADS), W
+
+
+def test_batch_matches_individual_checks() -> None:
+    from pck.cuda import check_many
+
+    items = [make(*cfg, seed=i) for i, cfg in enumerate(CONFIGS)]
+    batched = check_many([it[:3] for it in items])
+    for (checker, x, y, _), res in zip(items, batched, strict=True):
+        alone = checker.check(x, y)
+        assert torch.equal(res.passed, alone.passed)
+        assert torch.equal(res.rho, alone.rho)
+        assert torch.equal(res.tau, alone.tau)
+        assert res.verdict.all()
+
+
+def test_more_than_one_launch_and_fault_isolation() -> None:
+    from pck.cuda import check_many
+
+    items = [make(*CONFIGS[i % len(CONFIGS)], seed=10 + i)[:3] for i in range(11)]
+    checker, x, y = items[9]
+    bad = y.clone()
+    bad[3] = float("inf")
+    items[9] = (checker, x, bad)
+    results = check_many(items)
+    assert len(results) == 11
+    for i, res in enumerate(results):
+        if i == 9:
+            assert not res.verdict[0] and res.verdict[1:].all()
+        else:
+            assert res.verdict.all()
+
+
+def test_rejects_same_checker_twice() -> None:
+    from pck.cuda import check_many
+
+    item = make(*CONFIGS[0], seed=0)[:3]
+    with pytest.raises(ValueError, match="once"):
+        check_many([item, item])
+
+
+def test_extension_rejects_bad_batches() -> None:
+    from pck.cuda._ext import extension
+
+    checker, x, y, _ = make(*CONFIGS[0], seed=0)
+    args = [checker.c, checker.a, checker.r, x, y, checker._partial_cx, checker._partial_s, checker._counters,
+            checker.coef, checker.geps, checker.tau_floor]  # fmt: skip
+    with pytest.raises(RuntimeError, match="batch size"):
+        extension().blocked_check(*([] for _ in args))
+    with pytest.raises(RuntimeError, match="batch size"):
+        extension().blocked_check(*([a] * 9 for a in args))
+    lists = [[a] for a in args]
+    lists[4] = [y, y]
+    with pytest.raises(RuntimeError, match="same length"):
+        extension().blocked_check(*lists)
+
+
+@pytest.mark.parametrize("cfg", CONFIGS)
+def test_fused_gemv_and_check_equal_the_separate_launches(cfg) -> None:
+    from pck.cuda import gemv_checked
+
+    checker, x, y_sep, W = make(*cfg, seed=3)
+    alone = checker.check(x, y_sep)
+    y, res = gemv_checked(W, x, checker, THREADS)
+    assert torch.equal(y.view(torch.int32), y_sep.view(torch.int32))  # same bits
+    assert torch.equal(res.passed, alone.passed)
+    assert torch.equal(res.rho, alone.rho)
+    assert torch.equal(res.tau, alone.tau)
+    assert res.verdict.all()
+
+
+def test_layer_in_one_launch_matches_oracle() -> None:
+    """q, k, v, o, gate, up, down of a Llama-3-8B layer (row counts scaled down 8x), each
+    checked at b = 128, in one persistent launch."""
+    from pck.cuda import GpuBlockedChecker, checked_gemvs
+
+    shapes = [(512, 4096), (128, 4096), (128, 4096), (512, 4096), (1792, 4096), (1792, 4096), (512, 14336)]
+    gen = torch.Generator().manual_seed(11)
+    items = []
+    for m, n in shapes:
+        W = (torch.randn(m, n, generator=gen) * 0.02).bfloat16().cuda()
+        x = torch.randn(n, generator=gen).bfloat16().cuda()
+        items.append((W, x, GpuBlockedChecker(W, 128, tree_height(n, 256, 8), checks=1, generator=gen)))
+    out = checked_gemvs(items, 256)
+    from oracle.gemv import gemv_coalesced_c
+
+    for (W, x, ch), (y, res) in zip(items, out, strict=True):
+        ref_y = gemv_coalesced_c(W.view(torch.uint16).cpu().numpy(), x.view(torch.uint16).cpu().numpy(), 256, 8)
+        np.testing.assert_array_equal(y.cpu().numpy().view(np.uint32), ref_y.view(np.uint32))
+        ref = ochk.gpu_verdict(ch.c.cpu().numpy(), ch.a.float().cpu().numpy(), ch.r.cpu().numpy(),
+                               x.float().cpu().numpy(), ref_y, ch.coef, ch.geps, ch.tau_floor)  # fmt: skip
+        np.testing.assert_array_equal(res.passed.cpu().numpy(), ref["passed"])
+        assert res.verdict.all()
+
+
+def test_fused_check_catches_a_fault_planted_in_the_bank_path() -> None:
+    """A fused launch whose y disagrees with the bank (the bank built for other weights)
+    fails every block: the verdict reads y as stored and recomputes c . x independently."""
+    from pck.cuda import GpuBlockedChecker, gemv_checked
+
+    gen = torch.Generator().manual_seed(5)
+    W = (torch.randn(512, 4096, generator=gen) * 0.02).bfloat16().cuda()
+    W2 = W.clone()
+    W2[::3] *= 1.5  # every block has perturbed rows
+    x = torch.randn(4096, generator=gen).bfloat16().cuda()
+    checker = GpuBlockedChecker(W2, 128, tree_height(4096, 256, 8), checks=2, generator=gen)
+    _, res = gemv_checked(W, x, checker)
+    assert not res.verdict.any()
+
+
+def test_batched_check_columns_match_single_checks() -> None:
+    from pck.cuda import GpuBlockedChecker, gemv_coalesced
+
+    gen = torch.Generator().manual_seed(21)
+    W = (torch.randn(1024, 4096, generator=gen) * 0.02).bfloat16().cuda()
+    X = torch.randn(4, 4096, generator=gen).bfloat16().cuda()
+    ch = GpuBlockedChecker(W, 128, tree_height(4096, 256, 8), checks=2, generator=gen)
+    Y = gemv_coalesced(W, X, 256)
+    Y[2, 300] += 1.0
+    res = ch.check(X, Y)
+    assert res.passed.shape == (4, 2, 8)
+    for b in range(4):
+        alone = ch.check(X[b].contiguous(), Y[b].contiguous())
+        assert torch.equal(res.passed[b], alone.passed)
+        assert torch.equal(res.rho[b], alone.rho)
+    assert not res.verdict[2, 300 // 128] and res.verdict.sum() == 4 * 8 - 1
+
+
+def test_side_stream_matches_same_stream() -> None:
+    from pck.cuda import SideStreamChecker
+
+    checker, x, y, _ = make(512, 4096, 64, 2, None, seed=0)
+    serial = checker.check(x, y)
+    result = SideStreamChecker().submit(checker, x, y).wait()
+    assert torch.equal(result.passed, serial.passed)
+    assert torch.equal(result.rho, serial.rho)
+    assert torch.equal(result.tau, serial.tau)
+
+
+def test_side_stream_sees_output_even_if_freed_and_overwritten() -> None:
+    from pck.cuda import SideStreamChecker, gemv_coalesced
+
+    checker, x, _, W = make(1024, 4096, 64, 2, None, seed=1)
+    side = SideStreamChecker()
+    pending = []
+    for _ in range(20):
+        y = gemv_coalesced(W, x, THREADS)
+        pending.append(side.submit(checker, x, y))
+        del y
+        garbage = torch.full((1024,), float("nan"), device="cuda")
+        garbage.add_(1)
+    for p in pending:
+        assert p.wait().verdict.all()
