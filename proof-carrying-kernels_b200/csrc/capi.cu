@@ -196,11 +196,19 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   // Shared memory: activations, then as many stages as fit (at least two).
   x_bytes = (x_bytes + 127) / 128 * 128;
   stage_bytes = (stage_bytes + 127) / 128 * 128;
-  int stages = 0;
+  // The stage count is a multiple of the consumer warps, so each stage has one owner warp
+  // (see stream_kernel.cuh); stages too large for eight warps run with fewer.
+  int stages = 0, consumers = pck::kConsumerWarps;
   if (tma) {
     const int64_t room = pck::kSmemCap - x_bytes - 8 * (2 * pck::kMaxStages + 2) - 64;
-    stages = room > 0 ? static_cast<int>(std::min<int64_t>(pck::kMaxStages, room / stage_bytes)) : 0;
-    if (stages < 2) tma = false;
+    const int64_t fit = room > 0 ? std::min<int64_t>(pck::kMaxStages, room / stage_bytes) : 0;
+    if (fit >= pck::kConsumerWarps) {
+      stages = static_cast<int>(fit / pck::kConsumerWarps * pck::kConsumerWarps);
+    } else if (fit >= 2) {
+      stages = consumers = static_cast<int>(fit);
+    } else {
+      tma = false;
+    }
   }
   size_t smem = 0;
   if (tma) {
@@ -208,6 +216,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
     plan.stages = stages;
     plan.stage_bytes = static_cast<int32_t>(stage_bytes);
     plan.x_bytes = static_cast<int32_t>(x_bytes);
+    plan.consumers = consumers;
   }
 
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs

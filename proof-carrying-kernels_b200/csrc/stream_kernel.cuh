@@ -3,9 +3,12 @@
 //
 // Data path (kTma): one producer warp streams each unit's bytes from HBM into a ring of
 // shared-memory stages with cp.async.bulk (completion counted on a per-stage mbarrier);
-// the activations X of the CTA's job are copied to shared memory once. Eight consumer
-// warps take the units in turn: warp w reduces units w, w + 8, ... of the CTA's range and
-// hands each stage back through its "empty" mbarrier. Without kTma (unaligned pointers,
+// the activations X of the CTA's job are copied to shared memory once. C consumer warps
+// (C <= 8, the stage count a multiple of C) take the units in turn: warp w reduces units
+// w, w + C, ... of the CTA's range and hands each stage back through its "empty" mbarrier.
+// Unit i uses stage i mod stages, so every use of a stage belongs to the same warp: a
+// warp waiting for use u of its stage has itself consumed use u - 1, which keeps the
+// mbarrier's phase within one of the awaited one and the parity wait exact. Without kTma (unaligned pointers,
 // n not a multiple of the vector width) the consumer warps read global memory directly
 // with scalar loads; the arithmetic is identical.
 //
@@ -545,21 +548,23 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kPlainThreads, 1)
     }
 
     // consumers
+    const int consumers = plan.consumers;
+    if (warp >= consumers) return;  // idle warp (stages too large for eight)
     const uint16_t* X = reinterpret_cast<const uint16_t*>(xs);
     const bool have_x = mbar_wait(xbar, 0);
     if (e4m3) {
       if (have_x && !x_allows_fma(X, static_cast<int64_t>(jb.batch) * jb.n,
-                                  static_cast<int>(threadIdx.x), kPlainThreads)) {
+                                  static_cast<int>(threadIdx.x), consumers * kWarp)) {
         atomicOr(flag, 1u);
       }
-      named_barrier(1, kPlainThreads);
+      named_barrier(1, consumers * kWarp);
     }
     if (!have_x) return;
     const bool fma = e4m3 && *flag == 0;
 
     int64_t cur_beta = -1;
     uint32_t pending = 0;
-    for (int64_t i = warp; i < count; i += kConsumerWarps) {
+    for (int64_t i = warp; i < count; i += consumers) {
       const int st = static_cast<int>(i % stages);
       if (!mbar_wait(full + st, static_cast<uint32_t>((i / stages) & 1))) return;
       const Unit un = decode_unit(jb, u0 + i);

@@ -78,7 +78,7 @@ struct Plan {
   int32_t stage_bytes;
   int32_t x_bytes;
   int32_t threads;      // tree parameter T (all W jobs share it)
-  int32_t per_pad;
+  int32_t consumers;    // consumer warps in use (staged path); stages is a multiple of it
 };
 
 // Host-side launch of one instantiation family (stream_bf16.cu, stream_e4m3.cu). nv is

