@@ -146,7 +146,12 @@ typedef struct pck_gemv_job {
   int32_t batch;                /* [1, 16]                                                */
   int32_t threads;              /* tree parameter, power of two in [32, 1024]             */
   int32_t weight_format;
-  int32_t reserved;
+  /* bfloat16 weights only, optional (0 = unknown): the smallest exponent field (bits
+     7-14) of a nonzero weight, subnormals counted as 1, and the largest exponent field.
+     When they and the activations prove every product exact in binary32, the kernel
+     adds each product with one FMA, which is then bit-identical to product-then-sum. */
+  int16_t w_exp_min;
+  int16_t w_exp_max;
   const pck_check_desc* check;  /* NULL: unchecked                                        */
 } pck_gemv_job;
 

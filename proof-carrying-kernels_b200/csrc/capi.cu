@@ -74,6 +74,8 @@ struct Spec {
   int wfmt;
   bool has_w;
   const pck_check_desc* check;
+  int w_exp_min;
+  int w_exp_max;
 };
 
 int validate_check(const pck_check_desc* d) {
@@ -97,8 +99,9 @@ int validate_check(const pck_check_desc* d) {
   return PCK_OK;
 }
 
-// Plans and launches the streaming kernel for `specs` (all validated by the caller except
-// for the checks done here).
+constexpr int64_t kUnitTarget = 32 * 1024;  // largest row unit the staged path builds
+
+// Plans and launches the streaming kernel for `specs` (validated by the caller).
 int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   if (specs.empty() || specs.size() > static_cast<size_t>(pck::kMaxJobs)) {
     return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %zu", pck::kMaxJobs, specs.size());
@@ -120,36 +123,60 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
     threads = 256;
     batch = 1;
   }
+  const int nv = threads / 32;
   const int vec = wfmt == pck::kWeightsBf16 ? 8 : 16;
   const int esize = wfmt == pck::kWeightsBf16 ? 2 : 1;
 
-  pck::Plan plan{};
+  // Pass 1: which jobs have work, and whether the staged (bulk-copy) path applies.
+  std::vector<const Spec*> live;
   bool tma = true;
-  int64_t x_bytes = 0, stage_bytes = 0;
+  int max_batch = 1;
+  for (const Spec& s : specs) {
+    const int64_t m = s.check ? static_cast<int64_t>(s.check->num_blocks) * s.check->block : s.m;
+    if (m == 0) continue;
+    live.push_back(&s);
+    const int64_t n = s.check ? s.check->n : s.n;
+    const int b = s.check ? s.check->batch : s.batch;
+    max_batch = std::max(max_batch, b);
+    if (s.has_w && (!aligned16(s.W) || !aligned16(s.X) || n % vec != 0)) tma = false;
+    if (s.check) {
+      const pck_check_desc* d = s.check;
+      if (!aligned16(d->c) || !aligned16(d->a) || !aligned16(d->x) || d->n % 8 != 0) tma = false;
+    }
+  }
+  if (live.empty()) return ok();
+
+  // Pass 2: units and bytes of every job.
+  pck::Plan plan{};
+  const int max_rows = pck::unit_rows(wfmt, nv);
+  int64_t x_bytes = 0, stage_bytes = 0, sum_bytes = 0;
   std::vector<int64_t> bytes;
   int nj = 0;
-  for (const Spec& s : specs) {
+  for (const Spec* sp : live) {
+    const Spec& s = *sp;
     pck::JobPlan jb{};
     jb.W = s.W;
     jb.X = static_cast<const uint16_t*>(s.has_w ? s.X : s.check->x);
     jb.Y = s.Y;
     jb.has_w = s.has_w ? 1 : 0;
     jb.has_check = s.check ? 1 : 0;
+    jb.w_exp_min = s.w_exp_min;
+    jb.w_exp_max = s.w_exp_max;
     if (s.check) {
-      const pck_check_desc* d = s.check;
-      jb.m = static_cast<int64_t>(d->num_blocks) * d->block;
-      jb.n = d->n;
-      jb.batch = d->batch;
+      jb.m = static_cast<int64_t>(s.check->num_blocks) * s.check->block;
+      jb.n = s.check->n;
+      jb.batch = s.check->batch;
     } else {
       jb.m = s.m;
       jb.n = s.n;
       jb.batch = s.batch;
     }
-    if (jb.m == 0) continue;
     jb.row_bytes = jb.n * esize;
-    if (s.has_w) {
-      if (!aligned16(s.W) || !aligned16(s.X) || jb.n % vec != 0) tma = false;
+    int rows = 1;
+    if (tma && s.has_w) {
+      while (rows * 2 <= max_rows && rows * 2 * jb.row_bytes <= kUnitTarget) rows *= 2;
     }
+    jb.rows = rows;
     if (s.check) {
       const pck_check_desc* d = s.check;
       jb.block = d->block;
@@ -173,50 +200,62 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
       jb.coef = d->coef;
       jb.geps = d->geps;
       jb.tau_floor = d->tau_floor;
-      const int64_t bw = s.has_w ? d->block : 0;
-      jb.period_units = bw + static_cast<int64_t>(d->checks + 1) * jb.segs;
-      jb.period_bytes = bw * jb.row_bytes + (4LL * d->checks + 2) * d->n;
+      jb.row_units = s.has_w ? static_cast<int32_t>((d->block + rows - 1) / rows) : 0;
+      jb.period_units = jb.row_units + static_cast<int64_t>(d->checks + 1) * jb.segs;
+      jb.period_bytes = (s.has_w ? d->block * jb.row_bytes : 0) + (4LL * d->checks + 2) * d->n;
       jb.units = jb.period_units * d->num_blocks;
       jb.total_bytes = jb.period_bytes * d->num_blocks;
-      if (!aligned16(d->c) || !aligned16(d->a) || !aligned16(d->x) || d->n % 8 != 0) tma = false;
       stage_bytes = std::max<int64_t>(stage_bytes, 4 * len);
     } else {
+      jb.row_units = static_cast<int32_t>((jb.m + rows - 1) / rows);
       jb.period_units = 1;
-      jb.period_bytes = jb.row_bytes;
-      jb.units = jb.m;
+      jb.period_bytes = rows * jb.row_bytes;
+      jb.units = jb.row_units;
       jb.total_bytes = jb.m * jb.row_bytes;
     }
-    if (s.has_w) stage_bytes = std::max<int64_t>(stage_bytes, jb.row_bytes);
+    if (s.has_w) stage_bytes = std::max<int64_t>(stage_bytes, rows * jb.row_bytes);
     x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 2);
+    sum_bytes = std::max<int64_t>(sum_bytes, std::max<int64_t>(4LL * rows * nv * jb.batch, 64LL * jb.batch));
     plan.jobs[nj++] = jb;
     bytes.push_back(jb.total_bytes);
   }
-  if (nj == 0) return ok();
 
-  // Shared memory: activations, then as many stages as fit (at least two).
+  // Shared memory: activations, then as many stages (with their scratch) as fit.
   x_bytes = (x_bytes + 127) / 128 * 128;
   stage_bytes = (stage_bytes + 127) / 128 * 128;
-  // The stage count is a multiple of the consumer warps, so each stage has one owner warp
-  // (see stream_kernel.cuh); stages too large for eight warps run with fewer.
-  int stages = 0, consumers = pck::kConsumerWarps;
+  sum_bytes = (sum_bytes + 15) / 16 * 16;
+  int stages = 0;
   if (tma) {
-    const int64_t room = pck::kSmemCap - x_bytes - 8 * (2 * pck::kMaxStages + 2) - 64;
-    const int64_t fit = room > 0 ? std::min<int64_t>(pck::kMaxStages, room / stage_bytes) : 0;
-    if (fit >= pck::kConsumerWarps) {
-      stages = static_cast<int>(fit / pck::kConsumerWarps * pck::kConsumerWarps);
-    } else if (fit >= 2) {
-      stages = consumers = static_cast<int>(fit);
-    } else {
-      tma = false;
+    const int64_t fixed = x_bytes + 8 * 1 + 8 + 256;
+    const int64_t per_stage = stage_bytes + sum_bytes + 2 * 8 + 4;
+    const int64_t fit = (pck::kSmemCap - fixed) / per_stage;
+    stages = static_cast<int>(std::min<int64_t>(pck::kMaxStages, fit));
+    if (stages < 2) tma = false;
+  }
+  if (!tma) {  // the plain path takes one row per unit
+    for (int j = 0; j < nj; ++j) {
+      pck::JobPlan& jb = plan.jobs[j];
+      if (!jb.has_w || jb.rows == 1) continue;
+      jb.rows = 1;
+      if (jb.has_check) {
+        jb.row_units = jb.block;
+        jb.period_units = jb.row_units + static_cast<int64_t>(jb.checks + 1) * jb.segs;
+        jb.units = jb.period_units * jb.num_blocks;
+      } else {
+        jb.row_units = static_cast<int32_t>(jb.m);
+        jb.period_bytes = jb.row_bytes;
+        jb.units = jb.m;
+      }
     }
   }
   size_t smem = 0;
   if (tma) {
-    smem = static_cast<size_t>(x_bytes + stages * stage_bytes + 8 * (2 * stages + 2) + 16);
+    smem = static_cast<size_t>(x_bytes + stages * (stage_bytes + sum_bytes) + 8 * (2 * stages + 1) +
+                               4 * (stages + 2) + 16);
     plan.stages = stages;
     plan.stage_bytes = static_cast<int32_t>(stage_bytes);
     plan.x_bytes = static_cast<int32_t>(x_bytes);
-    plan.consumers = consumers;
+    plan.sum_bytes = static_cast<int32_t>(sum_bytes);
   }
 
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs
@@ -259,11 +298,10 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   plan.njobs = nj;
   plan.threads = threads;
 
-  const int nv = threads / 32;
   int bg = 1;
   if (tma) {
-    const int limit = std::min(8, 64 / nv);
-    while (bg * 2 <= limit && bg * 2 <= batch) bg *= 2;
+    const int acc = pck::warp_accumulators(wfmt, nv);
+    while (bg * 2 <= 8 && bg * 2 <= max_batch && bg * 2 * acc <= 32) bg *= 2;
   }
   const unsigned grid = static_cast<unsigned>(begin);
   const cudaError_t err = wfmt == pck::kWeightsBf16
@@ -327,7 +365,7 @@ int pck_gemv_batched(int weight_format, const void* W, const void* X, float* Y, 
     return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %lld", pck::kMaxBatch, static_cast<long long>(batch));
   }
   if (m == 0) return ok();
-  std::vector<Spec> specs{{W, X, Y, m, n, static_cast<int>(batch), threads, weight_format, true, nullptr}};
+  std::vector<Spec> specs{{W, X, Y, m, n, static_cast<int>(batch), threads, weight_format, true, nullptr, 0, 0}};
   return run_stream(specs, static_cast<cudaStream_t>(stream));
 }
 
@@ -349,7 +387,7 @@ int pck_blocked_check(const pck_check_desc* descs, int count, void* stream) {
   for (int i = 0; i < count; ++i) {
     if (int rc = validate_check(descs + i)) return rc;
     specs.push_back(Spec{nullptr, nullptr, nullptr, 0, descs[i].n, descs[i].batch, 256,
-                         PCK_WEIGHTS_BF16, false, descs + i});
+                         PCK_WEIGHTS_BF16, false, descs + i, 0, 0});
   }
   return run_stream(specs, static_cast<cudaStream_t>(stream));
 }
@@ -377,7 +415,7 @@ int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream) {
       }
     }
     specs.push_back(Spec{jb.W, jb.X, jb.Y, jb.m, jb.n, jb.batch, jb.threads, jb.weight_format,
-                         true, jb.check});
+                         true, jb.check, jb.w_exp_min, jb.w_exp_max});
   }
   return run_stream(specs, static_cast<cudaStream_t>(stream));
 }

@@ -1,27 +1,25 @@
 // The persistent streaming kernel: GEMV rows, checksum-bank segments and the block
 // verdicts of the trusted checker, for every job of a launch plan (stream_plan.h).
 //
-// Data path (kTma): one producer warp streams each unit's bytes from HBM into a ring of
-// shared-memory stages with cp.async.bulk (completion counted on a per-stage mbarrier);
-// the activations X of the CTA's job are copied to shared memory once. C consumer warps
-// (C <= 8, the stage count a multiple of C) take the units in turn: warp w reduces units
-// w, w + C, ... of the CTA's range and hands each stage back through its "empty" mbarrier.
-// Unit i uses stage i mod stages, so every use of a stage belongs to the same warp: a
-// warp waiting for use u of its stage has itself consumed use u - 1, which keeps the
-// mbarrier's phase within one of the awaited one and the parity wait exact. Without kTma (unaligned pointers,
-// n not a multiple of the vector width) the consumer warps read global memory directly
-// with scalar loads; the arithmetic is identical.
+// Staged path (kTma): one producer warp streams each unit's bytes from HBM into a ring of
+// shared-memory stages with cp.async.bulk (completion counted as transaction bytes on a
+// per-stage "full" mbarrier); the activations X of the CTA's job are copied to shared
+// memory once. All eight consumer warps work on every stage, in order: each takes its
+// share of the unit, publishes a partial result in the stage's scratch and takes a ticket
+// (a shared-memory atomic); the warp with the last ticket finishes the unit (final
+// reduction, store) and every warp hands the stage back through its "empty" mbarrier
+// (eight arrivals). Because every warp consumes every stage in order, a warp waiting for
+// use u of a stage has itself consumed use u - 1, so the mbarrier parity waits are exact.
+// Plain path (unaligned pointers, n not a multiple of the vector width): each warp takes
+// whole units and reads global memory directly; the arithmetic is the same.
 //
 // GEMV row arithmetic (bit-exact with the reference's model of its coalesced kernel,
 // src/pck/gemv.py:71-101 / src/pck/cuda/csrc/gemv_kernel.cu:139-178): with T = 32*NV
-// chains, chain t = 32*w + l owns vectors t, t + T, ... of V columns (V = 8 bfloat16 or
-// 16 E4M3 weights per 16-byte vector). Lane l of the warp holds the NV chains
-// l, 32 + l, ..., 32*(NV-1) + l of the row in registers and adds each chain's products in
-// order (binary32 product, then binary32 sum; an E4M3 x bfloat16 product is exact, so
-// when no product can overflow the pair is one FMA). The chains of each group of 32 are
-// combined by the halving tree (i += i + 16, ..., i += i + 1) and the NV group sums by
-// halving again; the exchange scheme in `halve_groups` evaluates exactly those additions
-// while moving only half of the live values at each level.
+// chains, chain t = 32*g + l (group g, lane l) owns vectors t, t + T, ... of V columns
+// (V = 8 bfloat16 or 16 E4M3 weights per 16-byte vector) and adds its products in order
+// (binary32 product, then binary32 sum — or one FMA where the product is provably exact).
+// Each group of 32 chains is reduced by halving across lanes (l += l + 16, ..., l += l + 1)
+// and the NV group sums by halving again (g += g + NV/2, ..., g += g + 1).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -53,7 +51,8 @@ struct Unit {
   int kind;
   int k;
   int s;
-  int64_t row;   // kUnitRow
+  int rows;      // kUnitRow: rows in this unit
+  int64_t row;   // kUnitRow: first row
   int64_t beta;  // row block (checked jobs)
   int64_t col0;  // first column (segments)
   int64_t len;   // columns (segments)
@@ -69,23 +68,26 @@ __device__ __forceinline__ Unit decode_unit(const JobPlan& jb, int64_t u) {
   Unit x{};
   if (!jb.has_check) {
     x.kind = kUnitRow;
-    x.row = u;
-    x.src = static_cast<const uint8_t*>(jb.W) + u * jb.row_bytes;
-    x.bytes = static_cast<uint32_t>(jb.row_bytes);
+    x.row = u * jb.rows;
+    x.rows = static_cast<int>(min(static_cast<int64_t>(jb.rows), jb.m - x.row));
+    x.src = static_cast<const uint8_t*>(jb.W) + x.row * jb.row_bytes;
+    x.bytes = static_cast<uint32_t>(x.rows * jb.row_bytes);
     return x;
   }
   const int64_t beta = u / jb.period_units;
   int64_t o = u - beta * jb.period_units;
   x.beta = beta;
-  const int64_t bw = jb.has_w ? jb.block : 0;
-  if (o < bw) {
+  const int64_t ru = jb.has_w ? jb.row_units : 0;
+  if (o < ru) {
     x.kind = kUnitRow;
-    x.row = beta * jb.block + o;
+    const int64_t first = o * jb.rows;
+    x.row = beta * jb.block + first;
+    x.rows = static_cast<int>(min(static_cast<int64_t>(jb.rows), jb.block - first));
     x.src = static_cast<const uint8_t*>(jb.W) + x.row * jb.row_bytes;
-    x.bytes = static_cast<uint32_t>(jb.row_bytes);
+    x.bytes = static_cast<uint32_t>(x.rows * jb.row_bytes);
     return x;
   }
-  o -= bw;
+  o -= ru;
   const int64_t cs = static_cast<int64_t>(jb.checks) * jb.segs;
   if (o < cs) {
     x.kind = kUnitC;
@@ -111,24 +113,25 @@ __device__ __forceinline__ Unit decode_unit(const JobPlan& jb, int64_t u) {
 __device__ __forceinline__ int64_t first_unit_at(const JobPlan& jb, int64_t target) {
   if (target <= 0) return 0;
   if (target >= jb.total_bytes) return jb.units;
-  if (!jb.has_check) return ceil_div64(target, jb.row_bytes);
+  const int64_t unit_bytes = jb.rows * jb.row_bytes;
+  if (!jb.has_check) return ceil_div64(target, unit_bytes);
   const int64_t beta = target / jb.period_bytes;
   int64_t rem = target - beta * jb.period_bytes;
   const int64_t base = beta * jb.period_units;
   if (rem == 0) return base;
-  const int64_t bw = jb.has_w ? jb.block : 0;
-  const int64_t wbytes = bw * jb.row_bytes;
-  if (rem <= wbytes) return base + ceil_div64(rem, jb.row_bytes);
+  const int64_t ru = jb.has_w ? jb.row_units : 0;
+  const int64_t wbytes = jb.has_w ? jb.block * jb.row_bytes : 0;
+  if (rem <= wbytes) return base + ceil_div64(rem, unit_bytes);
   rem -= wbytes;
   const int64_t crow = 4 * jb.n;
   const int64_t cbytes = jb.checks * crow;
   if (rem <= cbytes) {
     const int64_t k = rem / crow;
     const int64_t r3 = rem - k * crow;
-    return base + bw + k * jb.segs + ceil_div64(r3, 4 * jb.seg_len);
+    return base + ru + k * jb.segs + ceil_div64(r3, 4 * jb.seg_len);
   }
   rem -= cbytes;
-  return base + bw + static_cast<int64_t>(jb.checks) * jb.segs + ceil_div64(rem, 2 * jb.seg_len);
+  return base + ru + static_cast<int64_t>(jb.checks) * jb.segs + ceil_div64(rem, 2 * jb.seg_len);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -457,32 +460,261 @@ __device__ __forceinline__ void credit_block(const JobPlan& jb, int64_t beta, ui
   if (before + count == total) merge_block(jb, beta, lane);
 }
 
-// One unit: reduce it and store its result.
-template <int WFMT, int NV, int BG, bool kFast, bool kFma>
-__device__ __forceinline__ void run_unit(const JobPlan& jb, const Unit& un, const uint8_t* data,
-                                         const uint16_t* X, int lane) {
+// ---------------------------------------------------------------------------------------
+// Plain path: one warp per unit, global memory.
+
+template <int WFMT, int NV, int BG>
+__device__ __forceinline__ void plain_unit(const JobPlan& jb, const Unit& un, const uint16_t* X,
+                                           int lane) {
   if (un.kind == kUnitRow) {
-    gemv_row<WFMT, NV, BG, kFast, kFma>(data, X, jb.n, jb.batch, jb.Y, jb.m, un.row, lane);
+    for (int r = 0; r < un.rows; ++r) {
+      const uint8_t* wrow = static_cast<const uint8_t*>(un.src) + r * jb.row_bytes;
+      gemv_row<WFMT, NV, BG, false, false>(wrow, X, jb.n, jb.batch, jb.Y, jb.m, un.row + r, lane);
+    }
   } else if (un.kind == kUnitC) {
     const int64_t nb = jb.num_blocks;
     double* out = jb.partial_cx + (static_cast<int64_t>(un.k) * nb + un.beta) * jb.seg_alloc + un.s;
     const int64_t stride = static_cast<int64_t>(jb.checks) * nb * jb.seg_alloc;
-    c_segment<kFast>(reinterpret_cast<const float*>(data), X, jb.n, jb.batch, un.col0, un.len, out,
+    c_segment<false>(static_cast<const float*>(un.src), X, jb.n, jb.batch, un.col0, un.len, out,
                      stride, lane);
   } else {
     const int64_t nb = jb.num_blocks;
     double* out = jb.partial_s + un.beta * jb.seg_alloc + un.s;
-    a_segment<kFast>(reinterpret_cast<const uint16_t*>(data), X, jb.n, jb.batch, un.col0, un.len,
-                     out, nb * jb.seg_alloc, lane);
+    a_segment<false>(static_cast<const uint16_t*>(un.src), X, jb.n, jb.batch, un.col0, un.len, out,
+                     nb * jb.seg_alloc, lane);
   }
 }
 
-// E4M3 x bfloat16 products are exact; an FMA equals product-then-sum unless a product
-// overflows, which needs |x| >= 2^128 / 448. True when every |x| < 2^119 and finite.
-__device__ __forceinline__ bool x_allows_fma(const uint16_t* X, int64_t count, int first, int step) {
-  bool ok = true;
-  for (int64_t j = first; j < count; j += step) ok &= (X[j] & 0x7fffu) < 0x7b00u;
-  return ok;
+// ---------------------------------------------------------------------------------------
+// Staged path: all consumer warps share each unit.
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+// Which chains and rows of a row unit a consumer warp owns. Pairs (row r, group g) are
+// dealt to the eight warps: with NV >= 8 groups, warp w takes groups w, w + 8, ... for
+// every row; with fewer, warp w takes group w % NV for rows w / NV, w / NV + 8 / NV, ...
+// A warp loads each activation vector once and uses it for all its rows.
+template <int WFMT, int NV>
+struct Share {
+  static constexpr int kRows = unit_rows(WFMT, NV);                    // rows per unit, max
+  static constexpr int kGroups = NV >= kConsumerWarps ? NV / kConsumerWarps : 1;
+  static constexpr int kRowsPerWarp = NV >= kConsumerWarps ? kRows : kRows * NV / kConsumerWarps;
+  static __device__ __forceinline__ int group(int warp, int j) {
+    return NV >= kConsumerWarps ? warp + kConsumerWarps * j : warp % NV;
+  }
+  static __device__ __forceinline__ int row(int warp, int k) {
+    return NV >= kConsumerWarps ? k : warp / NV + (kConsumerWarps / NV) * k;
+  }
+};
+
+__device__ __forceinline__ float lane_halving(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_down_sync(kFullMask, v, o));
+  return v;
+}
+
+// This warp's share of a row unit at stage address `stage` (rows of row_bytes), against
+// the activations at `xs` (batch rows of n bfloat16). Publishes the group sums
+// sums[(r * NV + g) * batch + b] for its (row, group) pairs.
+template <int WFMT, int NV, int BG, bool kFma>
+__device__ __forceinline__ void rows_share(const JobPlan& jb, uint32_t stage, uint32_t xs, float* sums,
+                                           int rows_here, int warp, int lane) {
+  using S = Share<WFMT, NV>;
+  constexpr int V = Format<WFMT>::kVec;
+  constexpr int T = NV * kWarp;
+  constexpr uint32_t kWV = 16;          // bytes of one weight vector
+  constexpr uint32_t kXV = V * 2;       // bytes of one activation vector (16 or 32)
+  const int nvec = static_cast<int>(jb.n / V);  // n % V == 0 on this path
+  const int full = nvec / T;
+  const bool tail = full * T != nvec;
+  const uint32_t row_bytes = static_cast<uint32_t>(jb.row_bytes);
+  const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
+  const int batch = jb.batch;
+  for (int g0 = 0; g0 < batch; g0 += BG) {
+    float acc[S::kRowsPerWarp][S::kGroups][BG];
+#pragma unroll
+    for (int k = 0; k < S::kRowsPerWarp; ++k)
+#pragma unroll
+      for (int j = 0; j < S::kGroups; ++j)
+#pragma unroll
+        for (int b = 0; b < BG; ++b) acc[k][j][b] = -0.0f;  // -0 + p == p for every p
+
+    const int iters = full + (tail ? 1 : 0);
+    for (int v = 0; v < iters; ++v) {
+#pragma unroll
+      for (int j = 0; j < S::kGroups; ++j) {
+        const int q = v * T + S::group(warp, j) * kWarp + lane;
+        if (v == full && q >= nvec) {  // padding past n: +0 terms
+#pragma unroll
+          for (int k = 0; k < S::kRowsPerWarp; ++k)
+#pragma unroll
+            for (int b = 0; b < BG; ++b) acc[k][j][b] = __fadd_rn(acc[k][j][b], 0.0f);
+          continue;
+        }
+        uint4 xa[BG], xb[BG];
+#pragma unroll
+        for (int b = 0; b < BG; ++b) {
+          const uint32_t xaddr = xs + static_cast<uint32_t>(min(g0 + b, batch - 1)) * xcol + q * kXV;
+          xa[b] = lds128(xaddr);
+          if constexpr (WFMT == kWeightsE4m3) xb[b] = lds128(xaddr + 16);
+        }
+#pragma unroll
+        for (int k = 0; k < S::kRowsPerWarp; ++k) {
+          const int r = S::row(warp, k);
+          if (r < rows_here) {
+            const uint4 wv = lds128(stage + r * row_bytes + q * kWV);
+#pragma unroll
+            for (int b = 0; b < BG; ++b) {
+              if constexpr (WFMT == kWeightsBf16) {
+                if constexpr (kFma) {
+                  chain_pair<true>(acc[k][j][b], bf16_lo(wv.x), bf16_lo(xa[b].x));
+                  chain_pair<true>(acc[k][j][b], bf16_hi(wv.x), bf16_hi(xa[b].x));
+                  chain_pair<true>(acc[k][j][b], bf16_lo(wv.y), bf16_lo(xa[b].y));
+                  chain_pair<true>(acc[k][j][b], bf16_hi(wv.y), bf16_hi(xa[b].y));
+                  chain_pair<true>(acc[k][j][b], bf16_lo(wv.z), bf16_lo(xa[b].z));
+                  chain_pair<true>(acc[k][j][b], bf16_hi(wv.z), bf16_hi(xa[b].z));
+                  chain_pair<true>(acc[k][j][b], bf16_lo(wv.w), bf16_lo(xa[b].w));
+                  chain_pair<true>(acc[k][j][b], bf16_hi(wv.w), bf16_hi(xa[b].w));
+                } else {
+                  chain_bf16(acc[k][j][b], wv, xa[b]);
+                }
+              } else {
+                chain_e4m3<kFma>(acc[k][j][b], wv, xa[b], xb[b]);
+              }
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < S::kRowsPerWarp; ++k) {
+      const int r = S::row(warp, k);
+#pragma unroll
+      for (int j = 0; j < S::kGroups; ++j) {
+#pragma unroll
+        for (int b = 0; b < BG; ++b) {
+          const float s = lane_halving(acc[k][j][b]);
+          if (lane == 0 && r < rows_here && g0 + b < batch) {
+            sums[(r * NV + S::group(warp, j)) * batch + g0 + b] = s;
+          }
+        }
+      }
+    }
+  }
+}
+
+// Last warp of a row unit: halving over the NV group sums of every (row, column).
+template <int NV>
+__device__ __forceinline__ void rows_finish(const JobPlan& jb, const float* sums, int64_t row0,
+                                            int rows_here, int lane) {
+  const int batch = jb.batch;
+  for (int o = lane; o < rows_here * batch; o += kWarp) {
+    const int r = o / batch;
+    const int b = o - r * batch;
+    float g[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) g[i] = sums[(r * NV + i) * batch + b];
+#pragma unroll
+    for (int h = NV / 2; h >= 1; h /= 2) {
+#pragma unroll
+      for (int i = 0; i < h; ++i) g[i] = __fadd_rn(g[i], g[i + h]);
+    }
+    jb.Y[static_cast<int64_t>(b) * jb.m + row0 + r] = g[0];
+  }
+}
+
+// This warp's share of a c- or a-segment: elements (4 at a time) warp*32 + lane, + 256, ...
+// Publishes dsums[warp * batch + b].
+template <bool kAbs>
+__device__ __forceinline__ void segment_share(const JobPlan& jb, const Unit& un, uint32_t stage,
+                                              uint32_t xs, double* dsums, int warp, int lane) {
+  const int batch = jb.batch;
+  const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
+  const int len = static_cast<int>(un.len);
+  for (int b = 0; b < batch; ++b) {
+    const uint32_t xb = xs + static_cast<uint32_t>(b) * xcol + static_cast<uint32_t>(un.col0) * 2;
+    double acc = 0.0;
+    for (int e = (warp * kWarp + lane) * 4; e < len; e += kConsumerWarps * kWarp * 4) {
+      const uint2 xv = lds64(xb + e * 2);
+      if constexpr (kAbs) {
+        const uint2 av = lds64(stage + e * 2);
+        acc = __fma_ru(static_cast<double>(bf16_lo(av.x)), fabs(static_cast<double>(bf16_lo(xv.x))), acc);
+        acc = __fma_ru(static_cast<double>(bf16_hi(av.x)), fabs(static_cast<double>(bf16_hi(xv.x))), acc);
+        acc = __fma_ru(static_cast<double>(bf16_lo(av.y)), fabs(static_cast<double>(bf16_lo(xv.y))), acc);
+        acc = __fma_ru(static_cast<double>(bf16_hi(av.y)), fabs(static_cast<double>(bf16_hi(xv.y))), acc);
+      } else {
+        const uint4 cv = lds128(stage + e * 4);
+        acc = __fma_rn(static_cast<double>(__uint_as_float(cv.x)), static_cast<double>(bf16_lo(xv.x)), acc);
+        acc = __fma_rn(static_cast<double>(__uint_as_float(cv.y)), static_cast<double>(bf16_hi(xv.x)), acc);
+        acc = __fma_rn(static_cast<double>(__uint_as_float(cv.z)), static_cast<double>(bf16_lo(xv.y)), acc);
+        acc = __fma_rn(static_cast<double>(__uint_as_float(cv.w)), static_cast<double>(bf16_hi(xv.y)), acc);
+      }
+    }
+    acc = kAbs ? warp_sum_ru(acc) : warp_sum_rn(acc);
+    if (lane == 0) dsums[warp * batch + b] = acc;
+  }
+}
+
+// Last warp of a segment: the warp partials in warp order, stored to the block's scratch.
+__device__ __forceinline__ void segment_finish(const JobPlan& jb, const Unit& un, const double* dsums,
+                                               int lane) {
+  const int batch = jb.batch;
+  const int64_t nb = jb.num_blocks;
+  for (int b = lane; b < batch; b += kWarp) {
+    double total = 0.0;
+    if (un.kind == kUnitC) {
+      for (int w = 0; w < kConsumerWarps; ++w) total = __dadd_rn(total, dsums[w * batch + b]);
+      jb.partial_cx[((static_cast<int64_t>(b) * jb.checks + un.k) * nb + un.beta) * jb.seg_alloc + un.s] = total;
+    } else {
+      for (int w = 0; w < kConsumerWarps; ++w) total = __dadd_ru(total, dsums[w * batch + b]);
+      jb.partial_s[(static_cast<int64_t>(b) * nb + un.beta) * jb.seg_alloc + un.s] = total;
+    }
+  }
+}
+
+// Exponent fields (bfloat16 bits 7-14) of the activations: smallest over nonzero values
+// (subnormals count as 1) and largest over all.
+__device__ __forceinline__ void x_exponents(const uint16_t* X, int64_t count, int first, int step,
+                                            unsigned* lo, unsigned* hi) {
+  unsigned mn = 1000, mx = 0;
+  for (int64_t j = first; j < count; j += step) {
+    const unsigned mag = X[j] & 0x7fffu;
+    const unsigned e = mag >> 7;
+    mx = max(mx, e);
+    if (mag) mn = min(mn, max(e, 1u));
+  }
+  atomicMin(lo, mn);
+  atomicMax(hi, mx);
+}
+
+// Whether one FMA equals the product-then-sum for every weight x activation pair.
+// E4M3 x bfloat16: the product is always exact (<= 12 significant bits, lowest bit >=
+// 2^-142) unless it overflows, which needs an activation exponent field >= 246.
+// bfloat16 x bfloat16: exact iff no product falls below 2^-126 with bits under 2^-149 and
+// none overflows: e_w + e_x >= 119 for the smallest nonzero exponent fields, and
+// e_w + e_x <= 380 for the largest (the weights' range comes with the job, 0 = unknown).
+template <int WFMT>
+__device__ __forceinline__ bool fma_is_exact(const JobPlan& jb, unsigned x_lo, unsigned x_hi) {
+  if constexpr (WFMT == kWeightsE4m3) {
+    return x_hi <= 245u;
+  } else {
+    if (jb.w_exp_min <= 0 || jb.w_exp_max <= 0) return false;
+    const bool low_ok = x_lo >= 1000u || static_cast<int>(x_lo) + jb.w_exp_min >= 119;
+    const bool high_ok = static_cast<int>(x_hi) + jb.w_exp_max <= 380;
+    return low_ok && high_ok;
+  }
 }
 
 template <int WFMT, int NV, int BG, bool kTma>
@@ -500,23 +732,27 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kPlainThreads, 1)
   if (count <= 0) return;  // uniform for the whole CTA
   const int warp = static_cast<int>(threadIdx.x) / kWarp;
   const int lane = static_cast<int>(threadIdx.x) % kWarp;
-  const bool e4m3 = WFMT == kWeightsE4m3 && jb.has_w;
 
   if constexpr (kTma) {
     const int stages = plan.stages;
+    const int sum_bytes = plan.sum_bytes;
     uint8_t* xs = smem;
     uint8_t* ring = smem + plan.x_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + static_cast<int64_t>(stages) * plan.stage_bytes);
+    uint8_t* scratch = ring + static_cast<int64_t>(stages) * plan.stage_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(scratch + static_cast<int64_t>(stages) * sum_bytes);
     uint64_t* empty = full + stages;
     uint64_t* xbar = empty + stages;
-    uint32_t* flag = reinterpret_cast<uint32_t*>(xbar + 1);
+    uint32_t* tickets = reinterpret_cast<uint32_t*>(xbar + 1);
+    uint32_t* xexp = tickets + stages;  // [0] smallest, [1] largest exponent field of x
     if (threadIdx.x == 0) {
       for (int s = 0; s < stages; ++s) {
         mbar_init(full + s, 1);
-        mbar_init(empty + s, 1);
+        mbar_init(empty + s, kConsumerWarps);
+        tickets[s] = 0;
       }
       mbar_init(xbar, 1);
-      *flag = 0;
+      xexp[0] = 1000;
+      xexp[1] = 0;
       fence_barrier_init();
     }
     __syncthreads();
@@ -524,7 +760,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kPlainThreads, 1)
     if (warp == kConsumerWarps) {  // producer
       if (lane == 0) {
         const uint64_t keep = policy_evict_last();
-        const uint64_t stream = policy_evict_first();
+        const uint64_t once = policy_evict_first();
         const uint32_t xbytes = static_cast<uint32_t>(static_cast<int64_t>(jb.batch) * jb.n * 2);
         mbar_arrive_expect_tx(xbar, xbytes);
         bulk_load(xs, jb.X, xbytes, xbar, keep);
@@ -534,8 +770,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kPlainThreads, 1)
           if (i >= stages && !mbar_wait(empty + st, static_cast<uint32_t>((i / stages - 1) & 1))) break;
           const Unit un = decode_unit(jb, u0 + i);
           mbar_arrive_expect_tx(full + st, un.bytes);
-          bulk_load(ring + static_cast<int64_t>(st) * plan.stage_bytes, un.src, un.bytes, full + st,
-                    stream);
+          bulk_load(ring + static_cast<int64_t>(st) * plan.stage_bytes, un.src, un.bytes, full + st, once);
           ++issued;
         }
         // Leave only after every copy into this CTA's shared memory has landed.
@@ -548,35 +783,58 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kPlainThreads, 1)
     }
 
     // consumers
-    const int consumers = plan.consumers;
-    if (warp >= consumers) return;  // idle warp (stages too large for eight)
     const uint16_t* X = reinterpret_cast<const uint16_t*>(xs);
     const bool have_x = mbar_wait(xbar, 0);
-    if (e4m3) {
-      if (have_x && !x_allows_fma(X, static_cast<int64_t>(jb.batch) * jb.n,
-                                  static_cast<int>(threadIdx.x), consumers * kWarp)) {
-        atomicOr(flag, 1u);
-      }
-      named_barrier(1, consumers * kWarp);
+    if (have_x && jb.has_w) {
+      x_exponents(X, static_cast<int64_t>(jb.batch) * jb.n, static_cast<int>(threadIdx.x), kPlainThreads,
+                  xexp, xexp + 1);
     }
+    named_barrier(1, kPlainThreads);
     if (!have_x) return;
-    const bool fma = e4m3 && *flag == 0;
+    const bool fma = jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]);
+    const uint32_t xs_addr = smem_addr(xs);
+    const uint32_t ring_addr = smem_addr(ring);
 
     int64_t cur_beta = -1;
     uint32_t pending = 0;
-    for (int64_t i = warp; i < count; i += consumers) {
+    for (int64_t i = 0; i < count; ++i) {
       const int st = static_cast<int>(i % stages);
       if (!mbar_wait(full + st, static_cast<uint32_t>((i / stages) & 1))) return;
       const Unit un = decode_unit(jb, u0 + i);
-      const uint8_t* data = ring + static_cast<int64_t>(st) * plan.stage_bytes;
-      if (fma) {
-        run_unit<WFMT, NV, BG, true, true>(jb, un, data, X, lane);
+      const uint32_t stage = ring_addr + static_cast<uint32_t>(st) * static_cast<uint32_t>(plan.stage_bytes);
+      uint8_t* sums = scratch + static_cast<int64_t>(st) * sum_bytes;
+      if (un.kind == kUnitRow) {
+        if (fma) {
+          rows_share<WFMT, NV, BG, true>(jb, stage, xs_addr, reinterpret_cast<float*>(sums), un.rows, warp, lane);
+        } else {
+          rows_share<WFMT, NV, BG, false>(jb, stage, xs_addr, reinterpret_cast<float*>(sums), un.rows, warp, lane);
+        }
+      } else if (un.kind == kUnitC) {
+        segment_share<false>(jb, un, stage, xs_addr, reinterpret_cast<double*>(sums), warp, lane);
       } else {
-        run_unit<WFMT, NV, BG, true, false>(jb, un, data, X, lane);
+        segment_share<true>(jb, un, stage, xs_addr, reinterpret_cast<double*>(sums), warp, lane);
+      }
+      __syncwarp();
+      uint32_t ticket = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        ticket = atomicAdd(tickets + st, 1u);
+      }
+      ticket = __shfl_sync(kFullMask, ticket, 0);
+      const bool last = ticket == kConsumerWarps - 1;
+      if (last) {
+        __threadfence_block();
+        if (un.kind == kUnitRow) {
+          rows_finish<NV>(jb, reinterpret_cast<const float*>(sums), un.row, un.rows, lane);
+        } else {
+          segment_finish(jb, un, reinterpret_cast<const double*>(sums), lane);
+        }
+        __syncwarp();
+        if (lane == 0) tickets[st] = 0;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty + st);
-      if (jb.has_check) {
+      if (last && jb.has_check) {
         if (un.beta != cur_beta && pending) {
           credit_block(jb, cur_beta, pending, lane);
           pending = 0;
@@ -587,15 +845,14 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kPlainThreads, 1)
     }
     if (pending) credit_block(jb, cur_beta, pending, lane);
   } else {
-    // Plain path: every warp is a consumer and reads global memory directly, one element
-    // at a time (product, then sum: the same values as the fast path's).
-    (void)e4m3;
+    // Plain path: every warp takes whole units and reads global memory directly, one
+    // element at a time (product, then sum: the same values as the staged path's).
     const uint16_t* X = jb.X;
     int64_t cur_beta = -1;
     uint32_t pending = 0;
     for (int64_t i = warp; i < count; i += kConsumerWarps) {
       const Unit un = decode_unit(jb, u0 + i);
-      run_unit<WFMT, NV, BG, false, false>(jb, un, static_cast<const uint8_t*>(un.src), X, lane);
+      plain_unit<WFMT, NV, BG>(jb, un, X, lane);
       if (jb.has_check) {
         if (un.beta != cur_beta && pending) {
           credit_block(jb, cur_beta, pending, lane);

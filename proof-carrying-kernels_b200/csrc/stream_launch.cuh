@@ -31,11 +31,12 @@ template <int WFMT, int NV>
 cudaError_t launch_nv(const Plan& plan, int bg, bool tma, unsigned grid, size_t smem,
                       cudaStream_t stream) {
   if (!tma) return launch_variant<WFMT, NV, 1, false>(plan, grid, smem, stream);
+  constexpr int kAcc = warp_accumulators(WFMT, NV);
   switch (bg) {
     case 1: return launch_variant<WFMT, NV, 1, true>(plan, grid, smem, stream);
-    case 2: return launch_variant<WFMT, NV, (NV <= 32 ? 2 : 1), true>(plan, grid, smem, stream);
-    case 4: return launch_variant<WFMT, NV, (NV <= 16 ? 4 : 1), true>(plan, grid, smem, stream);
-    case 8: return launch_variant<WFMT, NV, (NV <= 8 ? 8 : 1), true>(plan, grid, smem, stream);
+    case 2: return launch_variant<WFMT, NV, (2 * kAcc <= 32 ? 2 : 1), true>(plan, grid, smem, stream);
+    case 4: return launch_variant<WFMT, NV, (4 * kAcc <= 32 ? 4 : 1), true>(plan, grid, smem, stream);
+    case 8: return launch_variant<WFMT, NV, (8 * kAcc <= 32 ? 8 : 1), true>(plan, grid, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }

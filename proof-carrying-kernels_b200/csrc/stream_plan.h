@@ -1,15 +1,15 @@
 // Launch plan of the persistent streaming kernel (host and device view).
 //
-// A launch processes up to kMaxJobs jobs. A job is a GEMV over W (m, n) with its
-// activations X (batch, n) and outputs Y (batch, m), a check of one GEMV output against
-// its checksum bank, or both (a checked GEMV). Its work is a sequence of "units", each a
-// contiguous byte range that one warp reduces against the activations:
-//   - a W row (n weights)                         -> y[b, row] for every column b
-//   - a segment of a checksum row c[k, beta, :]   -> partial c . x_b (binary64)
-//   - a segment of a bound row a[beta, :]         -> partial a . |x_b| (binary64, up)
+// A launch processes up to kMaxJobs jobs. A job is a GEMV over W (m, n) with activations
+// X (batch, n) and outputs Y (batch, m), a check of one GEMV output against its checksum
+// bank, or both (a checked GEMV). Its work is a sequence of "units", each a contiguous
+// byte range that the CTA's consumer warps reduce against the activations together:
+//   - R consecutive W rows                         -> y[b, row] for every column b
+//   - a segment of a checksum row c[k, beta, :]    -> partial c . x_b (binary64)
+//   - a segment of a bound row a[beta, :]          -> partial a . |x_b| (binary64, up)
 // For a checked job the units of row block beta are laid out contiguously:
-//   [block W rows (fused only)] [checks x segments c-segments] [segments a-segments]
-// and the last unit of the block to finish (an atomic ticket) computes the verdict.
+//   [ceil(block / R) row units (fused only)] [checks x segs c-units] [segs a-units]
+// and the unit of the block that finishes last (an atomic ticket) computes the verdict.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -29,8 +29,23 @@ constexpr int kMaxBatch = 16;
 constexpr int kWeightsBf16 = 0;
 constexpr int kWeightsE4m3 = 1;
 
+// Rows per unit for a tree of 32*nv chains: every consumer warp gets one group of 32
+// chains (or nv/8 of them) for rows_per_warp rows of the unit, so a warp loads each
+// activation vector once per unit and uses it for all its rows.
+__host__ __device__ constexpr int unit_rows(int wfmt, int nv) {
+  return wfmt == kWeightsBf16 ? (nv == 1 ? 8 : nv == 2 ? 4 : nv <= 16 ? 2 : 1)
+                              : (nv == 1 ? 8 : nv <= 8 ? 4 : 2);
+}
+
+// Accumulators per batch column of one consumer warp in a row unit (see Share in
+// stream_kernel.cuh): rows it owns times chain groups it owns.
+__host__ __device__ constexpr int warp_accumulators(int wfmt, int nv) {
+  return nv >= kConsumerWarps ? unit_rows(wfmt, nv) * (nv / kConsumerWarps)
+                              : unit_rows(wfmt, nv) * nv / kConsumerWarps;
+}
+
 struct JobPlan {
-  // GEMV part (has_w): W (m, n) rows are units.
+  // GEMV part (has_w): W (m, n); units of R rows.
   const void* W;
   const uint16_t* X;  // (batch, n) bfloat16 bits
   float* Y;           // (batch, m)
@@ -39,6 +54,10 @@ struct JobPlan {
   int64_t row_bytes;  // n * element size
   int32_t batch;
   int32_t has_w;
+  int32_t rows;       // R, rows per row unit
+  int32_t row_units;  // row units per block (checked) or in total (unchecked)
+  int32_t w_exp_min;  // smallest exponent field of a nonzero weight (1 for subnormals); 0 = unknown
+  int32_t w_exp_max;  // largest exponent field of a weight; 0 = unknown
   // check part (has_check)
   int32_t has_check;
   int32_t block;
@@ -63,12 +82,10 @@ struct JobPlan {
   // partition
   int64_t units;         // total units
   int64_t period_units;  // units per row block (checked) or 1 (unchecked)
-  int64_t period_bytes;  // bytes per period
+  int64_t period_bytes;  // bytes per period (checked)
   int64_t total_bytes;
   int32_t cta_begin;
   int32_t cta_count;
-  int32_t x_fp8_fma;     // host hint unused by the kernel (kept zero)
-  int32_t pad;
 };
 
 struct Plan {
@@ -77,8 +94,8 @@ struct Plan {
   int32_t stages;
   int32_t stage_bytes;
   int32_t x_bytes;
-  int32_t threads;      // tree parameter T (all W jobs share it)
-  int32_t consumers;    // consumer warps in use (staged path); stages is a multiple of it
+  int32_t threads;    // tree parameter T (all W jobs share it)
+  int32_t sum_bytes;  // per-stage scratch for the cross-warp reduction
 };
 
 // Host-side launch of one instantiation family (stream_bf16.cu, stream_e4m3.cu). nv is

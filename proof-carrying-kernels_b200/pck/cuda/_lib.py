@@ -43,7 +43,8 @@ class GemvJob(ctypes.Structure):
 
     _fields_ = [
         ("W", _p), ("X", _p), ("Y", _p), ("m", _i64), ("n", _i64),
-        ("batch", _i32), ("threads", _i32), ("weight_format", _i32), ("reserved", _i32),
+        ("batch", _i32), ("threads", _i32), ("weight_format", _i32),
+        ("w_exp_min", ctypes.c_int16), ("w_exp_max", ctypes.c_int16),
         ("check", ctypes.POINTER(CheckDesc)),
     ]  # fmt: skip
 

@@ -19,6 +19,19 @@ from pck.cuda._ext import extension, on_device, stream_handle
 from pck.cuda.checker import CheckResult, GpuBlockedChecker
 
 
+def exponent_range(W: torch.Tensor) -> tuple[int, int]:
+    """(smallest exponent field of a nonzero weight, subnormals counted as 1; largest
+    exponent field) of bfloat16 ``W``, or (0, 0) when W has no nonzero weight. With these
+    the kernel can prove every product w*x exact in binary32 and add it with one FMA."""
+    mag = W.view(torch.int16).to(torch.int32) & 0x7FFF
+    exp = mag >> 7
+    nonzero = mag != 0
+    if not bool(nonzero.any()):
+        return 0, 0
+    lo = int(torch.where(nonzero, exp.clamp(min=1), torch.full_like(exp, 1000)).min())
+    return lo, int(exp.max())
+
+
 class GemvLaunch:
     """One launch of up to 16 GEMVs y_i = W_i x_i, each optionally checked.
 
@@ -59,6 +72,8 @@ class GemvLaunch:
             job.m, job.n = W.size(0), W.size(1)
             job.batch = x.size(0) if x.dim() == 2 else 1
             job.threads, job.weight_format = threads, self.fmt
+            if self.fmt == _lib.PCK_WEIGHTS_BF16:
+                job.w_exp_min, job.w_exp_max = exponent_range(W)
             if ch is None:
                 job.check = None
                 self.results.append(None)
