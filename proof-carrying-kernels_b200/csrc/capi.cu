@@ -99,7 +99,8 @@ int validate_check(const pck_check_desc* d) {
   return PCK_OK;
 }
 
-constexpr int64_t kUnitTarget = 32 * 1024;  // largest row unit the staged path builds
+constexpr int64_t kPieceTarget = 8 * 1024;  // row piece size the staged path aims for
+constexpr int kMaxSlots = 4;                // ring slots per warp
 
 // Plans and launches the streaming kernel for `specs` (validated by the caller).
 int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
@@ -146,11 +147,11 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   }
   if (live.empty()) return ok();
 
-  // Pass 2: units and bytes of every job.
+  // Pass 2: units and bytes of every job (one row per row unit).
   pck::Plan plan{};
-  const int max_rows = pck::unit_rows(wfmt, nv);
-  int64_t x_bytes = 0, stage_bytes = 0, sum_bytes = 0;
+  int64_t x_bytes = 0;
   std::vector<int64_t> bytes;
+  int64_t max_row_bytes = 0;
   int nj = 0;
   for (const Spec* sp : live) {
     const Spec& s = *sp;
@@ -172,11 +173,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
       jb.batch = s.batch;
     }
     jb.row_bytes = jb.n * esize;
-    int rows = 1;
-    if (tma && s.has_w) {
-      while (rows * 2 <= max_rows && rows * 2 * jb.row_bytes <= kUnitTarget) rows *= 2;
-    }
-    jb.rows = rows;
+    jb.rows = 1;
     if (s.check) {
       const pck_check_desc* d = s.check;
       jb.block = d->block;
@@ -200,62 +197,57 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
       jb.coef = d->coef;
       jb.geps = d->geps;
       jb.tau_floor = d->tau_floor;
-      jb.row_units = s.has_w ? static_cast<int32_t>((d->block + rows - 1) / rows) : 0;
+      jb.row_units = s.has_w ? d->block : 0;
       jb.period_units = jb.row_units + static_cast<int64_t>(d->checks + 1) * jb.segs;
       jb.period_bytes = (s.has_w ? d->block * jb.row_bytes : 0) + (4LL * d->checks + 2) * d->n;
       jb.units = jb.period_units * d->num_blocks;
       jb.total_bytes = jb.period_bytes * d->num_blocks;
-      stage_bytes = std::max<int64_t>(stage_bytes, 4 * len);
     } else {
-      jb.row_units = static_cast<int32_t>((jb.m + rows - 1) / rows);
+      jb.row_units = static_cast<int32_t>(jb.m);
       jb.period_units = 1;
-      jb.period_bytes = rows * jb.row_bytes;
-      jb.units = jb.row_units;
+      jb.period_bytes = jb.row_bytes;
+      jb.units = jb.m;
       jb.total_bytes = jb.m * jb.row_bytes;
     }
-    if (s.has_w) stage_bytes = std::max<int64_t>(stage_bytes, rows * jb.row_bytes);
+    if (s.has_w) max_row_bytes = std::max<int64_t>(max_row_bytes, jb.row_bytes);
     x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 2);
-    sum_bytes = std::max<int64_t>(sum_bytes, std::max<int64_t>(4LL * rows * nv * jb.batch, 64LL * jb.batch));
     plan.jobs[nj++] = jb;
     bytes.push_back(jb.total_bytes);
   }
 
-  // Shared memory: activations, then as many stages (with their scratch) as fit.
+  // Columns reduced together; a batch wider than that re-reads each row from its slot, so
+  // such rows stay whole in one piece.
+  int bg = 1;
+  while (bg * 2 <= 8 && bg * 2 <= max_batch && bg * 2 * nv <= 64) bg *= 2;
+
+  // Staged path: a row piece is whole vector iterations (T * 16 bytes) up to kPieceTarget,
+  // or the whole row; every warp has `slots` slots of the largest piece.
   x_bytes = (x_bytes + 127) / 128 * 128;
-  stage_bytes = (stage_bytes + 127) / 128 * 128;
-  sum_bytes = (sum_bytes + 15) / 16 * 16;
-  int stages = 0;
+  int64_t row_piece = 512, slot_bytes = 512;
+  int slots = 0;
   if (tma) {
-    const int64_t fixed = x_bytes + 8 * 1 + 8 + 256;
-    const int64_t per_stage = stage_bytes + sum_bytes + 2 * 8 + 4;
-    const int64_t fit = (pck::kSmemCap - fixed) / per_stage;
-    stages = static_cast<int>(std::min<int64_t>(pck::kMaxStages, fit));
-    if (stages < 2) tma = false;
-  }
-  if (!tma) {  // the plain path takes one row per unit
-    for (int j = 0; j < nj; ++j) {
-      pck::JobPlan& jb = plan.jobs[j];
-      if (!jb.has_w || jb.rows == 1) continue;
-      jb.rows = 1;
-      if (jb.has_check) {
-        jb.row_units = jb.block;
-        jb.period_units = jb.row_units + static_cast<int64_t>(jb.checks + 1) * jb.segs;
-        jb.units = jb.period_units * jb.num_blocks;
+    const int64_t viter = static_cast<int64_t>(threads) * 16;
+    if (max_row_bytes > 0) {
+      if (max_batch > bg || max_row_bytes <= kPieceTarget) {
+        row_piece = max_row_bytes;
       } else {
-        jb.row_units = static_cast<int32_t>(jb.m);
-        jb.period_bytes = jb.row_bytes;
-        jb.units = jb.m;
+        row_piece = std::max<int64_t>(viter, kPieceTarget / viter * viter);
       }
     }
+    slot_bytes = (std::max<int64_t>(row_piece, 512) + 127) / 128 * 128;
+    const int64_t room = pck::kSmemCap - x_bytes - 8 * (pck::kConsumerWarps * kMaxSlots + 1) - 64;
+    const int64_t fit = room / (pck::kConsumerWarps * slot_bytes);
+    slots = static_cast<int>(std::min<int64_t>(kMaxSlots, fit));
+    if (slots < 1) tma = false;
   }
   size_t smem = 0;
   if (tma) {
-    smem = static_cast<size_t>(x_bytes + stages * (stage_bytes + sum_bytes) + 8 * (2 * stages + 1) +
-                               4 * (stages + 2) + 16);
-    plan.stages = stages;
-    plan.stage_bytes = static_cast<int32_t>(stage_bytes);
+    smem = static_cast<size_t>(x_bytes + pck::kConsumerWarps * slots * slot_bytes +
+                               8 * (pck::kConsumerWarps * slots + 1) + 16);
+    plan.stages = slots;
+    plan.stage_bytes = static_cast<int32_t>(slot_bytes);
     plan.x_bytes = static_cast<int32_t>(x_bytes);
-    plan.sum_bytes = static_cast<int32_t>(sum_bytes);
+    plan.sum_bytes = static_cast<int32_t>(row_piece);
   }
 
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs
@@ -298,11 +290,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   plan.njobs = nj;
   plan.threads = threads;
 
-  int bg = 1;
-  if (tma) {
-    const int acc = pck::warp_accumulators(wfmt, nv);
-    while (bg * 2 <= 8 && bg * 2 <= max_batch && bg * 2 * acc <= 32) bg *= 2;
-  }
+  if (!tma) bg = 1;
   const unsigned grid = static_cast<unsigned>(begin);
   const cudaError_t err = wfmt == pck::kWeightsBf16
                               ? pck::launch_stream_bf16(plan, nv, bg, tma, grid, smem, stream)

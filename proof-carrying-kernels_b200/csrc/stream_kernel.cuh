@@ -1,25 +1,25 @@
 // The persistent streaming kernel: GEMV rows, checksum-bank segments and the block
 // verdicts of the trusted checker, for every job of a launch plan (stream_plan.h).
 //
-// Staged path (kTma): one producer warp streams each unit's bytes from HBM into a ring of
-// shared-memory stages with cp.async.bulk (completion counted as transaction bytes on a
-// per-stage "full" mbarrier); the activations X of the CTA's job are copied to shared
-// memory once. All eight consumer warps work on every stage, in order: each takes its
-// share of the unit, publishes a partial result in the stage's scratch and takes a ticket
-// (a shared-memory atomic); the warp with the last ticket finishes the unit (final
-// reduction, store) and every warp hands the stage back through its "empty" mbarrier
-// (eight arrivals). Because every warp consumes every stage in order, a warp waiting for
-// use u of a stage has itself consumed use u - 1, so the mbarrier parity waits are exact.
-// Plain path (unaligned pointers, n not a multiple of the vector width): each warp takes
-// whole units and reads global memory directly; the arithmetic is the same.
+// Staged path (kTma): each of the eight warps of a CTA owns the units w, w + 8, ... of the
+// CTA's range and streams them through its own ring of `slots` shared-memory pieces with
+// cp.async.bulk: lane 0 arms the piece's mbarrier with the expected bytes and issues the
+// copy; the warp waits for the barrier's phase, reduces the piece, and refills the same
+// slot with its next piece. Each slot is used by one warp in order, so every parity wait
+// is exact. Rows longer than a piece are split at vector-iteration boundaries and their
+// chains carry over in registers. The activations X of the CTA's job are copied to shared
+// memory once. Plain path (unaligned pointers, n not a multiple of the vector width): the
+// same units read straight from global memory with scalar loads; the arithmetic is the
+// same.
 //
 // GEMV row arithmetic (bit-exact with the reference's model of its coalesced kernel,
 // src/pck/gemv.py:71-101 / src/pck/cuda/csrc/gemv_kernel.cu:139-178): with T = 32*NV
 // chains, chain t = 32*g + l (group g, lane l) owns vectors t, t + T, ... of V columns
 // (V = 8 bfloat16 or 16 E4M3 weights per 16-byte vector) and adds its products in order
 // (binary32 product, then binary32 sum — or one FMA where the product is provably exact).
-// Each group of 32 chains is reduced by halving across lanes (l += l + 16, ..., l += l + 1)
-// and the NV group sums by halving again (g += g + NV/2, ..., g += g + 1).
+// Lane l holds the NV chains l, 32 + l, ... of the row; each group of 32 chains is reduced
+// by halving across lanes (l += l + 16, ..., l += l + 1) and the NV group sums by halving
+// again (g += g + NV/2, ..., g += g + 1); `halve_groups` evaluates exactly those additions.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -347,10 +347,11 @@ __device__ __forceinline__ void c_segment(const float* __restrict__ cs,
         acc = __fma_rn(static_cast<double>(cv.z), static_cast<double>(bf16_lo(xv.y)), acc);
         acc = __fma_rn(static_cast<double>(cv.w), static_cast<double>(bf16_hi(xv.y)), acc);
       }
-    } else {
-      for (int64_t j = lane; j < len; j += kWarp) {
-        acc = __fma_rn(static_cast<double>(cs[j]), static_cast<double>(bf16_bits_to_float(xb[j])),
-                       acc);
+    } else {  // the same element order as above: lane l takes 4l..4l+3, then + 128
+      for (int64_t j = lane * 4; j < len; j += 4 * kWarp) {
+        for (int64_t e = j; e < j + 4 && e < len; ++e) {
+          acc = __fma_rn(static_cast<double>(cs[e]), static_cast<double>(bf16_bits_to_float(xb[e])), acc);
+        }
       }
     }
     acc = warp_sum_rn(acc);
@@ -376,10 +377,12 @@ __device__ __forceinline__ void a_segment(const uint16_t* __restrict__ as,
         acc = __fma_ru(static_cast<double>(bf16_lo(av.y)), fabs(static_cast<double>(bf16_lo(xv.y))), acc);
         acc = __fma_ru(static_cast<double>(bf16_hi(av.y)), fabs(static_cast<double>(bf16_hi(xv.y))), acc);
       }
-    } else {
-      for (int64_t j = lane; j < len; j += kWarp) {
-        acc = __fma_ru(static_cast<double>(bf16_bits_to_float(as[j])),
-                       fabs(static_cast<double>(bf16_bits_to_float(xb[j]))), acc);
+    } else {  // the same element order as above
+      for (int64_t j = lane * 4; j < len; j += 4 * kWarp) {
+        for (int64_t e = j; e < j + 4 && e < len; ++e) {
+          acc = __fma_ru(static_cast<double>(bf16_bits_to_float(as[e])),
+                         fabs(static_cast<double>(bf16_bits_to_float(xb[e]))), acc);
+        }
       }
     }
     acc = warp_sum_ru(acc);
@@ -486,7 +489,7 @@ __device__ __forceinline__ void plain_unit(const JobPlan& jb, const Unit& un, co
 }
 
 // ---------------------------------------------------------------------------------------
-// Staged path: all consumer warps share each unit.
+// Staged path: every warp streams its own units through a private ring of pieces.
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
@@ -502,184 +505,106 @@ __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   return v;
 }
 
-// Which chains and rows of a row unit a consumer warp owns. Pairs (row r, group g) are
-// dealt to the eight warps: with NV >= 8 groups, warp w takes groups w, w + 8, ... for
-// every row; with fewer, warp w takes group w % NV for rows w / NV, w / NV + 8 / NV, ...
-// A warp loads each activation vector once and uses it for all its rows.
-template <int WFMT, int NV>
-struct Share {
-  static constexpr int kRows = unit_rows(WFMT, NV);                    // rows per unit, max
-  static constexpr int kGroups = NV >= kConsumerWarps ? NV / kConsumerWarps : 1;
-  static constexpr int kRowsPerWarp = NV >= kConsumerWarps ? kRows : kRows * NV / kConsumerWarps;
-  static __device__ __forceinline__ int group(int warp, int j) {
-    return NV >= kConsumerWarps ? warp + kConsumerWarps * j : warp % NV;
-  }
-  static __device__ __forceinline__ int row(int warp, int k) {
-    return NV >= kConsumerWarps ? k : warp / NV + (kConsumerWarps / NV) * k;
+// Orders this thread's earlier shared-memory reads before a later bulk copy into the same
+// bytes (generic proxy, then async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Row accumulators of one warp: NV chains per lane for each of BG batch columns.
+template <int WFMT, int NV, int BG>
+struct RowState {
+  float acc[BG][NV];
+  __device__ __forceinline__ void reset() {
+#pragma unroll
+    for (int b = 0; b < BG; ++b)
+#pragma unroll
+      for (int g = 0; g < NV; ++g) acc[b][g] = -0.0f;  // -0 + p == p for every p
   }
 };
 
-__device__ __forceinline__ float lane_halving(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_down_sync(kFullMask, v, o));
-  return v;
-}
-
-// This warp's share of a row unit at stage address `stage` (rows of row_bytes), against
-// the activations at `xs` (batch rows of n bfloat16). Publishes the group sums
-// sums[(r * NV + g) * batch + b] for its (row, group) pairs.
+// The vector iterations [v_lo, v_hi) of a row against columns [g0, g0 + BG) of X. The piece
+// holds the row bytes from vector v_lo * T on; vector q of the row is at
+// piece + (q - v_lo * T) * 16. nvec = n / V (n % V == 0 on this path).
 template <int WFMT, int NV, int BG, bool kFma>
-__device__ __forceinline__ void rows_share(const JobPlan& jb, uint32_t stage, uint32_t xs, float* sums,
-                                           int rows_here, int warp, int lane) {
-  using S = Share<WFMT, NV>;
+__device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uint32_t piece, uint32_t xs,
+                                          uint32_t xcol, int g0, int batch, int v_lo, int v_hi,
+                                          int nvec, int lane) {
   constexpr int V = Format<WFMT>::kVec;
   constexpr int T = NV * kWarp;
-  constexpr uint32_t kWV = 16;          // bytes of one weight vector
-  constexpr uint32_t kXV = V * 2;       // bytes of one activation vector (16 or 32)
-  const int nvec = static_cast<int>(jb.n / V);  // n % V == 0 on this path
-  const int full = nvec / T;
-  const bool tail = full * T != nvec;
-  const uint32_t row_bytes = static_cast<uint32_t>(jb.row_bytes);
-  const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
-  const int batch = jb.batch;
-  for (int g0 = 0; g0 < batch; g0 += BG) {
-    float acc[S::kRowsPerWarp][S::kGroups][BG];
+  constexpr uint32_t kXV = V * 2;  // bytes of one activation vector
+  uint32_t xcol_addr[BG];
 #pragma unroll
-    for (int k = 0; k < S::kRowsPerWarp; ++k)
+  for (int b = 0; b < BG; ++b) xcol_addr[b] = xs + static_cast<uint32_t>(min(g0 + b, batch - 1)) * xcol;
+  for (int v = v_lo; v < v_hi; ++v) {
+    const uint32_t wbase = piece + static_cast<uint32_t>((v - v_lo) * T + lane) * 16u;
+    const int qbase = v * T + lane;
+    const bool partial = (v + 1) * T > nvec;
 #pragma unroll
-      for (int j = 0; j < S::kGroups; ++j)
+    for (int g = 0; g < NV; ++g) {
+      const int q = qbase + g * kWarp;
+      if (partial && q >= nvec) {  // padding past n: +0 terms
 #pragma unroll
-        for (int b = 0; b < BG; ++b) acc[k][j][b] = -0.0f;  // -0 + p == p for every p
-
-    const int iters = full + (tail ? 1 : 0);
-    for (int v = 0; v < iters; ++v) {
-#pragma unroll
-      for (int j = 0; j < S::kGroups; ++j) {
-        const int q = v * T + S::group(warp, j) * kWarp + lane;
-        if (v == full && q >= nvec) {  // padding past n: +0 terms
-#pragma unroll
-          for (int k = 0; k < S::kRowsPerWarp; ++k)
-#pragma unroll
-            for (int b = 0; b < BG; ++b) acc[k][j][b] = __fadd_rn(acc[k][j][b], 0.0f);
-          continue;
-        }
-        uint4 xa[BG], xb[BG];
-#pragma unroll
-        for (int b = 0; b < BG; ++b) {
-          const uint32_t xaddr = xs + static_cast<uint32_t>(min(g0 + b, batch - 1)) * xcol + q * kXV;
-          xa[b] = lds128(xaddr);
-          if constexpr (WFMT == kWeightsE4m3) xb[b] = lds128(xaddr + 16);
-        }
-#pragma unroll
-        for (int k = 0; k < S::kRowsPerWarp; ++k) {
-          const int r = S::row(warp, k);
-          if (r < rows_here) {
-            const uint4 wv = lds128(stage + r * row_bytes + q * kWV);
-#pragma unroll
-            for (int b = 0; b < BG; ++b) {
-              if constexpr (WFMT == kWeightsBf16) {
-                if constexpr (kFma) {
-                  chain_pair<true>(acc[k][j][b], bf16_lo(wv.x), bf16_lo(xa[b].x));
-                  chain_pair<true>(acc[k][j][b], bf16_hi(wv.x), bf16_hi(xa[b].x));
-                  chain_pair<true>(acc[k][j][b], bf16_lo(wv.y), bf16_lo(xa[b].y));
-                  chain_pair<true>(acc[k][j][b], bf16_hi(wv.y), bf16_hi(xa[b].y));
-                  chain_pair<true>(acc[k][j][b], bf16_lo(wv.z), bf16_lo(xa[b].z));
-                  chain_pair<true>(acc[k][j][b], bf16_hi(wv.z), bf16_hi(xa[b].z));
-                  chain_pair<true>(acc[k][j][b], bf16_lo(wv.w), bf16_lo(xa[b].w));
-                  chain_pair<true>(acc[k][j][b], bf16_hi(wv.w), bf16_hi(xa[b].w));
-                } else {
-                  chain_bf16(acc[k][j][b], wv, xa[b]);
-                }
-              } else {
-                chain_e4m3<kFma>(acc[k][j][b], wv, xa[b], xb[b]);
-              }
-            }
-          }
-        }
+        for (int b = 0; b < BG; ++b) st.acc[b][g] = __fadd_rn(st.acc[b][g], 0.0f);
+        continue;
       }
-    }
+      const uint4 wv = lds128(wbase + g * (kWarp * 16u));
 #pragma unroll
-    for (int k = 0; k < S::kRowsPerWarp; ++k) {
-      const int r = S::row(warp, k);
-#pragma unroll
-      for (int j = 0; j < S::kGroups; ++j) {
-#pragma unroll
-        for (int b = 0; b < BG; ++b) {
-          const float s = lane_halving(acc[k][j][b]);
-          if (lane == 0 && r < rows_here && g0 + b < batch) {
-            sums[(r * NV + S::group(warp, j)) * batch + g0 + b] = s;
+      for (int b = 0; b < BG; ++b) {
+        const uint32_t xaddr = xcol_addr[b] + static_cast<uint32_t>(q) * kXV;
+        const uint4 xa = lds128(xaddr);
+        if constexpr (WFMT == kWeightsBf16) {
+          if constexpr (kFma) {
+            chain_pair<true>(st.acc[b][g], bf16_lo(wv.x), bf16_lo(xa.x));
+            chain_pair<true>(st.acc[b][g], bf16_hi(wv.x), bf16_hi(xa.x));
+            chain_pair<true>(st.acc[b][g], bf16_lo(wv.y), bf16_lo(xa.y));
+            chain_pair<true>(st.acc[b][g], bf16_hi(wv.y), bf16_hi(xa.y));
+            chain_pair<true>(st.acc[b][g], bf16_lo(wv.z), bf16_lo(xa.z));
+            chain_pair<true>(st.acc[b][g], bf16_hi(wv.z), bf16_hi(xa.z));
+            chain_pair<true>(st.acc[b][g], bf16_lo(wv.w), bf16_lo(xa.w));
+            chain_pair<true>(st.acc[b][g], bf16_hi(wv.w), bf16_hi(xa.w));
+          } else {
+            chain_bf16(st.acc[b][g], wv, xa);
           }
+        } else {
+          const uint4 xb = lds128(xaddr + 16);
+          chain_e4m3<kFma>(st.acc[b][g], wv, xa, xb);
         }
       }
     }
   }
 }
 
-// Last warp of a row unit: halving over the NV group sums of every (row, column).
-template <int NV>
-__device__ __forceinline__ void rows_finish(const JobPlan& jb, const float* sums, int64_t row0,
-                                            int rows_here, int lane) {
-  const int batch = jb.batch;
-  for (int o = lane; o < rows_here * batch; o += kWarp) {
-    const int r = o / batch;
-    const int b = o - r * batch;
-    float g[NV];
-#pragma unroll
-    for (int i = 0; i < NV; ++i) g[i] = sums[(r * NV + i) * batch + b];
-#pragma unroll
-    for (int h = NV / 2; h >= 1; h /= 2) {
-#pragma unroll
-      for (int i = 0; i < h; ++i) g[i] = __fadd_rn(g[i], g[i + h]);
-    }
-    jb.Y[static_cast<int64_t>(b) * jb.m + row0 + r] = g[0];
-  }
-}
-
-// This warp's share of a c- or a-segment: elements (4 at a time) warp*32 + lane, + 256, ...
-// Publishes dsums[warp * batch + b].
+// Elements [e_lo, e_hi) of a c- or a-segment (element e of the piece at piece + e * size):
+// lane l adds elements 4l..4l+3, then + 128, ..., in order — the same order as the plain
+// path's c_segment / a_segment over the whole segment when e_lo is a multiple of 128.
 template <bool kAbs>
-__device__ __forceinline__ void segment_share(const JobPlan& jb, const Unit& un, uint32_t stage,
-                                              uint32_t xs, double* dsums, int warp, int lane) {
-  const int batch = jb.batch;
-  const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
-  const int len = static_cast<int>(un.len);
-  for (int b = 0; b < batch; ++b) {
-    const uint32_t xb = xs + static_cast<uint32_t>(b) * xcol + static_cast<uint32_t>(un.col0) * 2;
-    double acc = 0.0;
-    for (int e = (warp * kWarp + lane) * 4; e < len; e += kConsumerWarps * kWarp * 4) {
-      const uint2 xv = lds64(xb + e * 2);
-      if constexpr (kAbs) {
-        const uint2 av = lds64(stage + e * 2);
-        acc = __fma_ru(static_cast<double>(bf16_lo(av.x)), fabs(static_cast<double>(bf16_lo(xv.x))), acc);
-        acc = __fma_ru(static_cast<double>(bf16_hi(av.x)), fabs(static_cast<double>(bf16_hi(xv.x))), acc);
-        acc = __fma_ru(static_cast<double>(bf16_lo(av.y)), fabs(static_cast<double>(bf16_lo(xv.y))), acc);
-        acc = __fma_ru(static_cast<double>(bf16_hi(av.y)), fabs(static_cast<double>(bf16_hi(xv.y))), acc);
-      } else {
-        const uint4 cv = lds128(stage + e * 4);
-        acc = __fma_rn(static_cast<double>(__uint_as_float(cv.x)), static_cast<double>(bf16_lo(xv.x)), acc);
-        acc = __fma_rn(static_cast<double>(__uint_as_float(cv.y)), static_cast<double>(bf16_hi(xv.x)), acc);
-        acc = __fma_rn(static_cast<double>(__uint_as_float(cv.z)), static_cast<double>(bf16_lo(xv.y)), acc);
-        acc = __fma_rn(static_cast<double>(__uint_as_float(cv.w)), static_cast<double>(bf16_hi(xv.y)), acc);
-      }
-    }
-    acc = kAbs ? warp_sum_ru(acc) : warp_sum_rn(acc);
-    if (lane == 0) dsums[warp * batch + b] = acc;
-  }
-}
-
-// Last warp of a segment: the warp partials in warp order, stored to the block's scratch.
-__device__ __forceinline__ void segment_finish(const JobPlan& jb, const Unit& un, const double* dsums,
-                                               int lane) {
-  const int batch = jb.batch;
-  const int64_t nb = jb.num_blocks;
-  for (int b = lane; b < batch; b += kWarp) {
-    double total = 0.0;
-    if (un.kind == kUnitC) {
-      for (int w = 0; w < kConsumerWarps; ++w) total = __dadd_rn(total, dsums[w * batch + b]);
-      jb.partial_cx[((static_cast<int64_t>(b) * jb.checks + un.k) * nb + un.beta) * jb.seg_alloc + un.s] = total;
+__device__ __forceinline__ void segment_piece(double* acc, uint32_t piece, uint32_t xs, uint32_t xcol,
+                                              int64_t col0, int batch, int e_lo, int e_hi, int lane) {
+  for (int e = e_lo + lane * 4; e < e_hi; e += 4 * kWarp) {
+    const uint32_t off = static_cast<uint32_t>(e - e_lo);
+    uint4 cv;
+    uint2 av;
+    if constexpr (kAbs) {
+      av = lds64(piece + off * 2);
     } else {
-      for (int w = 0; w < kConsumerWarps; ++w) total = __dadd_ru(total, dsums[w * batch + b]);
-      jb.partial_s[(static_cast<int64_t>(b) * nb + un.beta) * jb.seg_alloc + un.s] = total;
+      cv = lds128(piece + off * 4);
+    }
+    for (int b = 0; b < batch; ++b) {
+      const uint2 xv = lds64(xs + static_cast<uint32_t>(b) * xcol + static_cast<uint32_t>(col0 + e) * 2);
+      double a = acc[b];
+      if constexpr (kAbs) {
+        a = __fma_ru(static_cast<double>(bf16_lo(av.x)), fabs(static_cast<double>(bf16_lo(xv.x))), a);
+        a = __fma_ru(static_cast<double>(bf16_hi(av.x)), fabs(static_cast<double>(bf16_hi(xv.x))), a);
+        a = __fma_ru(static_cast<double>(bf16_lo(av.y)), fabs(static_cast<double>(bf16_lo(xv.y))), a);
+        a = __fma_ru(static_cast<double>(bf16_hi(av.y)), fabs(static_cast<double>(bf16_hi(xv.y))), a);
+      } else {
+        a = __fma_rn(static_cast<double>(__uint_as_float(cv.x)), static_cast<double>(bf16_lo(xv.x)), a);
+        a = __fma_rn(static_cast<double>(__uint_as_float(cv.y)), static_cast<double>(bf16_hi(xv.x)), a);
+        a = __fma_rn(static_cast<double>(__uint_as_float(cv.z)), static_cast<double>(bf16_lo(xv.y)), a);
+        a = __fma_rn(static_cast<double>(__uint_as_float(cv.w)), static_cast<double>(bf16_hi(xv.y)), a);
+      }
+      acc[b] = a;
     }
   }
 }
@@ -717,9 +642,151 @@ __device__ __forceinline__ bool fma_is_exact(const JobPlan& jb, unsigned x_lo, u
   }
 }
 
+// A warp's walk over its pieces: units warp, warp + 8, ... of the CTA's range, each cut
+// into pieces.
+// Rows are cut into pieces of row_piece bytes (whole vector iterations), checksum-bank
+// segments into pieces of seg_piece bytes (a multiple of 512, so every piece starts at a
+// multiple of 128 elements and the lanes add the elements in one fixed order).
+struct PieceWalk {
+  int64_t unit;   // CTA-local unit index
+  int piece;
+  int pieces;     // pieces of `unit`
+  uint32_t size;  // piece size of `unit`
+  Unit un;
+};
+
+__device__ __forceinline__ void walk_to(PieceWalk& w, const JobPlan& jb, int64_t u0, int64_t local,
+                                        int64_t count, uint32_t row_piece, uint32_t seg_piece) {
+  w.unit = local;
+  w.piece = 0;
+  if (local < count) {
+    w.un = decode_unit(jb, u0 + local);
+    w.size = w.un.kind == kUnitRow ? row_piece : seg_piece;
+    w.pieces = static_cast<int>((w.un.bytes + w.size - 1) / w.size);
+  } else {
+    w.pieces = 0;
+  }
+}
+
+__device__ __forceinline__ void walk_next(PieceWalk& w, const JobPlan& jb, int64_t u0, int64_t count,
+                                          uint32_t row_piece, uint32_t seg_piece) {
+  if (++w.piece >= w.pieces) walk_to(w, jb, u0, w.unit + kConsumerWarps, count, row_piece, seg_piece);
+}
+
+template <int WFMT, int NV, int BG, bool kFma>
+__device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots,
+                                            uint32_t slot_bytes, uint32_t row_piece, uint8_t* ring,
+                                            uint64_t* full, uint32_t xs, int warp, int lane) {
+  constexpr int V = Format<WFMT>::kVec;
+  constexpr int T = NV * kWarp;
+  const uint64_t once = policy_evict_first();
+  const uint32_t ring_addr = smem_addr(ring);
+  const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
+  const int nvec = static_cast<int>(jb.n / V);
+  const int vtotal = (nvec + T - 1) / T;
+  const int vpp = static_cast<int>(row_piece / (T * 16u));  // vector iterations per row piece
+  const uint32_t seg_piece = slot_bytes / 512u * 512u;
+
+  PieceWalk issue, take;
+  walk_to(issue, jb, u0, warp, count, row_piece, seg_piece);
+  walk_to(take, jb, u0, warp, count, row_piece, seg_piece);
+  int64_t issued = 0, taken = 0;
+  auto issue_one = [&]() {
+    const int slot = static_cast<int>(issued % slots);
+    if (lane == 0) {
+      const uint32_t off = static_cast<uint32_t>(issue.piece) * issue.size;
+      const uint32_t bytes = min(issue.size, issue.un.bytes - off);
+      mbar_arrive_expect_tx(full + slot, bytes);
+      bulk_load(ring + static_cast<int64_t>(slot) * slot_bytes, static_cast<const uint8_t*>(issue.un.src) + off,
+                bytes, full + slot, once);
+    }
+    ++issued;
+    walk_next(issue, jb, u0, count, row_piece, seg_piece);
+  };
+  for (int s = 0; s < slots && issue.pieces > 0; ++s) issue_one();
+
+  RowState<WFMT, NV, BG> row;
+  double dacc[kMaxBatch];
+  int64_t cur_beta = -1;
+  uint32_t pending = 0;
+  bool ok = true;
+  while (take.pieces > 0) {
+    const int slot = static_cast<int>(taken % slots);
+    if (!mbar_wait(full + slot, static_cast<uint32_t>((taken / slots) & 1))) {
+      ok = false;
+      break;
+    }
+    const uint32_t piece = ring_addr + static_cast<uint32_t>(slot) * slot_bytes;
+    const Unit& un = take.un;
+    const bool first = take.piece == 0;
+    const bool last = take.piece + 1 == take.pieces;
+    if (un.kind == kUnitRow) {
+      // one piece per column group when the batch exceeds BG (the host keeps such rows whole)
+      for (int g0 = 0; g0 < jb.batch; g0 += BG) {
+        if (first) row.reset();
+        const int v_lo = take.piece * vpp;
+        const int v_hi = min(v_lo + vpp, vtotal);
+        reduce_row_piece<WFMT, NV, BG, kFma>(row, piece, xs, xcol, g0, jb.batch, v_lo, v_hi, nvec, lane);
+        if (last) {
+#pragma unroll
+          for (int b = 0; b < BG; ++b) {
+            const float yv = halve_groups<NV>(row.acc[b], lane);
+            if (lane == 0 && g0 + b < jb.batch) jb.Y[static_cast<int64_t>(g0 + b) * jb.m + un.row] = yv;
+          }
+        }
+      }
+    } else {
+      if (first) {
+        for (int b = 0; b < jb.batch; ++b) dacc[b] = 0.0;
+      }
+      const int esz = un.kind == kUnitC ? 4 : 2;
+      const int e_lo = static_cast<int>(static_cast<int64_t>(take.piece) * take.size / esz);
+      const int e_hi = static_cast<int>(min(static_cast<int64_t>(e_lo) + take.size / esz, un.len));
+      if (un.kind == kUnitC) {
+        segment_piece<false>(dacc, piece, xs, xcol, un.col0, jb.batch, e_lo, e_hi, lane);
+      } else {
+        segment_piece<true>(dacc, piece, xs, xcol, un.col0, jb.batch, e_lo, e_hi, lane);
+      }
+      if (last) {
+        const int64_t nb = jb.num_blocks;
+        for (int b = 0; b < jb.batch; ++b) {
+          if (un.kind == kUnitC) {
+            const double t = warp_sum_rn(dacc[b]);
+            if (lane == 0) {
+              jb.partial_cx[((static_cast<int64_t>(b) * jb.checks + un.k) * nb + un.beta) * jb.seg_alloc + un.s] = t;
+            }
+          } else {
+            const double t = warp_sum_ru(dacc[b]);
+            if (lane == 0) jb.partial_s[(static_cast<int64_t>(b) * nb + un.beta) * jb.seg_alloc + un.s] = t;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    ++taken;
+    if (issue.pieces > 0) {  // refill the slot just consumed
+      if (lane == 0) fence_proxy_async_smem();
+      issue_one();
+    }
+    const int64_t beta = un.beta;
+    const bool unit_done = last;
+    walk_next(take, jb, u0, count, row_piece, seg_piece);
+    if (unit_done && jb.has_check) {
+      if (beta != cur_beta && pending) {
+        credit_block(jb, cur_beta, pending, lane);
+        pending = 0;
+      }
+      cur_beta = beta;
+      ++pending;
+    }
+  }
+  if (ok && pending) credit_block(jb, cur_beta, pending, lane);
+  // Leave only after every copy into this warp's slots has landed.
+  for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
+}
+
 template <int WFMT, int NV, int BG, bool kTma>
-__global__ void __launch_bounds__(kTma ? kTmaThreads : kPlainThreads, 1)
-    stream_kernel(const __grid_constant__ Plan plan) {
+__global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_constant__ Plan plan) {
   extern __shared__ __align__(128) uint8_t smem[];
   int j = 0;
   while (j + 1 < plan.njobs && static_cast<int>(blockIdx.x) >= plan.jobs[j + 1].cta_begin) ++j;
@@ -734,116 +801,43 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kPlainThreads, 1)
   const int lane = static_cast<int>(threadIdx.x) % kWarp;
 
   if constexpr (kTma) {
-    const int stages = plan.stages;
-    const int sum_bytes = plan.sum_bytes;
+    const int slots = plan.stages;  // per warp
+    const uint32_t slot_bytes = static_cast<uint32_t>(plan.stage_bytes);
+    const uint32_t row_piece = static_cast<uint32_t>(plan.sum_bytes);
     uint8_t* xs = smem;
-    uint8_t* ring = smem + plan.x_bytes;
-    uint8_t* scratch = ring + static_cast<int64_t>(stages) * plan.stage_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(scratch + static_cast<int64_t>(stages) * sum_bytes);
-    uint64_t* empty = full + stages;
-    uint64_t* xbar = empty + stages;
-    uint32_t* tickets = reinterpret_cast<uint32_t*>(xbar + 1);
-    uint32_t* xexp = tickets + stages;  // [0] smallest, [1] largest exponent field of x
+    uint8_t* rings = smem + plan.x_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rings + static_cast<int64_t>(kConsumerWarps) * slots * slot_bytes);
+    uint64_t* xbar = bars + kConsumerWarps * slots;
+    uint32_t* xexp = reinterpret_cast<uint32_t*>(xbar + 1);  // [0] smallest, [1] largest exponent of x
     if (threadIdx.x == 0) {
-      for (int s = 0; s < stages; ++s) {
-        mbar_init(full + s, 1);
-        mbar_init(empty + s, kConsumerWarps);
-        tickets[s] = 0;
-      }
+      for (int s = 0; s < kConsumerWarps * slots; ++s) mbar_init(bars + s, 1);
       mbar_init(xbar, 1);
       xexp[0] = 1000;
       xexp[1] = 0;
       fence_barrier_init();
     }
     __syncthreads();
-
-    if (warp == kConsumerWarps) {  // producer
-      if (lane == 0) {
-        const uint64_t keep = policy_evict_last();
-        const uint64_t once = policy_evict_first();
-        const uint32_t xbytes = static_cast<uint32_t>(static_cast<int64_t>(jb.batch) * jb.n * 2);
-        mbar_arrive_expect_tx(xbar, xbytes);
-        bulk_load(xs, jb.X, xbytes, xbar, keep);
-        int64_t issued = 0;
-        for (int64_t i = 0; i < count; ++i) {
-          const int st = static_cast<int>(i % stages);
-          if (i >= stages && !mbar_wait(empty + st, static_cast<uint32_t>((i / stages - 1) & 1))) break;
-          const Unit un = decode_unit(jb, u0 + i);
-          mbar_arrive_expect_tx(full + st, un.bytes);
-          bulk_load(ring + static_cast<int64_t>(st) * plan.stage_bytes, un.src, un.bytes, full + st, once);
-          ++issued;
-        }
-        // Leave only after every copy into this CTA's shared memory has landed.
-        for (int64_t i = issued > stages ? issued - stages : 0; i < issued; ++i) {
-          mbar_wait(full + i % stages, static_cast<uint32_t>((i / stages) & 1));
-        }
-        mbar_wait(xbar, 0);
-      }
-      return;
+    if (threadIdx.x == 0) {
+      const uint32_t xbytes = static_cast<uint32_t>(static_cast<int64_t>(jb.batch) * jb.n * 2);
+      mbar_arrive_expect_tx(xbar, xbytes);
+      bulk_load(xs, jb.X, xbytes, xbar, policy_evict_last());
     }
-
-    // consumers
-    const uint16_t* X = reinterpret_cast<const uint16_t*>(xs);
     const bool have_x = mbar_wait(xbar, 0);
     if (have_x && jb.has_w) {
-      x_exponents(X, static_cast<int64_t>(jb.batch) * jb.n, static_cast<int>(threadIdx.x), kPlainThreads,
-                  xexp, xexp + 1);
+      x_exponents(reinterpret_cast<const uint16_t*>(xs), static_cast<int64_t>(jb.batch) * jb.n,
+                  static_cast<int>(threadIdx.x), kPlainThreads, xexp, xexp + 1);
     }
-    named_barrier(1, kPlainThreads);
+    __syncthreads();
     if (!have_x) return;
     const bool fma = jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]);
+    uint8_t* ring = rings + static_cast<int64_t>(warp) * slots * slot_bytes;
+    uint64_t* full = bars + warp * slots;
     const uint32_t xs_addr = smem_addr(xs);
-    const uint32_t ring_addr = smem_addr(ring);
-
-    int64_t cur_beta = -1;
-    uint32_t pending = 0;
-    for (int64_t i = 0; i < count; ++i) {
-      const int st = static_cast<int>(i % stages);
-      if (!mbar_wait(full + st, static_cast<uint32_t>((i / stages) & 1))) return;
-      const Unit un = decode_unit(jb, u0 + i);
-      const uint32_t stage = ring_addr + static_cast<uint32_t>(st) * static_cast<uint32_t>(plan.stage_bytes);
-      uint8_t* sums = scratch + static_cast<int64_t>(st) * sum_bytes;
-      if (un.kind == kUnitRow) {
-        if (fma) {
-          rows_share<WFMT, NV, BG, true>(jb, stage, xs_addr, reinterpret_cast<float*>(sums), un.rows, warp, lane);
-        } else {
-          rows_share<WFMT, NV, BG, false>(jb, stage, xs_addr, reinterpret_cast<float*>(sums), un.rows, warp, lane);
-        }
-      } else if (un.kind == kUnitC) {
-        segment_share<false>(jb, un, stage, xs_addr, reinterpret_cast<double*>(sums), warp, lane);
-      } else {
-        segment_share<true>(jb, un, stage, xs_addr, reinterpret_cast<double*>(sums), warp, lane);
-      }
-      __syncwarp();
-      uint32_t ticket = 0;
-      if (lane == 0) {
-        __threadfence_block();
-        ticket = atomicAdd(tickets + st, 1u);
-      }
-      ticket = __shfl_sync(kFullMask, ticket, 0);
-      const bool last = ticket == kConsumerWarps - 1;
-      if (last) {
-        __threadfence_block();
-        if (un.kind == kUnitRow) {
-          rows_finish<NV>(jb, reinterpret_cast<const float*>(sums), un.row, un.rows, lane);
-        } else {
-          segment_finish(jb, un, reinterpret_cast<const double*>(sums), lane);
-        }
-        __syncwarp();
-        if (lane == 0) tickets[st] = 0;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty + st);
-      if (last && jb.has_check) {
-        if (un.beta != cur_beta && pending) {
-          credit_block(jb, cur_beta, pending, lane);
-          pending = 0;
-        }
-        cur_beta = un.beta;
-        ++pending;
-      }
+    if (fma) {
+      staged_warp<WFMT, NV, BG, true>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane);
+    } else {
+      staged_warp<WFMT, NV, BG, false>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane);
     }
-    if (pending) credit_block(jb, cur_beta, pending, lane);
   } else {
     // Plain path: every warp takes whole units and reads global memory directly, one
     // element at a time (product, then sum: the same values as the staged path's).

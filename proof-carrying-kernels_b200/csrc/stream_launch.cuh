@@ -23,7 +23,7 @@ cudaError_t launch_variant(const Plan& plan, unsigned grid, size_t smem, cudaStr
       configured[dev] = 1;
     }
   }
-  fn<<<grid, kTma ? kTmaThreads : kPlainThreads, smem, stream>>>(plan);
+  fn<<<grid, kPlainThreads, smem, stream>>>(plan);
   return cudaGetLastError();
 }
 
@@ -34,9 +34,9 @@ cudaError_t launch_nv(const Plan& plan, int bg, bool tma, unsigned grid, size_t 
   constexpr int kAcc = warp_accumulators(WFMT, NV);
   switch (bg) {
     case 1: return launch_variant<WFMT, NV, 1, true>(plan, grid, smem, stream);
-    case 2: return launch_variant<WFMT, NV, (2 * kAcc <= 32 ? 2 : 1), true>(plan, grid, smem, stream);
-    case 4: return launch_variant<WFMT, NV, (4 * kAcc <= 32 ? 4 : 1), true>(plan, grid, smem, stream);
-    case 8: return launch_variant<WFMT, NV, (8 * kAcc <= 32 ? 8 : 1), true>(plan, grid, smem, stream);
+    case 2: return launch_variant<WFMT, NV, (2 * kAcc <= 64 ? 2 : 1), true>(plan, grid, smem, stream);
+    case 4: return launch_variant<WFMT, NV, (4 * kAcc <= 64 ? 4 : 1), true>(plan, grid, smem, stream);
+    case 8: return launch_variant<WFMT, NV, (8 * kAcc <= 64 ? 8 : 1), true>(plan, grid, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }

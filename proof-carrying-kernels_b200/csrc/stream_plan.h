@@ -29,20 +29,8 @@ constexpr int kMaxBatch = 16;
 constexpr int kWeightsBf16 = 0;
 constexpr int kWeightsE4m3 = 1;
 
-// Rows per unit for a tree of 32*nv chains: every consumer warp gets one group of 32
-// chains (or nv/8 of them) for rows_per_warp rows of the unit, so a warp loads each
-// activation vector once per unit and uses it for all its rows.
-__host__ __device__ constexpr int unit_rows(int wfmt, int nv) {
-  return wfmt == kWeightsBf16 ? (nv == 1 ? 8 : nv == 2 ? 4 : nv <= 16 ? 2 : 1)
-                              : (nv == 1 ? 8 : nv <= 8 ? 4 : 2);
-}
-
-// Accumulators per batch column of one consumer warp in a row unit (see Share in
-// stream_kernel.cuh): rows it owns times chain groups it owns.
-__host__ __device__ constexpr int warp_accumulators(int wfmt, int nv) {
-  return nv >= kConsumerWarps ? unit_rows(wfmt, nv) * (nv / kConsumerWarps)
-                              : unit_rows(wfmt, nv) * nv / kConsumerWarps;
-}
+// Accumulators per batch column of a warp reducing a row: NV chains per lane.
+__host__ __device__ constexpr int warp_accumulators(int /*wfmt*/, int nv) { return nv; }
 
 struct JobPlan {
   // GEMV part (has_w): W (m, n); units of R rows.
@@ -91,11 +79,11 @@ struct JobPlan {
 struct Plan {
   JobPlan jobs[kMaxJobs];
   int32_t njobs;
-  int32_t stages;
-  int32_t stage_bytes;
+  int32_t stages;       // staged path: ring slots per warp
+  int32_t stage_bytes;  // staged path: bytes per slot
   int32_t x_bytes;
-  int32_t threads;    // tree parameter T (all W jobs share it)
-  int32_t sum_bytes;  // per-stage scratch for the cross-warp reduction
+  int32_t threads;      // tree parameter T (all W jobs share it)
+  int32_t sum_bytes;    // staged path: bytes per row piece (whole vector iterations)
 };
 
 // Host-side launch of one instantiation family (stream_bf16.cu, stream_e4m3.cu). nv is

