@@ -684,7 +684,6 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
   const int nvec = static_cast<int>(jb.n / V);
   const int vtotal = (nvec + T - 1) / T;
-  const int vpp = static_cast<int>(row_piece / (T * 16u));  // vector iterations per row piece
   const uint32_t seg_piece = slot_bytes / 512u * 512u;
 
   PieceWalk issue, take;
@@ -722,10 +721,13 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
     const bool last = take.piece + 1 == take.pieces;
     if (un.kind == kUnitRow) {
       // one piece per column group when the batch exceeds BG (the host keeps such rows whole)
+      // vector iterations in this piece (pieces of a multi-piece row are whole iterations)
+      const uint32_t off = static_cast<uint32_t>(take.piece) * take.size;
+      const uint32_t bytes = min(take.size, un.bytes - off);
+      const int v_lo = static_cast<int>(off / (T * 16u));
+      const int v_hi = min(static_cast<int>((off + bytes + T * 16u - 1) / (T * 16u)), vtotal);
       for (int g0 = 0; g0 < jb.batch; g0 += BG) {
         if (first) row.reset();
-        const int v_lo = take.piece * vpp;
-        const int v_hi = min(v_lo + vpp, vtotal);
         reduce_row_piece<WFMT, NV, BG, kFma>(row, piece, xs, xcol, g0, jb.batch, v_lo, v_hi, nvec, lane);
         if (last) {
 #pragma unroll
