@@ -523,13 +523,54 @@ struct RowState {
   }
 };
 
+// Eight bfloat16 weights w (one 16-byte vector) times eight bfloat16 activations x, added
+// to a chain in element order with the mixed-precision multiply-add of sm_100
+// (fma.rn.f32.bf16: the exact product plus the binary32 chain, rounded once). kFma: one
+// instruction per term — equal to product-then-sum because the product is exact.
+// Otherwise the product is rounded first (fma with -0 addend, which is RN(w*x) for every
+// input, signed zeros included) and added with its own rounding, as the reference does.
+template <bool kFma>
+__device__ __forceinline__ void chain8_bf16(float& acc, const uint4 w, const uint4 x) {
+  if constexpr (kFma) {
+    asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
+        "mov.b32 {w0, w1}, %1;\n\tmov.b32 {x0, x1}, %5;\n\t"
+        "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+        "mov.b32 {w0, w1}, %2;\n\tmov.b32 {x0, x1}, %6;\n\t"
+        "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+        "mov.b32 {w0, w1}, %3;\n\tmov.b32 {x0, x1}, %7;\n\t"
+        "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+        "mov.b32 {w0, w1}, %4;\n\tmov.b32 {x0, x1}, %8;\n\t"
+        "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w));
+  } else {
+    asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t.reg .f32 p;\n\t"
+        "mov.b32 {w0, w1}, %1;\n\tmov.b32 {x0, x1}, %5;\n\t"
+        "fma.rn.f32.bf16 p, w0, x0, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "fma.rn.f32.bf16 p, w1, x1, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "mov.b32 {w0, w1}, %2;\n\tmov.b32 {x0, x1}, %6;\n\t"
+        "fma.rn.f32.bf16 p, w0, x0, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "fma.rn.f32.bf16 p, w1, x1, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "mov.b32 {w0, w1}, %3;\n\tmov.b32 {x0, x1}, %7;\n\t"
+        "fma.rn.f32.bf16 p, w0, x0, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "fma.rn.f32.bf16 p, w1, x1, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "mov.b32 {w0, w1}, %4;\n\tmov.b32 {x0, x1}, %8;\n\t"
+        "fma.rn.f32.bf16 p, w0, x0, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "fma.rn.f32.bf16 p, w1, x1, %9;\n\tadd.rn.f32 %0, %0, p;\n\t}"
+        : "+f"(acc)
+        : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w),
+          "f"(-0.0f));
+  }
+}
+
 // The vector iterations [v_lo, v_hi) of a row against columns [g0, g0 + BG) of X. The piece
 // holds the row bytes from vector v_lo * T on; vector q of the row is at
-// piece + (q - v_lo * T) * 16. nvec = n / V (n % V == 0 on this path).
+// piece + (q - v_lo * T) * 16. nvec = n / V (n % V == 0 on this path). The shared-memory
+// loads of an iteration are issued together, before its arithmetic.
 template <int WFMT, int NV, int BG, bool kFma>
 __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uint32_t piece, uint32_t xs,
-                                          uint32_t xcol, int g0, int batch, int v_lo, int v_hi,
-                                          int nvec, int lane) {
+                                                 uint32_t xcol, int g0, int batch, int v_lo, int v_hi,
+                                                 int nvec, int lane) {
   constexpr int V = Format<WFMT>::kVec;
   constexpr int T = NV * kWarp;
   constexpr uint32_t kXV = V * 2;  // bytes of one activation vector
@@ -538,38 +579,49 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
   for (int b = 0; b < BG; ++b) xcol_addr[b] = xs + static_cast<uint32_t>(min(g0 + b, batch - 1)) * xcol;
   for (int v = v_lo; v < v_hi; ++v) {
     const uint32_t wbase = piece + static_cast<uint32_t>((v - v_lo) * T + lane) * 16u;
-    const int qbase = v * T + lane;
-    const bool partial = (v + 1) * T > nvec;
+    const uint32_t xoff = static_cast<uint32_t>(v * T + lane) * kXV;
+    if ((v + 1) * T > nvec) {  // the last, partial iteration: padding past n adds +0
+      const int qbase = v * T + lane;
 #pragma unroll
-    for (int g = 0; g < NV; ++g) {
-      const int q = qbase + g * kWarp;
-      if (partial && q >= nvec) {  // padding past n: +0 terms
+      for (int g = 0; g < NV; ++g) {
+        const bool in = qbase + g * kWarp < nvec;
+        const uint4 wv = in ? lds128(wbase + g * (kWarp * 16u)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int b = 0; b < BG; ++b) st.acc[b][g] = __fadd_rn(st.acc[b][g], 0.0f);
-        continue;
-      }
-      const uint4 wv = lds128(wbase + g * (kWarp * 16u));
-#pragma unroll
-      for (int b = 0; b < BG; ++b) {
-        const uint32_t xaddr = xcol_addr[b] + static_cast<uint32_t>(q) * kXV;
-        const uint4 xa = lds128(xaddr);
-        if constexpr (WFMT == kWeightsBf16) {
-          if constexpr (kFma) {
-            chain_pair<true>(st.acc[b][g], bf16_lo(wv.x), bf16_lo(xa.x));
-            chain_pair<true>(st.acc[b][g], bf16_hi(wv.x), bf16_hi(xa.x));
-            chain_pair<true>(st.acc[b][g], bf16_lo(wv.y), bf16_lo(xa.y));
-            chain_pair<true>(st.acc[b][g], bf16_hi(wv.y), bf16_hi(xa.y));
-            chain_pair<true>(st.acc[b][g], bf16_lo(wv.z), bf16_lo(xa.z));
-            chain_pair<true>(st.acc[b][g], bf16_hi(wv.z), bf16_hi(xa.z));
-            chain_pair<true>(st.acc[b][g], bf16_lo(wv.w), bf16_lo(xa.w));
-            chain_pair<true>(st.acc[b][g], bf16_hi(wv.w), bf16_hi(xa.w));
-          } else {
-            chain_bf16(st.acc[b][g], wv, xa);
+        for (int b = 0; b < BG; ++b) {
+          if (!in) {
+            st.acc[b][g] = __fadd_rn(st.acc[b][g], 0.0f);
+            continue;
           }
-        } else {
-          const uint4 xb = lds128(xaddr + 16);
-          chain_e4m3<kFma>(st.acc[b][g], wv, xa, xb);
+          const uint32_t xaddr = xcol_addr[b] + xoff + g * (kWarp * kXV);
+          if constexpr (WFMT == kWeightsBf16) {
+            chain8_bf16<kFma>(st.acc[b][g], wv, lds128(xaddr));
+          } else {
+            chain_e4m3<kFma>(st.acc[b][g], wv, lds128(xaddr), lds128(xaddr + 16));
+          }
         }
+      }
+      continue;
+    }
+    uint4 wv[NV];
+#pragma unroll
+    for (int g = 0; g < NV; ++g) wv[g] = lds128(wbase + g * (kWarp * 16u));
+#pragma unroll
+    for (int b = 0; b < BG; ++b) {
+      if constexpr (WFMT == kWeightsBf16) {
+        uint4 xv[NV];
+#pragma unroll
+        for (int g = 0; g < NV; ++g) xv[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV));
+#pragma unroll
+        for (int g = 0; g < NV; ++g) chain8_bf16<kFma>(st.acc[b][g], wv[g], xv[g]);
+      } else {
+        uint4 xa[NV], xb[NV];
+#pragma unroll
+        for (int g = 0; g < NV; ++g) {
+          xa[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV));
+          xb[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV) + 16);
+        }
+#pragma unroll
+        for (int g = 0; g < NV; ++g) chain_e4m3<kFma>(st.acc[b][g], wv[g], xa[g], xb[g]);
       }
     }
   }
