@@ -101,6 +101,7 @@ int validate_check(const pck_check_desc* d) {
 
 constexpr int64_t kPieceTarget = 8 * 1024;  // row piece size the staged path aims for
 constexpr int kMaxSlots = 4;                // ring slots per warp
+constexpr int64_t kSegmentTarget = 2048;    // columns per checksum-bank segment
 
 // Plans and launches the streaming kernel for `specs` (validated by the caller).
 int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
@@ -179,8 +180,12 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
       jb.block = d->block;
       jb.num_blocks = d->num_blocks;
       jb.checks = d->checks;
+      // Bank rows are cut into segments of about kSegmentTarget columns (at most the
+      // scratch's `segments`): the binary64 bound holds for any split, so the split is
+      // chosen for the kernel, not taken from the caller.
       jb.seg_alloc = d->segments;
-      int64_t len = (d->n + d->segments - 1) / d->segments;
+      const int64_t want = std::min<int64_t>(d->segments, (d->n + kSegmentTarget - 1) / kSegmentTarget);
+      int64_t len = (d->n + want - 1) / want;
       len = (len + 7) / 8 * 8;
       jb.seg_len = len;
       jb.segs = static_cast<int32_t>((d->n + len - 1) / len);

@@ -395,6 +395,22 @@ __device__ __forceinline__ void a_segment(const uint16_t* __restrict__ as,
 // every other unit's results were published (fence, then ticket). Reads y from memory.
 // Decision rule of the reference checker (src/pck/cuda/csrc/checker_kernel.cu:146-184).
 
+// Sum of the segment partials p[0..count) in index order (rounded up when kUp), computed
+// by lane 0 from values the lanes load together. Every lane returns it.
+template <bool kUp>
+__device__ __forceinline__ double ordered_sum(const double* p, int count, int lane) {
+  double total = 0.0;
+  for (int s0 = 0; s0 < count; s0 += kWarp) {
+    const double mine = s0 + lane < count ? __ldcg(p + s0 + lane) : 0.0;
+    const int here = min(kWarp, count - s0);
+    for (int i = 0; i < here; ++i) {
+      const double v = __shfl_sync(kFullMask, mine, i);
+      total = kUp ? __dadd_ru(total, v) : __dadd_rn(total, v);
+    }
+  }
+  return total;
+}
+
 static __device__ __noinline__ void merge_block(const JobPlan& jb, int64_t beta, int lane) {
   __threadfence();
   const int blk = jb.block;
@@ -413,11 +429,8 @@ static __device__ __noinline__ void merge_block(const JobPlan& jb, int64_t beta,
     }
     yabs = warp_sum_ru(yabs);
     bad = __any_sync(kFullMask, bad);
-    double s_total = 0.0;
-    if (lane == 0) {
-      const double* ps = jb.partial_s + (col * nb + beta) * jb.seg_alloc;
-      for (int s = 0; s < jb.segs; ++s) s_total = __dadd_ru(s_total, __ldcg(ps + s));
-    }
+    const double s_total =
+        ordered_sum<true>(jb.partial_s + (col * nb + beta) * jb.seg_alloc, jb.segs, lane);
     for (int k = 0; k < jb.checks; ++k) {
       const int8_t* rk = jb.r + (static_cast<int64_t>(k) * nb + beta) * blk;
       double ry = 0.0;
@@ -426,11 +439,10 @@ static __device__ __noinline__ void merge_block(const JobPlan& jb, int64_t beta,
         ry = __dadd_rn(ry, __ldg(rk + i) > 0 ? v : -v);
       }
       ry = warp_sum_rn(ry);
+      const double cx = ordered_sum<false>(
+          jb.partial_cx + ((static_cast<int64_t>(col) * jb.checks + k) * nb + beta) * jb.seg_alloc, jb.segs,
+          lane);
       if (lane == 0) {
-        const double* pc =
-            jb.partial_cx + ((static_cast<int64_t>(col) * jb.checks + k) * nb + beta) * jb.seg_alloc;
-        double cx = 0.0;
-        for (int s = 0; s < jb.segs; ++s) cx = __dadd_rn(cx, __ldcg(pc + s));
         const double rho = __dsub_rn(cx, ry);
         const double cabs = __dmul_ru(kOnePlusU32, s_total);
         const double eps = __dmul_ru(jb.geps, __dadd_ru(cabs, yabs));
@@ -642,7 +654,9 @@ __device__ __forceinline__ void segment_piece(double* acc, uint32_t piece, uint3
     } else {
       cv = lds128(piece + off * 4);
     }
-    for (int b = 0; b < batch; ++b) {
+#pragma unroll
+    for (int b = 0; b < kMaxBatch; ++b) {
+      if (b >= batch) break;
       const uint2 xv = lds64(xs + static_cast<uint32_t>(b) * xcol + static_cast<uint32_t>(col0 + e) * 2);
       double a = acc[b];
       if constexpr (kAbs) {
@@ -757,7 +771,7 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   for (int s = 0; s < slots && issue.pieces > 0; ++s) issue_one();
 
   RowState<WFMT, NV, BG> row;
-  double dacc[kMaxBatch];
+  double dacc[kMaxBatch];  // indexed only by unrolled loops: registers
   int64_t cur_beta = -1;
   uint32_t pending = 0;
   bool ok = true;
@@ -791,7 +805,8 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
       }
     } else {
       if (first) {
-        for (int b = 0; b < jb.batch; ++b) dacc[b] = 0.0;
+#pragma unroll
+        for (int b = 0; b < kMaxBatch; ++b) dacc[b] = 0.0;
       }
       const int esz = un.kind == kUnitC ? 4 : 2;
       const int e_lo = static_cast<int>(static_cast<int64_t>(take.piece) * take.size / esz);
@@ -803,7 +818,9 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
       }
       if (last) {
         const int64_t nb = jb.num_blocks;
-        for (int b = 0; b < jb.batch; ++b) {
+#pragma unroll
+        for (int b = 0; b < kMaxBatch; ++b) {
+          if (b >= jb.batch) break;
           if (un.kind == kUnitC) {
             const double t = warp_sum_rn(dacc[b]);
             if (lane == 0) {
