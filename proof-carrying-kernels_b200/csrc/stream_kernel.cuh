@@ -64,6 +64,41 @@ __host__ __device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) {
   return (a + b - 1) / b;
 }
 
+// Unit o of row block beta of a checked job.
+__device__ __forceinline__ Unit decode_checked(const JobPlan& jb, int64_t beta, int64_t o) {
+  Unit x{};
+  x.beta = beta;
+  const int64_t ru = jb.has_w ? jb.row_units : 0;
+  if (o < ru) {
+    x.kind = kUnitRow;
+    const int64_t first = o * jb.rows;
+    x.row = beta * jb.block + first;
+    x.rows = static_cast<int>(min(static_cast<int64_t>(jb.rows), jb.block - first));
+    x.src = static_cast<const uint8_t*>(jb.W) + x.row * jb.row_bytes;
+    x.bytes = static_cast<uint32_t>(x.rows * jb.row_bytes);
+    return x;
+  }
+  const int oc = static_cast<int>(o - ru);
+  const int cs = jb.checks * jb.segs;
+  if (oc < cs) {
+    x.kind = kUnitC;
+    x.k = oc / jb.segs;
+    x.s = oc - x.k * jb.segs;
+    x.col0 = x.s * jb.seg_len;
+    x.len = min(jb.seg_len, jb.n - x.col0);
+    x.src = jb.c + (static_cast<int64_t>(x.k) * jb.num_blocks + beta) * jb.n + x.col0;
+    x.bytes = static_cast<uint32_t>(x.len * 4);
+    return x;
+  }
+  x.kind = kUnitA;
+  x.s = oc - cs;
+  x.col0 = x.s * jb.seg_len;
+  x.len = min(jb.seg_len, jb.n - x.col0);
+  x.src = jb.a + beta * jb.n + x.col0;
+  x.bytes = static_cast<uint32_t>(x.len * 2);
+  return x;
+}
+
 __device__ __forceinline__ Unit decode_unit(const JobPlan& jb, int64_t u) {
   Unit x{};
   if (!jb.has_check) {
@@ -715,18 +750,19 @@ __device__ __forceinline__ bool fma_is_exact(const JobPlan& jb, unsigned x_lo, u
 // multiple of 128 elements and the lanes add the elements in one fixed order).
 struct PieceWalk {
   int64_t unit;   // CTA-local unit index
+  int64_t beta;   // checked jobs: row block of `unit` ...
+  int64_t o;      // ... and its index within the block
   int piece;
-  int pieces;     // pieces of `unit`
+  int pieces;     // pieces of `unit` (0: the walk is over)
   uint32_t size;  // piece size of `unit`
   Unit un;
 };
 
-__device__ __forceinline__ void walk_to(PieceWalk& w, const JobPlan& jb, int64_t u0, int64_t local,
-                                        int64_t count, uint32_t row_piece, uint32_t seg_piece) {
-  w.unit = local;
+__device__ __forceinline__ void walk_load(PieceWalk& w, const JobPlan& jb, int64_t u0, int64_t count,
+                                          uint32_t row_piece, uint32_t seg_piece) {
   w.piece = 0;
-  if (local < count) {
-    w.un = decode_unit(jb, u0 + local);
+  if (w.unit < count) {
+    w.un = jb.has_check ? decode_checked(jb, w.beta, w.o) : decode_unit(jb, u0 + w.unit);
     w.size = w.un.kind == kUnitRow ? row_piece : seg_piece;
     w.pieces = static_cast<int>((w.un.bytes + w.size - 1) / w.size);
   } else {
@@ -734,9 +770,30 @@ __device__ __forceinline__ void walk_to(PieceWalk& w, const JobPlan& jb, int64_t
   }
 }
 
+// Start at CTA-local unit `local` (one division, at the start only).
+__device__ __forceinline__ void walk_to(PieceWalk& w, const JobPlan& jb, int64_t u0, int64_t local,
+                                        int64_t count, uint32_t row_piece, uint32_t seg_piece) {
+  w.unit = local;
+  if (jb.has_check) {
+    w.beta = (u0 + local) / jb.period_units;
+    w.o = u0 + local - w.beta * jb.period_units;
+  }
+  walk_load(w, jb, u0, count, row_piece, seg_piece);
+}
+
+// Next piece; after the last piece of a unit, the unit kConsumerWarps further on.
 __device__ __forceinline__ void walk_next(PieceWalk& w, const JobPlan& jb, int64_t u0, int64_t count,
                                           uint32_t row_piece, uint32_t seg_piece) {
-  if (++w.piece >= w.pieces) walk_to(w, jb, u0, w.unit + kConsumerWarps, count, row_piece, seg_piece);
+  if (++w.piece < w.pieces) return;
+  w.unit += kConsumerWarps;
+  if (jb.has_check) {
+    w.o += kConsumerWarps;
+    while (w.o >= jb.period_units) {
+      w.o -= jb.period_units;
+      ++w.beta;
+    }
+  }
+  walk_load(w, jb, u0, count, row_piece, seg_piece);
 }
 
 template <int WFMT, int NV, int BG, bool kFma>
