@@ -215,7 +215,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
       jb.total_bytes = jb.m * jb.row_bytes;
     }
     if (s.has_w) max_row_bytes = std::max<int64_t>(max_row_bytes, jb.row_bytes);
-    x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 4);  // binary32
+    x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 2);
     plan.jobs[nj++] = jb;
     bytes.push_back(jb.total_bytes);
   }

@@ -570,83 +570,105 @@ struct RowState {
   }
 };
 
-// Eight bfloat16 weights (one 16-byte vector) times eight binary32 activations (the
-// bfloat16 values, widened exactly), added to a chain in element order. kFma: one FMA per
-// term, equal to product-then-sum because the product is exact; otherwise the product is
-// rounded first and then added, as the reference does.
+// Eight bfloat16 weights w (one 16-byte vector) times eight bfloat16 activations x, added
+// to a chain in element order with the mixed-precision multiply-add of sm_100
+// (fma.rn.f32.bf16: the exact product plus the binary32 chain, rounded once). kFma: one
+// instruction per term — equal to product-then-sum because the product is exact.
+// Otherwise the product is rounded first (fma with -0 addend, which is RN(w*x) for every
+// input, signed zeros included) and added with its own rounding, as the reference does.
 template <bool kFma>
-__device__ __forceinline__ void chain8_bf16(float& acc, const uint4 w, const float4 xa, const float4 xb) {
-  chain_pair<kFma>(acc, bf16_lo(w.x), xa.x);
-  chain_pair<kFma>(acc, bf16_hi(w.x), xa.y);
-  chain_pair<kFma>(acc, bf16_lo(w.y), xa.z);
-  chain_pair<kFma>(acc, bf16_hi(w.y), xa.w);
-  chain_pair<kFma>(acc, bf16_lo(w.z), xb.x);
-  chain_pair<kFma>(acc, bf16_hi(w.z), xb.y);
-  chain_pair<kFma>(acc, bf16_lo(w.w), xb.z);
-  chain_pair<kFma>(acc, bf16_hi(w.w), xb.w);
-}
-
-// Sixteen E4M3 weights times sixteen binary32 activations.
-template <bool kFma>
-__device__ __forceinline__ void chain16_e4m3(float& acc, const uint4 w, const float4 x0, const float4 x1,
-                                             const float4 x2, const float4 x3) {
-  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-  const float4 xs[4] = {x0, x1, x2, x3};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 lo = e4m3x2_to_float2(static_cast<uint16_t>(words[i] & 0xffffu));
-    const float2 hi = e4m3x2_to_float2(static_cast<uint16_t>(words[i] >> 16));
-    chain_pair<kFma>(acc, lo.x, xs[i].x);
-    chain_pair<kFma>(acc, lo.y, xs[i].y);
-    chain_pair<kFma>(acc, hi.x, xs[i].z);
-    chain_pair<kFma>(acc, hi.y, xs[i].w);
+__device__ __forceinline__ void chain8_bf16(float& acc, const uint4 w, const uint4 x) {
+  if constexpr (kFma) {
+    asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
+        "mov.b32 {w0, w1}, %1;\n\tmov.b32 {x0, x1}, %5;\n\t"
+        "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+        "mov.b32 {w0, w1}, %2;\n\tmov.b32 {x0, x1}, %6;\n\t"
+        "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+        "mov.b32 {w0, w1}, %3;\n\tmov.b32 {x0, x1}, %7;\n\t"
+        "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+        "mov.b32 {w0, w1}, %4;\n\tmov.b32 {x0, x1}, %8;\n\t"
+        "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w));
+  } else {
+    asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t.reg .f32 p;\n\t"
+        "mov.b32 {w0, w1}, %1;\n\tmov.b32 {x0, x1}, %5;\n\t"
+        "fma.rn.f32.bf16 p, w0, x0, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "fma.rn.f32.bf16 p, w1, x1, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "mov.b32 {w0, w1}, %2;\n\tmov.b32 {x0, x1}, %6;\n\t"
+        "fma.rn.f32.bf16 p, w0, x0, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "fma.rn.f32.bf16 p, w1, x1, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "mov.b32 {w0, w1}, %3;\n\tmov.b32 {x0, x1}, %7;\n\t"
+        "fma.rn.f32.bf16 p, w0, x0, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "fma.rn.f32.bf16 p, w1, x1, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "mov.b32 {w0, w1}, %4;\n\tmov.b32 {x0, x1}, %8;\n\t"
+        "fma.rn.f32.bf16 p, w0, x0, %9;\n\tadd.rn.f32 %0, %0, p;\n\t"
+        "fma.rn.f32.bf16 p, w1, x1, %9;\n\tadd.rn.f32 %0, %0, p;\n\t}"
+        : "+f"(acc)
+        : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w),
+          "f"(-0.0f));
   }
 }
 
-__device__ __forceinline__ float4 lds128f(uint32_t addr) {
-  const uint4 v = lds128(addr);
-  return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
-}
-
-// The vector iterations [v_lo, v_hi) of a row against columns [g0, g0 + BG) of X (binary32
-// in shared memory, xcol bytes per column). The piece holds the row bytes from vector
-// v_lo * T on; vector q of the row is at piece + (q - v_lo * T) * 16. nvec = n / V (n % V
-// == 0 on this path). The shared-memory loads of an iteration are issued together.
+// The vector iterations [v_lo, v_hi) of a row against columns [g0, g0 + BG) of X. The piece
+// holds the row bytes from vector v_lo * T on; vector q of the row is at
+// piece + (q - v_lo * T) * 16. nvec = n / V (n % V == 0 on this path). The shared-memory
+// loads of an iteration are issued together, before its arithmetic.
 template <int WFMT, int NV, int BG, bool kFma>
 __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uint32_t piece, uint32_t xs,
                                                  uint32_t xcol, int g0, int batch, int v_lo, int v_hi,
                                                  int nvec, int lane) {
   constexpr int V = Format<WFMT>::kVec;
   constexpr int T = NV * kWarp;
-  constexpr uint32_t kXV = V * 4;  // bytes of one activation vector (binary32)
+  constexpr uint32_t kXV = V * 2;  // bytes of one activation vector
   uint32_t xcol_addr[BG];
 #pragma unroll
   for (int b = 0; b < BG; ++b) xcol_addr[b] = xs + static_cast<uint32_t>(min(g0 + b, batch - 1)) * xcol;
   for (int v = v_lo; v < v_hi; ++v) {
     const uint32_t wbase = piece + static_cast<uint32_t>((v - v_lo) * T + lane) * 16u;
     const uint32_t xoff = static_cast<uint32_t>(v * T + lane) * kXV;
-    const bool partial = (v + 1) * T > nvec;  // the last iteration: padding past n adds +0
-    const int qbase = v * T + lane;
-    uint4 wv[NV];
-#pragma unroll
-    for (int g = 0; g < NV; ++g) {
-      wv[g] = (!partial || qbase + g * kWarp < nvec) ? lds128(wbase + g * (kWarp * 16u)) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int b = 0; b < BG; ++b) {
+    if ((v + 1) * T > nvec) {  // the last, partial iteration: padding past n adds +0
+      const int qbase = v * T + lane;
 #pragma unroll
       for (int g = 0; g < NV; ++g) {
-        if (partial && qbase + g * kWarp >= nvec) {
-          st.acc[b][g] = __fadd_rn(st.acc[b][g], 0.0f);
-          continue;
+        const bool in = qbase + g * kWarp < nvec;
+        const uint4 wv = in ? lds128(wbase + g * (kWarp * 16u)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int b = 0; b < BG; ++b) {
+          if (!in) {
+            st.acc[b][g] = __fadd_rn(st.acc[b][g], 0.0f);
+            continue;
+          }
+          const uint32_t xaddr = xcol_addr[b] + xoff + g * (kWarp * kXV);
+          if constexpr (WFMT == kWeightsBf16) {
+            chain8_bf16<kFma>(st.acc[b][g], wv, lds128(xaddr));
+          } else {
+            chain_e4m3<kFma>(st.acc[b][g], wv, lds128(xaddr), lds128(xaddr + 16));
+          }
         }
-        const uint32_t xaddr = xcol_addr[b] + xoff + g * (kWarp * kXV);
-        if constexpr (WFMT == kWeightsBf16) {
-          chain8_bf16<kFma>(st.acc[b][g], wv[g], lds128f(xaddr), lds128f(xaddr + 16));
-        } else {
-          chain16_e4m3<kFma>(st.acc[b][g], wv[g], lds128f(xaddr), lds128f(xaddr + 16), lds128f(xaddr + 32),
-                             lds128f(xaddr + 48));
+      }
+      continue;
+    }
+    uint4 wv[NV];
+#pragma unroll
+    for (int g = 0; g < NV; ++g) wv[g] = lds128(wbase + g * (kWarp * 16u));
+#pragma unroll
+    for (int b = 0; b < BG; ++b) {
+      if constexpr (WFMT == kWeightsBf16) {
+        uint4 xv[NV];
+#pragma unroll
+        for (int g = 0; g < NV; ++g) xv[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV));
+#pragma unroll
+        for (int g = 0; g < NV; ++g) chain8_bf16<kFma>(st.acc[b][g], wv[g], xv[g]);
+      } else {
+        uint4 xa[NV], xb[NV];
+#pragma unroll
+        for (int g = 0; g < NV; ++g) {
+          xa[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV));
+          xb[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV) + 16);
         }
+#pragma unroll
+        for (int g = 0; g < NV; ++g) chain_e4m3<kFma>(st.acc[b][g], wv[g], xa[g], xb[g]);
       }
     }
   }
@@ -670,53 +692,34 @@ __device__ __forceinline__ void segment_piece(double* acc, uint32_t piece, uint3
 #pragma unroll
     for (int b = 0; b < kMaxBatch; ++b) {
       if (b >= batch) break;
-      const float4 xv = lds128f(xs + static_cast<uint32_t>(b) * xcol + static_cast<uint32_t>(col0 + e) * 4);
+      const uint2 xv = lds64(xs + static_cast<uint32_t>(b) * xcol + static_cast<uint32_t>(col0 + e) * 2);
       double a = acc[b];
       if constexpr (kAbs) {
-        a = __fma_ru(static_cast<double>(bf16_lo(av.x)), fabs(static_cast<double>(xv.x)), a);
-        a = __fma_ru(static_cast<double>(bf16_hi(av.x)), fabs(static_cast<double>(xv.y)), a);
-        a = __fma_ru(static_cast<double>(bf16_lo(av.y)), fabs(static_cast<double>(xv.z)), a);
-        a = __fma_ru(static_cast<double>(bf16_hi(av.y)), fabs(static_cast<double>(xv.w)), a);
+        a = __fma_ru(static_cast<double>(bf16_lo(av.x)), fabs(static_cast<double>(bf16_lo(xv.x))), a);
+        a = __fma_ru(static_cast<double>(bf16_hi(av.x)), fabs(static_cast<double>(bf16_hi(xv.x))), a);
+        a = __fma_ru(static_cast<double>(bf16_lo(av.y)), fabs(static_cast<double>(bf16_lo(xv.y))), a);
+        a = __fma_ru(static_cast<double>(bf16_hi(av.y)), fabs(static_cast<double>(bf16_hi(xv.y))), a);
       } else {
-        a = __fma_rn(static_cast<double>(__uint_as_float(cv.x)), static_cast<double>(xv.x), a);
-        a = __fma_rn(static_cast<double>(__uint_as_float(cv.y)), static_cast<double>(xv.y), a);
-        a = __fma_rn(static_cast<double>(__uint_as_float(cv.z)), static_cast<double>(xv.z), a);
-        a = __fma_rn(static_cast<double>(__uint_as_float(cv.w)), static_cast<double>(xv.w), a);
+        a = __fma_rn(static_cast<double>(__uint_as_float(cv.x)), static_cast<double>(bf16_lo(xv.x)), a);
+        a = __fma_rn(static_cast<double>(__uint_as_float(cv.y)), static_cast<double>(bf16_hi(xv.x)), a);
+        a = __fma_rn(static_cast<double>(__uint_as_float(cv.z)), static_cast<double>(bf16_lo(xv.y)), a);
+        a = __fma_rn(static_cast<double>(__uint_as_float(cv.w)), static_cast<double>(bf16_hi(xv.y)), a);
       }
       acc[b] = a;
     }
   }
 }
 
-// Widens the bfloat16 activations, landed at xs + 2 * count bytes, to binary32 at xs (in
-// place, increasing index, one chunk at a time: a chunk's binary32 values overwrite only
-// bfloat16 values of this or earlier chunks), and records the exponent fields (bits 7-14)
-// of the activations: the smallest over nonzero values (subnormals count as 1) in lo[0],
-// the largest in hi[0]. All threads of the CTA take part.
-__device__ __forceinline__ void widen_activations(uint8_t* xs, int count, unsigned* lo, unsigned* hi) {
-  constexpr int kPer = 8;
-  const int tid = static_cast<int>(threadIdx.x);
-  const uint16_t* src = reinterpret_cast<const uint16_t*>(xs + 2 * static_cast<int64_t>(count));
-  float* dst = reinterpret_cast<float*>(xs);
+// Exponent fields (bfloat16 bits 7-14) of the activations: smallest over nonzero values
+// (subnormals count as 1) and largest over all.
+__device__ __forceinline__ void x_exponents(const uint16_t* X, int64_t count, int first, int step,
+                                            unsigned* lo, unsigned* hi) {
   unsigned mn = 1000, mx = 0;
-  for (int c0 = 0; c0 < count; c0 += kPlainThreads * kPer) {
-    uint16_t v[kPer];
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int j = c0 + i * kPlainThreads + tid;
-      v[i] = j < count ? src[j] : 0;
-      const unsigned mag = v[i] & 0x7fffu;
-      const unsigned e = mag >> 7;
-      mx = max(mx, e);
-      if (mag) mn = min(mn, max(e, 1u));
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int j = c0 + i * kPlainThreads + tid;
-      if (j < count) dst[j] = bf16_bits_to_float(v[i]);
-    }
-    __syncthreads();
+  for (int64_t j = first; j < count; j += step) {
+    const unsigned mag = X[j] & 0x7fffu;
+    const unsigned e = mag >> 7;
+    mx = max(mx, e);
+    if (mag) mn = min(mn, max(e, 1u));
   }
   atomicMin(lo, mn);
   atomicMax(hi, mx);
@@ -801,7 +804,7 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   constexpr int T = NV * kWarp;
   const uint64_t once = policy_evict_first();
   const uint32_t ring_addr = smem_addr(ring);
-  const uint32_t xcol = static_cast<uint32_t>(jb.n * 4);  // binary32 activations
+  const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
   const int nvec = static_cast<int>(jb.n / V);
   const int vtotal = (nvec + T - 1) / T;
   const uint32_t seg_piece = slot_bytes / 512u * 512u;
@@ -942,16 +945,18 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
       fence_barrier_init();
     }
     __syncthreads();
-    const int xcount = jb.batch * static_cast<int>(jb.n);
-    if (threadIdx.x == 0) {  // bfloat16 activations land in the upper half of their area
-      const uint32_t xbytes = static_cast<uint32_t>(xcount) * 2u;
+    if (threadIdx.x == 0) {
+      const uint32_t xbytes = static_cast<uint32_t>(static_cast<int64_t>(jb.batch) * jb.n * 2);
       mbar_arrive_expect_tx(xbar, xbytes);
-      bulk_load(xs + xbytes, jb.X, xbytes, xbar, policy_evict_last());
+      bulk_load(xs, jb.X, xbytes, xbar, policy_evict_last());
     }
-    const bool have_x = __syncthreads_and(mbar_wait(xbar, 0));
-    if (!have_x) return;
-    widen_activations(xs, xcount, xexp, xexp + 1);
+    const bool have_x = mbar_wait(xbar, 0);
+    if (have_x && jb.has_w) {
+      x_exponents(reinterpret_cast<const uint16_t*>(xs), static_cast<int64_t>(jb.batch) * jb.n,
+                  static_cast<int>(threadIdx.x), kPlainThreads, xexp, xexp + 1);
+    }
     __syncthreads();
+    if (!have_x) return;
     const bool fma = jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]);
     uint8_t* ring = rings + static_cast<int64_t>(warp) * slots * slot_bytes;
     uint64_t* full = bars + warp * slots;
