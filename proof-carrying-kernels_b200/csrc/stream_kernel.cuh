@@ -610,6 +610,26 @@ __device__ __forceinline__ void chain8_bf16(float& acc, const uint4 w, const uin
   }
 }
 
+// One bfloat16 x bfloat16 term, element `hi` (0 = low half) of the words w and x.
+template <bool kFma, int kHi>
+__device__ __forceinline__ void term_bf16(float& acc, uint32_t w, uint32_t x) {
+  if constexpr (kFma) {
+    if constexpr (kHi) {
+      asm("{\n\t.reg .b16 a, b, c, d;\n\tmov.b32 {a, b}, %1;\n\tmov.b32 {c, d}, %2;\n\t"
+          "fma.rn.f32.bf16 %0, b, d, %0;\n\t}" : "+f"(acc) : "r"(w), "r"(x));
+    } else {
+      asm("{\n\t.reg .b16 a, b, c, d;\n\tmov.b32 {a, b}, %1;\n\tmov.b32 {c, d}, %2;\n\t"
+          "fma.rn.f32.bf16 %0, a, c, %0;\n\t}" : "+f"(acc) : "r"(w), "r"(x));
+    }
+  } else {
+    acc = __fadd_rn(acc, __fmul_rn(kHi ? bf16_hi(w) : bf16_lo(w), kHi ? bf16_hi(x) : bf16_lo(x)));
+  }
+}
+
+__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
 // The vector iterations [v_lo, v_hi) of a row against columns [g0, g0 + BG) of X. The piece
 // holds the row bytes from vector v_lo * T on; vector q of the row is at
 // piece + (q - v_lo * T) * 16. nvec = n / V (n % V == 0 on this path). The shared-memory
@@ -658,8 +678,14 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
         uint4 xv[NV];
 #pragma unroll
         for (int g = 0; g < NV; ++g) xv[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV));
+        // element by element across the NV independent chains (each chain keeps its order)
 #pragma unroll
-        for (int g = 0; g < NV; ++g) chain8_bf16<kFma>(st.acc[b][g], wv[g], xv[g]);
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int g = 0; g < NV; ++g) term_bf16<kFma, 0>(st.acc[b][g], word(wv[g], i), word(xv[g], i));
+#pragma unroll
+          for (int g = 0; g < NV; ++g) term_bf16<kFma, 1>(st.acc[b][g], word(wv[g], i), word(xv[g], i));
+        }
       } else {
         uint4 xa[NV], xb[NV];
 #pragma unroll
