@@ -99,7 +99,7 @@ int validate_check(const pck_check_desc* d) {
   return PCK_OK;
 }
 
-constexpr int64_t kPieceTarget = 8 * 1024;  // row piece size the staged path aims for
+constexpr int64_t kPieceTarget = 4 * 1024;  // row piece size the staged path aims for
 constexpr int kMaxSlots = 4;                // ring slots per warp
 constexpr int64_t kSegmentTarget = 2048;    // columns per checksum-bank segment
 
@@ -144,6 +144,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
     if (s.check) {
       const pck_check_desc* d = s.check;
       if (!aligned16(d->c) || !aligned16(d->a) || !aligned16(d->x) || d->n % 8 != 0) tma = false;
+      if (d->batch > pck::kSegBatch) tma = false;
     }
   }
   if (live.empty()) return ok();

@@ -669,32 +669,36 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
       }
       continue;
     }
-    uint4 wv[NV];
+    // chain groups four at a time: their loads together, then their terms interleaved
+    constexpr int kStep = NV < 4 ? NV : 4;
 #pragma unroll
-    for (int g = 0; g < NV; ++g) wv[g] = lds128(wbase + g * (kWarp * 16u));
+    for (int g0w = 0; g0w < NV; g0w += kStep) {
+      uint4 wv[kStep];
 #pragma unroll
-    for (int b = 0; b < BG; ++b) {
-      if constexpr (WFMT == kWeightsBf16) {
-        uint4 xv[NV];
+      for (int g = 0; g < kStep; ++g) wv[g] = lds128(wbase + (g0w + g) * (kWarp * 16u));
 #pragma unroll
-        for (int g = 0; g < NV; ++g) xv[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV));
-        // element by element across the NV independent chains (each chain keeps its order)
+      for (int b = 0; b < BG; ++b) {
+        if constexpr (WFMT == kWeightsBf16) {
+          uint4 xv[kStep];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+          for (int g = 0; g < kStep; ++g) xv[g] = lds128(xcol_addr[b] + xoff + (g0w + g) * (kWarp * kXV));
 #pragma unroll
-          for (int g = 0; g < NV; ++g) term_bf16<kFma, 0>(st.acc[b][g], word(wv[g], i), word(xv[g], i));
+          for (int i = 0; i < 4; ++i) {
 #pragma unroll
-          for (int g = 0; g < NV; ++g) term_bf16<kFma, 1>(st.acc[b][g], word(wv[g], i), word(xv[g], i));
+            for (int g = 0; g < kStep; ++g) term_bf16<kFma, 0>(st.acc[b][g0w + g], word(wv[g], i), word(xv[g], i));
+#pragma unroll
+            for (int g = 0; g < kStep; ++g) term_bf16<kFma, 1>(st.acc[b][g0w + g], word(wv[g], i), word(xv[g], i));
+          }
+        } else {
+          uint4 xa[kStep], xb[kStep];
+#pragma unroll
+          for (int g = 0; g < kStep; ++g) {
+            xa[g] = lds128(xcol_addr[b] + xoff + (g0w + g) * (kWarp * kXV));
+            xb[g] = lds128(xcol_addr[b] + xoff + (g0w + g) * (kWarp * kXV) + 16);
+          }
+#pragma unroll
+          for (int g = 0; g < kStep; ++g) chain_e4m3<kFma>(st.acc[b][g0w + g], wv[g], xa[g], xb[g]);
         }
-      } else {
-        uint4 xa[NV], xb[NV];
-#pragma unroll
-        for (int g = 0; g < NV; ++g) {
-          xa[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV));
-          xb[g] = lds128(xcol_addr[b] + xoff + g * (kWarp * kXV) + 16);
-        }
-#pragma unroll
-        for (int g = 0; g < NV; ++g) chain_e4m3<kFma>(st.acc[b][g], wv[g], xa[g], xb[g]);
       }
     }
   }
@@ -716,7 +720,7 @@ __device__ __forceinline__ void segment_piece(double* acc, uint32_t piece, uint3
       cv = lds128(piece + off * 4);
     }
 #pragma unroll
-    for (int b = 0; b < kMaxBatch; ++b) {
+    for (int b = 0; b < kSegBatch; ++b) {
       if (b >= batch) break;
       const uint2 xv = lds64(xs + static_cast<uint32_t>(b) * xcol + static_cast<uint32_t>(col0 + e) * 2);
       double a = acc[b];
@@ -781,16 +785,20 @@ struct PieceWalk {
   int piece;
   int pieces;     // pieces of `unit` (0: the walk is over)
   uint32_t size;  // piece size of `unit`
-  Unit un;
 };
+
+// The unit a walk stands on (decoded again where needed: cheaper than keeping it).
+__device__ __forceinline__ Unit walk_unit(const PieceWalk& w, const JobPlan& jb, int64_t u0) {
+  return jb.has_check ? decode_checked(jb, w.beta, w.o) : decode_unit(jb, u0 + w.unit);
+}
 
 __device__ __forceinline__ void walk_load(PieceWalk& w, const JobPlan& jb, int64_t u0, int64_t count,
                                           uint32_t row_piece, uint32_t seg_piece) {
   w.piece = 0;
   if (w.unit < count) {
-    w.un = jb.has_check ? decode_checked(jb, w.beta, w.o) : decode_unit(jb, u0 + w.unit);
-    w.size = w.un.kind == kUnitRow ? row_piece : seg_piece;
-    w.pieces = static_cast<int>((w.un.bytes + w.size - 1) / w.size);
+    const Unit un = walk_unit(w, jb, u0);
+    w.size = un.kind == kUnitRow ? row_piece : seg_piece;
+    w.pieces = static_cast<int>((un.bytes + w.size - 1) / w.size);
   } else {
     w.pieces = 0;
   }
@@ -842,10 +850,11 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   auto issue_one = [&]() {
     const int slot = static_cast<int>(issued % slots);
     if (lane == 0) {
+      const Unit iu = walk_unit(issue, jb, u0);
       const uint32_t off = static_cast<uint32_t>(issue.piece) * issue.size;
-      const uint32_t bytes = min(issue.size, issue.un.bytes - off);
+      const uint32_t bytes = min(issue.size, iu.bytes - off);
       mbar_arrive_expect_tx(full + slot, bytes);
-      bulk_load(ring + static_cast<int64_t>(slot) * slot_bytes, static_cast<const uint8_t*>(issue.un.src) + off,
+      bulk_load(ring + static_cast<int64_t>(slot) * slot_bytes, static_cast<const uint8_t*>(iu.src) + off,
                 bytes, full + slot, once);
     }
     ++issued;
@@ -854,7 +863,7 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   for (int s = 0; s < slots && issue.pieces > 0; ++s) issue_one();
 
   RowState<WFMT, NV, BG> row;
-  double dacc[kMaxBatch];  // indexed only by unrolled loops: registers
+  double dacc[kSegBatch];  // indexed only by unrolled loops: registers
   int64_t cur_beta = -1;
   uint32_t pending = 0;
   bool ok = true;
@@ -865,7 +874,7 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
       break;
     }
     const uint32_t piece = ring_addr + static_cast<uint32_t>(slot) * slot_bytes;
-    const Unit& un = take.un;
+    const Unit un = walk_unit(take, jb, u0);
     const bool first = take.piece == 0;
     const bool last = take.piece + 1 == take.pieces;
     if (un.kind == kUnitRow) {
@@ -889,7 +898,7 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
     } else {
       if (first) {
 #pragma unroll
-        for (int b = 0; b < kMaxBatch; ++b) dacc[b] = 0.0;
+        for (int b = 0; b < kSegBatch; ++b) dacc[b] = 0.0;
       }
       const int esz = un.kind == kUnitC ? 4 : 2;
       const int e_lo = static_cast<int>(static_cast<int64_t>(take.piece) * take.size / esz);
@@ -902,7 +911,7 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
       if (last) {
         const int64_t nb = jb.num_blocks;
 #pragma unroll
-        for (int b = 0; b < kMaxBatch; ++b) {
+        for (int b = 0; b < kSegBatch; ++b) {
           if (b >= jb.batch) break;
           if (un.kind == kUnitC) {
             const double t = warp_sum_rn(dacc[b]);

@@ -20,12 +20,13 @@
 namespace pck {
 
 constexpr int kMaxJobs = 16;
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 16;
 constexpr int kTmaThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kPlainThreads = kConsumerWarps * 32;
 constexpr int kMaxStages = 32;
 constexpr int kSmemCap = 232448;  // 227 KB: the opt-in dynamic shared memory per CTA
 constexpr int kMaxBatch = 16;
+constexpr int kSegBatch = 4;  // staged path: batch columns of a checked job (more: plain path)
 constexpr int kWeightsBf16 = 0;
 constexpr int kWeightsE4m3 = 1;
 
