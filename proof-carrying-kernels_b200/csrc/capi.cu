@@ -287,6 +287,23 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
     ++cnt[best];
     ++assigned;
   }
+  // Never more CTAs than SMs on the staged path (one resident CTA each, so a dependent
+  // launch cannot take an SM that this grid still needs): trim the lightest jobs' extras.
+  const int64_t cap = tma ? std::max<int64_t>(sms, nj) : assigned;
+  while (assigned > cap) {
+    int best = -1;
+    double load = 1e300;
+    for (int j = 0; j < nj; ++j) {
+      const double l = static_cast<double>(bytes[j]) / static_cast<double>(cnt[j] - 1 > 0 ? cnt[j] - 1 : 1);
+      if (cnt[j] > 1 && l < load) {
+        best = j;
+        load = l;
+      }
+    }
+    if (best < 0) break;
+    --cnt[best];
+    --assigned;
+  }
   int64_t begin = 0;
   for (int j = 0; j < nj; ++j) {
     plan.jobs[j].cta_begin = static_cast<int32_t>(begin);

@@ -830,10 +830,13 @@ __device__ __forceinline__ void walk_next(PieceWalk& w, const JobPlan& jb, int64
   walk_load(w, jb, u0, count, row_piece, seg_piece);
 }
 
+// The consuming half of staged_warp (see there); `issue` and `issued` continue the walk
+// that primed the ring.
 template <int WFMT, int NV, int BG, bool kFma>
-__device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots,
-                                            uint32_t slot_bytes, uint32_t row_piece, uint8_t* ring,
-                                            uint64_t* full, uint32_t xs, int warp, int lane) {
+__device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, int64_t count, int slots,
+                                               uint32_t slot_bytes, uint32_t row_piece, uint8_t* ring,
+                                               uint64_t* full, uint32_t xs, int warp, int lane,
+                                               PieceWalk issue, int64_t issued) {
   constexpr int V = Format<WFMT>::kVec;
   constexpr int T = NV * kWarp;
   const uint64_t once = policy_evict_first();
@@ -842,11 +845,9 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   const int nvec = static_cast<int>(jb.n / V);
   const int vtotal = (nvec + T - 1) / T;
   const uint32_t seg_piece = slot_bytes / 512u * 512u;
-
-  PieceWalk issue, take;
-  walk_to(issue, jb, u0, warp, count, row_piece, seg_piece);
+  PieceWalk take;
   walk_to(take, jb, u0, warp, count, row_piece, seg_piece);
-  int64_t issued = 0, taken = 0;
+  int64_t taken = 0;
   auto issue_one = [&]() {
     const int slot = static_cast<int>(issued % slots);
     if (lane == 0) {
@@ -860,7 +861,6 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
     ++issued;
     walk_next(issue, jb, u0, count, row_piece, seg_piece);
   };
-  for (int s = 0; s < slots && issue.pieces > 0; ++s) issue_one();
 
   RowState<WFMT, NV, BG> row;
   double dacc[kSegBatch];  // indexed only by unrolled loops: registers
@@ -948,6 +948,46 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
 }
 
+// A warp's stream: primes its ring with weight pieces (weights are never written by a
+// kernel of this library, so this may overlap the previous kernel), then calls
+// `before_inputs` (which waits for the producers and brings in the activations; it returns
+// -1 if that failed, else whether the FMA form is exact), then reduces its units.
+template <int WFMT, int NV, int BG, typename Inputs>
+__device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots,
+                                            uint32_t slot_bytes, uint32_t row_piece, uint8_t* ring,
+                                            uint64_t* full, uint32_t xs, int warp, int lane,
+                                            Inputs before_inputs) {
+  const uint64_t once = policy_evict_first();
+  const uint32_t seg_piece = slot_bytes / 512u * 512u;
+  PieceWalk issue;
+  walk_to(issue, jb, u0, warp, count, row_piece, seg_piece);
+  int64_t issued = 0;
+  for (int s = 0; s < slots && issue.pieces > 0; ++s) {
+    if (lane == 0) {
+      const Unit iu = walk_unit(issue, jb, u0);
+      const uint32_t off = static_cast<uint32_t>(issue.piece) * issue.size;
+      const uint32_t bytes = min(issue.size, iu.bytes - off);
+      mbar_arrive_expect_tx(full + s, bytes);
+      bulk_load(ring + static_cast<int64_t>(s) * slot_bytes, static_cast<const uint8_t*>(iu.src) + off, bytes,
+                full + s, once);
+    }
+    ++issued;
+    walk_next(issue, jb, u0, count, row_piece, seg_piece);
+  }
+  const int fma_mode = before_inputs();
+  if (fma_mode < 0) {  // leave only after the copies into this warp's slots have landed
+    for (int64_t i = 0; i < issued; ++i) mbar_wait(full + i, 0);
+    return;
+  }
+  if (fma_mode) {
+    staged_consume<WFMT, NV, BG, true>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs, warp, lane,
+                                       issue, issued);
+  } else {
+    staged_consume<WFMT, NV, BG, false>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs, warp, lane,
+                                        issue, issued);
+  }
+}
+
 template <int WFMT, int NV, int BG, bool kTma>
 __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_constant__ Plan plan) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -980,30 +1020,34 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
       fence_barrier_init();
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      const uint32_t xbytes = static_cast<uint32_t>(static_cast<int64_t>(jb.batch) * jb.n * 2);
-      mbar_arrive_expect_tx(xbar, xbytes);
-      bulk_load(xs, jb.X, xbytes, xbar, policy_evict_last());
-    }
-    const bool have_x = mbar_wait(xbar, 0);
-    if (have_x && jb.has_w) {
-      x_exponents(reinterpret_cast<const uint16_t*>(xs), static_cast<int64_t>(jb.batch) * jb.n,
-                  static_cast<int>(threadIdx.x), kPlainThreads, xexp, xexp + 1);
-    }
-    __syncthreads();
-    if (!have_x) return;
-    const bool fma = jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]);
+    allow_dependents();
     uint8_t* ring = rings + static_cast<int64_t>(warp) * slots * slot_bytes;
     uint64_t* full = bars + warp * slots;
     const uint32_t xs_addr = smem_addr(xs);
-    if (fma) {
-      staged_warp<WFMT, NV, BG, true>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane);
-    } else {
-      staged_warp<WFMT, NV, BG, false>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane);
-    }
+    // After the weight prefetch: wait for the kernels this one depends on, then bring in the
+    // activations (every thread takes part, once).
+    auto inputs = [&]() -> int {
+      wait_for_producers();
+      if (threadIdx.x == 0) {
+        const uint32_t xbytes = static_cast<uint32_t>(static_cast<int64_t>(jb.batch) * jb.n * 2);
+        mbar_arrive_expect_tx(xbar, xbytes);
+        bulk_load(xs, jb.X, xbytes, xbar, policy_evict_last());
+      }
+      const bool have_x = __syncthreads_and(mbar_wait(xbar, 0));
+      if (!have_x) return -1;
+      if (jb.has_w) {
+        x_exponents(reinterpret_cast<const uint16_t*>(xs), static_cast<int64_t>(jb.batch) * jb.n,
+                    static_cast<int>(threadIdx.x), kPlainThreads, xexp, xexp + 1);
+      }
+      __syncthreads();
+      return jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]) ? 1 : 0;
+    };
+    staged_warp<WFMT, NV, BG>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane, inputs);
   } else {
     // Plain path: every warp takes whole units and reads global memory directly, one
     // element at a time (product, then sum: the same values as the staged path's).
+    allow_dependents();
+    wait_for_producers();
     const uint16_t* X = jb.X;
     int64_t cur_beta = -1;
     uint32_t pending = 0;

@@ -23,8 +23,19 @@ cudaError_t launch_variant(const Plan& plan, unsigned grid, size_t smem, cudaStr
       configured[dev] = 1;
     }
   }
-  fn<<<grid, kPlainThreads, smem, stream>>>(plan);
-  return cudaGetLastError();
+  // Programmatic dependent launch: this kernel may start while the previous kernel of the
+  // stream finishes; it prefetches only weights before griddepcontrol.wait.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kPlainThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, plan);
 }
 
 template <int WFMT, int NV>
