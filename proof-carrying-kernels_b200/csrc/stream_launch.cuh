@@ -6,6 +6,11 @@
 
 namespace pck {
 
+inline int current_device() {
+  int dev = -1;
+  return cudaGetDevice(&dev) == cudaSuccess ? dev : -1;
+}
+
 template <int WFMT, int NV, int BG, bool kTma>
 cudaError_t launch_variant(const Plan& plan, unsigned grid, size_t smem, cudaStream_t stream) {
   auto* fn = stream_kernel<WFMT, NV, BG, kTma>;
@@ -13,12 +18,10 @@ cudaError_t launch_variant(const Plan& plan, unsigned grid, size_t smem, cudaStr
     // The opt-in shared-memory size is a per-device function attribute: set it once per
     // device to the largest size this library ever asks for.
     static int configured[64] = {0};
-    int dev = 0;
-    cudaError_t err = cudaGetDevice(&dev);
-    if (err != cudaSuccess) return err;
+    const int dev = current_device();
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!configured[dev]) {
-      err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap);
+      const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap);
       if (err != cudaSuccess) return err;
       configured[dev] = 1;
     }
