@@ -163,6 +163,26 @@ typedef struct pck_gemv_job {
 int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream);
 
 /*
+ * pck_gemv_checked for callers that cannot allocate device memory: a serving engine that
+ * reserved nearly all of HBM for its own pool (a cudaMalloc beside it can fail and escapes
+ * its accounting), or a host runtime that reaches this library through a plain C FFI holding
+ * only device pointers the engine gave it. The checks' scratch (counters and partial sums;
+ * their fields in each job's descriptor are ignored and may be NULL) comes from one array of
+ * PCK_STATIC_SCRATCH_BYTES inside this library, one per device. A call needs, per checked
+ * job, 4*num_blocks bytes of counters and 8*batch*(checks+1)*num_blocks*segments bytes of
+ * partial sums, each region rounded up to 256 bytes; a call needing more is rejected with
+ * PCK_ERR_ARGUMENT before any work. Nothing is allocated: each call clears the counters on
+ * `stream` with cudaMemsetAsync and launches the same kernel as pck_gemv_checked, with
+ * bit-identical results. All calls on a device share the array, which keeps the last call's
+ * contents: calls whose work overlaps on the GPU (different streams or host threads) race
+ * and must be ordered by the caller. The first call on each device (with that device
+ * current) looks up the array's address with cudaGetSymbolAddress; make that first call
+ * before any stream capture. No counterpart in the reference.
+ */
+#define PCK_STATIC_SCRATCH_BYTES (4 << 20)
+int pck_gemv_checked_static(const pck_gemv_job* jobs, int count, void* stream);
+
+/*
  * Builds a checker's bank on the device from bfloat16 W (m, n) and signs r
  * (checks, m/block, block): c[k,beta,j] = fl32(sum_i r[k,beta,i] W[beta*block+i, j])
  * (binary64 sum over i in order, then rounded to nearest binary32) and

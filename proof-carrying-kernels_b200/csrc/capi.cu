@@ -448,3 +448,10 @@ int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m,
 }
 
 }  // extern "C"
+
+namespace pck {
+
+// Records `message` as the last error of this thread (for entry points in other files).
+int report_error(int code, const char* message) { return fail(code, "%s", message); }
+
+}  // namespace pck

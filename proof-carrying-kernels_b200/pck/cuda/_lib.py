@@ -17,6 +17,7 @@ PCK_WEIGHTS_BF16 = 0
 PCK_WEIGHTS_E4M3 = 1
 MAX_JOBS = 16  # PCK_MAX_JOBS
 MAX_BATCH = 16
+STATIC_SCRATCH_BYTES = 4 << 20  # PCK_STATIC_SCRATCH_BYTES
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -59,6 +60,7 @@ _SIGNATURES = {
     "pck_gemv_batched": ([_int, _p, _p, _p, _i64, _i64, _i64, _int, _p], _int),
     "pck_blocked_check": ([ctypes.POINTER(CheckDesc), _int, _p], _int),
     "pck_gemv_checked": ([ctypes.POINTER(GemvJob), _int, _p], _int),
+    "pck_gemv_checked_static": ([ctypes.POINTER(GemvJob), _int, _p], _int),
     "pck_bank_build": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _f64, _p], _int),
 }
 
