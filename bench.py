@@ -389,7 +389,7 @@ def main() -> None:
         from oracle.cpu_baseline import time_checked_layer
 
         mats = host_layer(args, groups)
-        timing = time_checked_layer(mats, args.threads, min_seconds=args.cpu_seconds)
+        timing = time_checked_layer(mats, args.threads, min_seconds=args.cpu_seconds, max_steps=10**6)
         cpu_value = layer_bytes(mats) * timing["steps"] / timing["seconds"] / 1e9
         cpu = {"value": round(cpu_value, 3), "unit": UNIT, "cores": timing["cores"], "kind": "port",
                "sample": f"{timing['steps']} whole checked layers in {timing['seconds']:.1f} s "
@@ -414,6 +414,8 @@ def main() -> None:
             "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / world / peak, 4),
                          "traffic": traffic,
+                         "scope": "one step = 4 launches of stream_kernel, the only kernel in the step; "
+                                  "achieved and traffic are per step (ncu summary in profiles/)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"},
             "e2e": {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e * 1e3, 4)},
