@@ -4,9 +4,11 @@ Workload: the Llama-3-8B decode-layer GEMV set (q 4096x4096, k/v 1024x4096, o 40
 gate/up 14336x4096, down 4096x14336), bfloat16 weights ~N(0, 0.02^2), activations ~N(0, 1)
 with 1% outlier channels x20, every output checked by the trusted blocked checker
 (b = 128, K = 1). A step is one decode layer: four launches of the persistent streaming
-kernel (q/k/v share their input, o, gate/up share theirs, down), each with its checks
-fused, captured in a CUDA graph. With N GPUs every matrix is row-sharded by whole checker
-blocks and one NCCL all-gather per step assembles the outputs and verdict bits.
+kernel (q/k/v share their input, o, gate/up share theirs, down), each with its checks'
+bank rows fused into the same pass over memory, then one verdict-kernel launch for all
+seven checks (the reference runs one checker launch per layer), captured in a CUDA graph.
+With N GPUs every matrix is row-sharded by whole checker blocks and one NCCL all-gather
+per step assembles the outputs and verdict bits.
 
 metric: checked-GEMV HBM throughput = algorithmic bytes of the step (weights, activations,
 outputs, checksum bank, verdicts) / device time, GB/s, over all ranks.
@@ -124,7 +126,7 @@ def outlier_x(n: int, batch: int, gen: torch.Generator) -> torch.Tensor:
 def build_layer(args, rank: int, world: int, device: torch.device):
     """Sharded weights, inputs, checkers and the launch objects of one decode layer."""
     from pck.cuda import GpuBlockedChecker
-    from pck.cuda.plan import LLAMA3_8B_GROUPS, GemvLaunch
+    from pck.cuda.plan import LLAMA3_8B_GROUPS, GemvLaunch, VerdictLaunch
     from pck.cuda.sharded import PackedOutputs, shard_rows
     from pck.fp import tree_height
 
@@ -152,10 +154,11 @@ def build_layer(args, rank: int, world: int, device: torch.device):
             y_views.append(ys.local_view(j))
             p_views.append(vs.local_view(j))
             j += 1
-        groups.append(GemvLaunch(items, args.threads, ys=y_views, passed=p_views))
+        groups.append(GemvLaunch(items, args.threads, ys=y_views, passed=p_views, verdicts=False))
         plain.append(GemvLaunch(items_plain, args.threads))
+    verdict = VerdictLaunch(groups)
     torch.cuda.synchronize()
-    return groups, plain, xs, ys, vs
+    return groups, verdict, plain, xs, ys, vs
 
 
 def cuda_graph(fn) -> torch.cuda.CUDAGraph:
@@ -341,11 +344,12 @@ def main() -> None:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)  # fmt: skip
 
-    groups, plain, xs, ys, vs = build_layer(args, rank, world, device)
+    groups, verdict, plain, xs, ys, vs = build_layer(args, rank, world, device)
+    launches = [*groups, verdict]
     step_bytes_local = sum(g.algorithmic_bytes for g in groups)
 
     def checked_step() -> None:
-        for g in groups:
+        for g in launches:
             g.launch()
         if world > 1:
             ys.gather()
@@ -373,7 +377,7 @@ def main() -> None:
         t_checked = timed(graph_checked, args.steps, args.warmup, world)
         t_plain = timed(graph_plain, args.steps, args.warmup, world)
     clock = clocks.summary()
-    t_e2e, h2d, d2h = e2e_step_time(groups, xs, ys, vs, max(20, args.steps // 10), args.warmup, world)
+    t_e2e, h2d, d2h = e2e_step_time(launches, xs, ys, vs, max(20, args.steps // 10), args.warmup, world)
 
     total_bytes = torch.tensor([float(step_bytes_local)], device=device)
     if world > 1:
@@ -404,7 +408,8 @@ def main() -> None:
             "config": {
                 "workload": "llama3-8b decode layer GEMV set (q,k,v,o,gate,up,down) + fused blocked check",
                 "batch": args.batch, "block": args.block, "checks": args.checks, "threads": args.threads,
-                "launches_per_step": len(groups), "parallelism": f"row-shard x{world}" if world > 1 else "single",
+                "launches_per_step": len(launches),
+                "verdicts": "one verdict-kernel launch per layer after the four GEMV launches", "parallelism": f"row-shard x{world}" if world > 1 else "single",
                 "l2": "inputs larger than L2 (436 MB of weights per step, 126 MB L2)",
                 "graph": "CUDA graph of one step, replayed",
             },
@@ -414,12 +419,12 @@ def main() -> None:
             "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / world / peak, 4),
                          "traffic": traffic,
-                         "scope": "one step = 4 launches of stream_kernel, the only kernel in the step; "
+                         "scope": "one step = 4 stream_kernel launches + 1 verdict_kernel launch; "
                                   "achieved and traffic are per step (ncu summary in profiles/)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"},
             "e2e": {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e * 1e3, 4)},
-            "gpu_launches": len(groups) * args.steps,
+            "gpu_launches": len(launches) * args.steps,
             "clocks": clock,
             "cpu_baseline": cpu,
         }  # fmt: skip

@@ -35,7 +35,7 @@ extern "C" {
 /* Message of the last failing call on this thread ("" if none). */
 const char* pck_last_error(void);
 
-/* ABI version of this library (increases when a declaration here changes). */
+/* ABI version of this library (increases when a declaration here changes): 2. */
 int pck_abi_version(void);
 
 /*
@@ -105,7 +105,7 @@ typedef struct pck_check_desc {
   const float* y;       /* (batch, num_blocks*block) binary32 output to check            */
   double* partial_cx;   /* scratch (batch, checks, num_blocks, segments)                 */
   double* partial_s;    /* scratch (batch, num_blocks, segments)                         */
-  uint32_t* counters;   /* scratch (num_blocks,), zero between calls; left zero          */
+  uint32_t* counters;   /* unused since ABI version 2 (may be NULL)                      */
   uint8_t* passed;      /* out (batch, checks, num_blocks), 1 = passed                   */
   double* rho;          /* out (batch, checks, num_blocks)                               */
   double* tau;          /* out (batch, checks, num_blocks)                               */
@@ -124,18 +124,19 @@ typedef struct pck_check_desc {
 #define PCK_MAX_JOBS 16
 
 /*
- * Checks up to PCK_MAX_JOBS GEMV outputs in one launch (the standalone check, run after the
- * producing kernel has finished). Replaces bindings.cpp:221-256 (`blocked_check`) and
+ * Checks up to PCK_MAX_JOBS GEMV outputs (the standalone check, run after the producing
+ * kernel has finished): one launch streams the bank rows into the partial sums, a second
+ * one decides every block. Replaces bindings.cpp:221-256 (`blocked_check`) and
  * checker_kernel.cu:189-196; the reference batches at most 8.
  */
 int pck_blocked_check(const pck_check_desc* descs, int count, void* stream);
 
 /*
- * One GEMV, optionally checked in the same launch.
+ * One GEMV, optionally checked in the same pass over memory.
  * weight_format: PCK_WEIGHTS_BF16 (vec 8) or PCK_WEIGHTS_E4M3 (vec 16).
- * If `check` is not NULL, its x and y must equal this job's X and Y; the verdict of each
- * row block is computed in the same kernel, by the last unit of that block to finish,
- * from the y values as stored in memory (fused production mode).
+ * If `check` is not NULL, its x and y must equal this job's X and Y; the streaming kernel
+ * reduces the job's bank rows against x together with W (fused production mode), and the
+ * verdict of each row block is then computed from the y values as stored in memory.
  */
 typedef struct pck_gemv_job {
   const void* W;                /* (m, n) weights                                         */
@@ -156,24 +157,41 @@ typedef struct pck_gemv_job {
 } pck_gemv_job;
 
 /*
- * Up to PCK_MAX_JOBS independent GEMVs (each optionally checked) in one persistent launch:
- * e.g. the q, k, v projections of a decode layer with their checks. No reference
+ * Up to PCK_MAX_JOBS independent GEMVs (each optionally checked) in one persistent launch
+ * of the streaming kernel, e.g. the q, k, v projections of a decode layer with their checks,
+ * followed by one launch of the verdict kernel for the checked jobs. No reference
  * counterpart: the reference launches each GEMV and the check separately.
  */
 int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream);
 
 /*
+ * pck_gemv_checked without the verdicts: the GEMVs and their checks' partial sums only.
+ * The caller decides the blocks later with pck_check_verdicts on the same stream (before
+ * reusing the checks' scratch), e.g. once for all checks of a decode layer, as the
+ * reference runs one checker launch per layer. No reference counterpart.
+ */
+int pck_gemv_partials(const pck_gemv_job* jobs, int count, void* stream);
+
+/*
+ * The block verdicts of up to PCK_MAX_JOBS checks whose partial sums an earlier
+ * pck_gemv_partials call on this stream computed (same descriptors), reading y as stored.
+ * The decision rule of src/pck/cuda/csrc/checker_kernel.cu:146-184.
+ */
+int pck_check_verdicts(const pck_check_desc* descs, int count, void* stream);
+
+/*
  * pck_gemv_checked for callers that cannot allocate device memory: a serving engine that
  * reserved nearly all of HBM for its own pool (a cudaMalloc beside it can fail and escapes
  * its accounting), or a host runtime that reaches this library through a plain C FFI holding
- * only device pointers the engine gave it. The checks' scratch (counters and partial sums;
- * their fields in each job's descriptor are ignored and may be NULL) comes from one array of
- * PCK_STATIC_SCRATCH_BYTES inside this library, one per device. A call needs, per checked
- * job, 4*num_blocks bytes of counters and 8*batch*(checks+1)*num_blocks*segments bytes of
- * partial sums, each region rounded up to 256 bytes; a call needing more is rejected with
- * PCK_ERR_ARGUMENT before any work. Nothing is allocated: each call clears the counters on
- * `stream` with cudaMemsetAsync and launches the same kernel as pck_gemv_checked, with
- * bit-identical results. All calls on a device share the array, which keeps the last call's
+ * only device pointers the engine gave it. The checks' scratch (the partial sums; the
+ * scratch fields of each job's descriptor are ignored and may be NULL) comes from one array
+ * of PCK_STATIC_SCRATCH_BYTES inside this library, one per device. A call needs, per checked
+ * job, 8*batch*checks*num_blocks*segments bytes for the c . x partials and
+ * 8*batch*num_blocks*segments bytes for the a . |x| partials, each region rounded up to 256
+ * bytes; a call needing more is rejected with PCK_ERR_ARGUMENT before any work. Nothing is
+ * allocated: the call launches the same kernels as pck_gemv_checked, with bit-identical
+ * results; nothing in the array has to start at zero, since every partial sum is written
+ * before it is read. All calls on a device share the array, which keeps the last call's
  * contents: calls whose work overlaps on the GPU (different streams or host threads) race
  * and must be ordered by the caller. The first call on each device (with that device
  * current) looks up the array's address with cudaGetSymbolAddress; make that first call

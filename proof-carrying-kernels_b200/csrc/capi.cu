@@ -13,6 +13,7 @@
 
 #include "pck_b200.h"
 #include "stream_plan.h"
+#include "verdict_plan.h"
 
 namespace pck {
 cudaError_t launch_gemv_naive(const void* W, const void* x, float* y, int64_t m, int64_t n,
@@ -81,7 +82,7 @@ struct Spec {
 int validate_check(const pck_check_desc* d) {
   if (!d) return fail(PCK_ERR_ARGUMENT, "check descriptor is NULL");
   if (!d->c || !d->a || !d->r || !d->x || !d->y || !d->partial_cx || !d->partial_s ||
-      !d->counters || !d->passed || !d->rho || !d->tau) {
+      !d->passed || !d->rho || !d->tau) {
     return fail(PCK_ERR_ARGUMENT, "check descriptor has a NULL pointer");
   }
   if (d->checks < 1 || d->num_blocks < 1 || d->n < 1 || d->block < 1) {
@@ -185,24 +186,11 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
       // scratch's `segments`): the binary64 bound holds for any split, so the split is
       // chosen for the kernel, not taken from the caller.
       jb.seg_alloc = d->segments;
-      const int64_t want = std::min<int64_t>(d->segments, (d->n + kSegmentTarget - 1) / kSegmentTarget);
-      int64_t len = (d->n + want - 1) / want;
-      len = (len + 7) / 8 * 8;
-      jb.seg_len = len;
-      jb.segs = static_cast<int32_t>((d->n + len - 1) / len);
+      pck::segment_split(d->n, d->segments, kSegmentTarget, &jb.seg_len, &jb.segs);
       jb.c = d->c;
       jb.a = static_cast<const uint16_t*>(d->a);
-      jb.r = d->r;
-      jb.y_check = d->y;
       jb.partial_cx = d->partial_cx;
       jb.partial_s = d->partial_s;
-      jb.counters = d->counters;
-      jb.passed = d->passed;
-      jb.rho = d->rho;
-      jb.tau = d->tau;
-      jb.coef = d->coef;
-      jb.geps = d->geps;
-      jb.tau_floor = d->tau_floor;
       jb.row_units = s.has_w ? d->block : 0;
       jb.period_units = jb.row_units + static_cast<int64_t>(d->checks + 1) * jb.segs;
       jb.period_bytes = (s.has_w ? d->block * jb.row_bytes : 0) + (4LL * d->checks + 2) * d->n;
@@ -322,6 +310,44 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   return ok();
 }
 
+// Launches the verdict kernel for `count` validated checks whose partial sums are (or will
+// be, earlier on the stream) in their scratch.
+int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream) {
+  if (count < 1 || count > pck::kMaxVerdictJobs) {
+    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", pck::kMaxVerdictJobs, count);
+  }
+  pck::VerdictPlan plan{};
+  int64_t tasks = 0;
+  for (int i = 0; i < count; ++i) {
+    const pck_check_desc* d = descs[i];
+    pck::VerdictJob& vj = plan.jobs[i];
+    int64_t seg_len = 0;
+    pck::segment_split(d->n, d->segments, kSegmentTarget, &seg_len, &vj.segs);
+    vj.y = d->y;
+    vj.r = d->r;
+    vj.partial_cx = d->partial_cx;
+    vj.partial_s = d->partial_s;
+    vj.passed = d->passed;
+    vj.rho = d->rho;
+    vj.tau = d->tau;
+    vj.block = d->block;
+    vj.num_blocks = d->num_blocks;
+    vj.checks = d->checks;
+    vj.seg_alloc = d->segments;
+    vj.batch = d->batch;
+    vj.coef = d->coef;
+    vj.geps = d->geps;
+    vj.tau_floor = d->tau_floor;
+    vj.task_begin = tasks;
+    vj.tasks = static_cast<int64_t>(d->batch) * d->checks * d->num_blocks;
+    tasks += vj.tasks;
+  }
+  plan.njobs = count;
+  const cudaError_t err = pck::launch_verdicts(plan, tasks, stream);
+  if (err != cudaSuccess) return cuda_fail("verdict kernel", err);
+  return ok();
+}
+
 int check_gemv_args(const void* W, const void* x, const float* y, int64_t m, int64_t n,
                     int threads, int min_threads) {
   if (m < 0 || n < 0) return fail(PCK_ERR_ARGUMENT, "expected W of shape (m, n) with m, n >= 0");
@@ -339,7 +365,7 @@ extern "C" {
 
 const char* pck_last_error(void) { return g_error.c_str(); }
 
-int pck_abi_version(void) { return 1; }
+int pck_abi_version(void) { return 2; }
 
 int pck_device_status(unsigned int* status, int clear) {
   if (!status) return fail(PCK_ERR_ARGUMENT, "status must not be NULL");
@@ -400,10 +426,13 @@ int pck_blocked_check(const pck_check_desc* descs, int count, void* stream) {
     specs.push_back(Spec{nullptr, nullptr, nullptr, 0, descs[i].n, descs[i].batch, 256,
                          PCK_WEIGHTS_BF16, false, descs + i, 0, 0});
   }
-  return run_stream(specs, static_cast<cudaStream_t>(stream));
+  if (int rc = run_stream(specs, static_cast<cudaStream_t>(stream))) return rc;
+  const pck_check_desc* checks[PCK_MAX_JOBS];
+  for (int i = 0; i < count; ++i) checks[i] = descs + i;
+  return run_verdicts(checks, count, static_cast<cudaStream_t>(stream));
 }
 
-int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream) {
+int pck_gemv_partials(const pck_gemv_job* jobs, int count, void* stream) {
   if (count < 1 || count > PCK_MAX_JOBS || !jobs) {
     return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", PCK_MAX_JOBS, count);
   }
@@ -429,6 +458,29 @@ int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream) {
                          true, jb.check, jb.w_exp_min, jb.w_exp_max});
   }
   return run_stream(specs, static_cast<cudaStream_t>(stream));
+}
+
+int pck_check_verdicts(const pck_check_desc* descs, int count, void* stream) {
+  if (count < 1 || count > PCK_MAX_JOBS || !descs) {
+    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", PCK_MAX_JOBS, count);
+  }
+  const pck_check_desc* checks[PCK_MAX_JOBS];
+  for (int i = 0; i < count; ++i) {
+    if (int rc = validate_check(descs + i)) return rc;
+    checks[i] = descs + i;
+  }
+  return run_verdicts(checks, count, static_cast<cudaStream_t>(stream));
+}
+
+int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream) {
+  if (int rc = pck_gemv_partials(jobs, count, stream)) return rc;
+  const pck_check_desc* checks[PCK_MAX_JOBS];
+  int n = 0;
+  for (int i = 0; i < count; ++i) {
+    if (jobs[i].check && jobs[i].m > 0) checks[n++] = jobs[i].check;
+  }
+  if (n == 0) return ok();
+  return run_verdicts(checks, n, static_cast<cudaStream_t>(stream));
 }
 
 int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m, int64_t n,

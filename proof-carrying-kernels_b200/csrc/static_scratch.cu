@@ -1,8 +1,8 @@
 // pck_gemv_checked_static: the fused checked GEMV of pck_gemv_checked for callers that
 // cannot allocate device memory.
 //
-// A check needs scratch beside its inputs and outputs: one ticket counter per row block and
-// the binary64 partial sums of the checksum and bound rows. pck_gemv_checked takes that
+// A check needs scratch beside its inputs and outputs: the binary64 partial sums of the
+// checksum and bound rows, per row block and column segment. pck_gemv_checked takes that
 // scratch from the caller. Some callers have none to give: a serving engine that reserved
 // almost all of HBM for its own pool up front (a cudaMalloc beside it can fail, and is
 // invisible to its memory accounting), or a host runtime that reaches this library through
@@ -11,9 +11,8 @@
 // this library's device code, so it allocates no device memory at all.
 //
 // The array is shared by every call on a device and keeps what the last call left in it.
-// Each call therefore clears the counters (the only part that must start at zero) on its
-// own stream before the launch; the partial sums are always written before they are read.
-// Two calls whose work overlaps on the GPU (other streams, other host threads) race on the
+// Nothing in it has to start at zero: every partial sum is written by the streaming kernel
+// before the verdict kernel of the same call reads it. Two calls whose work overlaps on the GPU (other streams, other host threads) race on the
 // array and may produce wrong verdicts; keep the calls of one device on one stream, or
 // order them.
 //
@@ -33,8 +32,8 @@ namespace pck {
 int report_error(int code, const char* message);
 }  // namespace pck
 
-// The scratch of pck_gemv_checked_static on each device: the checks' counters first, then
-// their partial sums, every region aligned to 256 bytes. Zero when the library is loaded.
+// The scratch of pck_gemv_checked_static on each device: the checks' partial sums, every
+// region aligned to 256 bytes.
 static __device__ __align__(256) unsigned char g_static_scratch[PCK_STATIC_SCRATCH_BYTES];
 
 namespace {
@@ -107,23 +106,17 @@ extern "C" int pck_gemv_checked_static(const pck_gemv_job* jobs, int count, void
 
   pck_gemv_job local[PCK_MAX_JOBS];
   pck_check_desc descs[PCK_MAX_JOBS];
-  int64_t counters_at[PCK_MAX_JOBS], cx_at[PCK_MAX_JOBS], s_at[PCK_MAX_JOBS];
+  int64_t cx_at[PCK_MAX_JOBS], s_at[PCK_MAX_JOBS];
 
-  // Layout: every check's counters, then every check's partial sums.
+  // Layout: each check's c . x partials, then its a . |x| partials.
   int64_t used = 0;
   for (int i = 0; i < count; ++i) {
     local[i] = jobs[i];
-    counters_at[i] = cx_at[i] = s_at[i] = 0;
+    cx_at[i] = s_at[i] = 0;
     if (!jobs[i].check) continue;
     descs[i] = *jobs[i].check;
     local[i].check = &descs[i];
     if (!sized(&descs[i])) continue;
-    counters_at[i] = used;
-    used += region(mul_sat(descs[i].num_blocks, 4));
-  }
-  const int64_t counters_span = used;
-  for (int i = 0; i < count; ++i) {
-    if (!jobs[i].check || !sized(&descs[i])) continue;
     const pck_check_desc& d = descs[i];
     const int64_t cells = mul_sat(mul_sat(d.batch, d.num_blocks), d.segments);
     cx_at[i] = used;
@@ -146,14 +139,9 @@ extern "C" int pck_gemv_checked_static(const pck_gemv_job* jobs, int count, void
   if (int rc = scratch_base(&base)) return rc;
   for (int i = 0; i < count; ++i) {
     if (!jobs[i].check) continue;
-    descs[i].counters = reinterpret_cast<uint32_t*>(base + counters_at[i]);
+    descs[i].counters = nullptr;
     descs[i].partial_cx = reinterpret_cast<double*>(base + cx_at[i]);
     descs[i].partial_s = reinterpret_cast<double*>(base + s_at[i]);
-  }
-  if (counters_span > 0) {
-    const cudaError_t err = cudaMemsetAsync(base, 0, static_cast<size_t>(counters_span),
-                                            static_cast<cudaStream_t>(stream));
-    if (err != cudaSuccess) return reject(PCK_ERR_CUDA, "static scratch clear failed: %s", cudaGetErrorString(err));
   }
   return pck_gemv_checked(local, count, stream);
 }

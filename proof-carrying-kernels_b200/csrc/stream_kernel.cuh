@@ -1,14 +1,15 @@
-// The persistent streaming kernel: GEMV rows, checksum-bank segments and the block
-// verdicts of the trusted checker, for every job of a launch plan (stream_plan.h).
+// The persistent streaming kernel: GEMV rows and the checksum-bank segments of the trusted
+// checker, for every job of a launch plan (stream_plan.h). The block verdicts follow in the
+// verdict kernel (verdict_kernel.cu).
 //
-// Staged path (kTma): each of the eight warps of a CTA owns the units w, w + 8, ... of the
+// Staged path (kTma): each of the 16 consumer warps of a CTA owns the units w, w + 16, ... of the
 // CTA's range and streams them through its own ring of `slots` shared-memory pieces with
 // cp.async.bulk: lane 0 arms the piece's mbarrier with the expected bytes and issues the
 // copy; the warp waits for the barrier's phase, reduces the piece, and refills the same
 // slot with its next piece. Each slot is used by one warp in order, so every parity wait
 // is exact. Rows longer than a piece are split at vector-iteration boundaries and their
 // chains carry over in registers. The activations X of the CTA's job are copied to shared
-// memory once. Plain path (unaligned pointers, n not a multiple of the vector width): the
+// memory once, after the weight prefetch. Plain path (unaligned pointers, n not a multiple of the vector width): the
 // same units read straight from global memory with scalar loads; the arithmetic is the
 // same.
 //
@@ -426,91 +427,6 @@ __device__ __forceinline__ void a_segment(const uint16_t* __restrict__ as,
 }
 
 // ---------------------------------------------------------------------------------------
-// Verdict of row block beta: runs in the warp that completed the block's last unit, after
-// every other unit's results were published (fence, then ticket). Reads y from memory.
-// Decision rule of the reference checker (src/pck/cuda/csrc/checker_kernel.cu:146-184).
-
-// Sum of the segment partials p[0..count) in index order (rounded up when kUp), computed
-// by lane 0 from values the lanes load together. Every lane returns it.
-template <bool kUp>
-__device__ __forceinline__ double ordered_sum(const double* p, int count, int lane) {
-  double total = 0.0;
-  for (int s0 = 0; s0 < count; s0 += kWarp) {
-    const double mine = s0 + lane < count ? __ldcg(p + s0 + lane) : 0.0;
-    const int here = min(kWarp, count - s0);
-    for (int i = 0; i < here; ++i) {
-      const double v = __shfl_sync(kFullMask, mine, i);
-      total = kUp ? __dadd_ru(total, v) : __dadd_rn(total, v);
-    }
-  }
-  return total;
-}
-
-static __device__ __noinline__ void merge_block(const JobPlan& jb, int64_t beta, int lane) {
-  __threadfence();
-  const int blk = jb.block;
-  const int64_t nb = jb.num_blocks;
-  const int64_t ldy = jb.m;
-  constexpr double kOnePlusU32 = 1.0 + 0x1p-24;
-  constexpr double kFloatMax = 3.4028234663852886e38;
-  for (int col = 0; col < jb.batch; ++col) {
-    const float* yb = jb.y_check + col * ldy + beta * blk;
-    double yabs = 0.0;
-    bool bad = false;
-    for (int i = lane; i < blk; i += kWarp) {
-      const float v = __ldcg(yb + i);
-      bad |= !isfinite(v);
-      yabs = __dadd_ru(yabs, fabs(static_cast<double>(v)));
-    }
-    yabs = warp_sum_ru(yabs);
-    bad = __any_sync(kFullMask, bad);
-    const double s_total =
-        ordered_sum<true>(jb.partial_s + (col * nb + beta) * jb.seg_alloc, jb.segs, lane);
-    for (int k = 0; k < jb.checks; ++k) {
-      const int8_t* rk = jb.r + (static_cast<int64_t>(k) * nb + beta) * blk;
-      double ry = 0.0;
-      for (int i = lane; i < blk; i += kWarp) {
-        const double v = static_cast<double>(__ldcg(yb + i));
-        ry = __dadd_rn(ry, __ldg(rk + i) > 0 ? v : -v);
-      }
-      ry = warp_sum_rn(ry);
-      const double cx = ordered_sum<false>(
-          jb.partial_cx + ((static_cast<int64_t>(col) * jb.checks + k) * nb + beta) * jb.seg_alloc, jb.segs,
-          lane);
-      if (lane == 0) {
-        const double rho = __dsub_rn(cx, ry);
-        const double cabs = __dmul_ru(kOnePlusU32, s_total);
-        const double eps = __dmul_ru(jb.geps, __dadd_ru(cabs, yabs));
-        double tau = __dadd_ru(__dadd_ru(__dmul_ru(jb.coef, s_total), eps), jb.tau_floor);
-        // Beyond the binary32 range of a.|x| the checked kernel's rounding model (no
-        // overflow) cannot hold: the threshold is unbounded and the block fails closed.
-        if (!(s_total <= kFloatMax)) tau = __longlong_as_double(0x7ff0000000000000LL);
-        const int64_t o = (static_cast<int64_t>(col) * jb.checks + k) * nb + beta;
-        jb.passed[o] = (!bad && isfinite(tau) && fabs(rho) <= tau) ? 1 : 0;
-        jb.rho[o] = rho;
-        jb.tau[o] = tau;
-      }
-    }
-  }
-  if (lane == 0) jb.counters[beta] = 0;  // ready for the next call
-}
-
-// Publishes `count` finished units of block beta; the warp that finishes the block
-// computes its verdict.
-__device__ __forceinline__ void credit_block(const JobPlan& jb, int64_t beta, uint32_t count,
-                                             int lane) {
-  __syncwarp();
-  uint32_t before = 0;
-  if (lane == 0) {
-    __threadfence();
-    before = atomicAdd(jb.counters + beta, count);
-  }
-  before = __shfl_sync(kFullMask, before, 0);
-  const uint32_t total = static_cast<uint32_t>(jb.period_units);
-  if (before + count == total) merge_block(jb, beta, lane);
-}
-
-// ---------------------------------------------------------------------------------------
 // Plain path: one warp per unit, global memory.
 
 template <int WFMT, int NV, int BG>
@@ -742,17 +658,39 @@ __device__ __forceinline__ void segment_piece(double* acc, uint32_t piece, uint3
 
 // Exponent fields (bfloat16 bits 7-14) of the activations: smallest over nonzero values
 // (subnormals count as 1) and largest over all.
-__device__ __forceinline__ void x_exponents(const uint16_t* X, int64_t count, int first, int step,
-                                            unsigned* lo, unsigned* hi) {
+// Copies the activations X (batch * n bfloat16, a multiple of 16 bytes, 16-byte aligned)
+// into shared memory with one 16-byte load per thread and step, through L2 (X may have been
+// written by the kernel this one waited for), and merges the smallest nonzero (subnormals
+// counted as 1) and the largest exponent field into xexp[0..1].
+__device__ __forceinline__ void load_activations(const JobPlan& jb, uint8_t* xs, uint32_t* xexp, int tid,
+                                                 int lane) {
+  const int64_t words = static_cast<int64_t>(jb.batch) * jb.n / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(jb.X);
+  uint4* dst = reinterpret_cast<uint4*>(xs);
   unsigned mn = 1000, mx = 0;
-  for (int64_t j = first; j < count; j += step) {
-    const unsigned mag = X[j] & 0x7fffu;
-    const unsigned e = mag >> 7;
-    mx = max(mx, e);
-    if (mag) mn = min(mn, max(e, 1u));
+  for (int64_t i = tid; i < words; i += kPlainThreads) {
+    const uint4 v = __ldcg(src + i);
+    dst[i] = v;
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      const unsigned mag = (h & 1 ? w[h / 2] >> 16 : w[h / 2]) & 0x7fffu;
+      const unsigned e = mag >> 7;
+      mx = max(mx, e);
+      if (mag) mn = min(mn, max(e, 1u));
+    }
   }
-  atomicMin(lo, mn);
-  atomicMax(hi, mx);
+  if (jb.has_w) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = min(mn, __shfl_xor_sync(kFullMask, mn, o));
+      mx = max(mx, __shfl_xor_sync(kFullMask, mx, o));
+    }
+    if (lane == 0) {
+      atomicMin(xexp, mn);
+      atomicMax(xexp + 1, mx);
+    }
+  }
 }
 
 // Whether one FMA equals the product-then-sum for every weight x activation pair.
@@ -864,15 +802,9 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
 
   RowState<WFMT, NV, BG> row;
   double dacc[kSegBatch];  // indexed only by unrolled loops: registers
-  int64_t cur_beta = -1;
-  uint32_t pending = 0;
-  bool ok = true;
   while (take.pieces > 0) {
     const int slot = static_cast<int>(taken % slots);
-    if (!mbar_wait(full + slot, static_cast<uint32_t>((taken / slots) & 1))) {
-      ok = false;
-      break;
-    }
+    if (!mbar_wait(full + slot, static_cast<uint32_t>((taken / slots) & 1))) break;
     const uint32_t piece = ring_addr + static_cast<uint32_t>(slot) * slot_bytes;
     const Unit un = walk_unit(take, jb, u0);
     const bool first = take.piece == 0;
@@ -931,19 +863,8 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
       if (lane == 0) fence_proxy_async_smem();
       issue_one();
     }
-    const int64_t beta = un.beta;
-    const bool unit_done = last;
     walk_next(take, jb, u0, count, row_piece, seg_piece);
-    if (unit_done && jb.has_check) {
-      if (beta != cur_beta && pending) {
-        credit_block(jb, cur_beta, pending, lane);
-        pending = 0;
-      }
-      cur_beta = beta;
-      ++pending;
-    }
   }
-  if (ok && pending) credit_block(jb, cur_beta, pending, lane);
   // Leave only after every copy into this warp's slots has landed.
   for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
 }
@@ -1010,11 +931,9 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
     uint8_t* xs = smem;
     uint8_t* rings = smem + plan.x_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(rings + static_cast<int64_t>(kConsumerWarps) * slots * slot_bytes);
-    uint64_t* xbar = bars + kConsumerWarps * slots;
-    uint32_t* xexp = reinterpret_cast<uint32_t*>(xbar + 1);  // [0] smallest, [1] largest exponent of x
+    uint32_t* xexp = reinterpret_cast<uint32_t*>(bars + kConsumerWarps * slots);  // [0] smallest, [1] largest exponent of x
     if (threadIdx.x == 0) {
       for (int s = 0; s < kConsumerWarps * slots; ++s) mbar_init(bars + s, 1);
-      mbar_init(xbar, 1);
       xexp[0] = 1000;
       xexp[1] = 0;
       fence_barrier_init();
@@ -1025,20 +944,11 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
     uint64_t* full = bars + warp * slots;
     const uint32_t xs_addr = smem_addr(xs);
     // After the weight prefetch: wait for the kernels this one depends on, then bring in the
-    // activations (every thread takes part, once).
+    // activations with 16-byte loads of every thread (not bulk copies, which would queue
+    // behind the weight pieces already requested) and take their exponent range.
     auto inputs = [&]() -> int {
       wait_for_producers();
-      if (threadIdx.x == 0) {
-        const uint32_t xbytes = static_cast<uint32_t>(static_cast<int64_t>(jb.batch) * jb.n * 2);
-        mbar_arrive_expect_tx(xbar, xbytes);
-        bulk_load(xs, jb.X, xbytes, xbar, policy_evict_last());
-      }
-      const bool have_x = __syncthreads_and(mbar_wait(xbar, 0));
-      if (!have_x) return -1;
-      if (jb.has_w) {
-        x_exponents(reinterpret_cast<const uint16_t*>(xs), static_cast<int64_t>(jb.batch) * jb.n,
-                    static_cast<int>(threadIdx.x), kPlainThreads, xexp, xexp + 1);
-      }
+      load_activations(jb, xs, xexp, static_cast<int>(threadIdx.x), lane);
       __syncthreads();
       return jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]) ? 1 : 0;
     };
@@ -1049,21 +959,9 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
     allow_dependents();
     wait_for_producers();
     const uint16_t* X = jb.X;
-    int64_t cur_beta = -1;
-    uint32_t pending = 0;
     for (int64_t i = warp; i < count; i += kConsumerWarps) {
-      const Unit un = decode_unit(jb, u0 + i);
-      plain_unit<WFMT, NV, BG>(jb, un, X, lane);
-      if (jb.has_check) {
-        if (un.beta != cur_beta && pending) {
-          credit_block(jb, cur_beta, pending, lane);
-          pending = 0;
-        }
-        cur_beta = un.beta;
-        ++pending;
-      }
+      plain_unit<WFMT, NV, BG>(jb, decode_unit(jb, u0 + i), X, lane);
     }
-    if (pending) credit_block(jb, cur_beta, pending, lane);
   }
 }
 

@@ -9,7 +9,8 @@
 //   - a segment of a bound row a[beta, :]          -> partial a . |x_b| (binary64, up)
 // For a checked job the units of row block beta are laid out contiguously:
 //   [ceil(block / R) row units (fused only)] [checks x segs c-units] [segs a-units]
-// and the unit of the block that finishes last (an atomic ticket) computes the verdict.
+// The segment units leave binary64 partial sums; the verdict kernel (verdict_plan.h) turns
+// them, with y as stored, into the block decisions once this kernel has finished.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -57,17 +58,8 @@ struct JobPlan {
   int64_t seg_len;    // columns per segment (multiple of 8)
   const float* c;
   const uint16_t* a;
-  const int8_t* r;
-  const float* y_check;  // (batch, m) the output whose blocks are checked
-  double* partial_cx;
-  double* partial_s;
-  uint32_t* counters;
-  uint8_t* passed;
-  double* rho;
-  double* tau;
-  double coef;
-  double geps;
-  double tau_floor;
+  double* partial_cx;  // (batch, checks, num_blocks, seg_alloc)
+  double* partial_s;   // (batch, num_blocks, seg_alloc)
   // partition
   int64_t units;         // total units
   int64_t period_units;  // units per row block (checked) or 1 (unchecked)

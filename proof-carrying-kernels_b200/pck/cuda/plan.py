@@ -42,7 +42,7 @@ class GemvLaunch:
 
     def __init__(self, items: Sequence[tuple[torch.Tensor, torch.Tensor, GpuBlockedChecker | None]],
                  threads: int = 256, ys: Sequence[torch.Tensor] | None = None,
-                 passed: Sequence[torch.Tensor | None] | None = None) -> None:  # fmt: skip
+                 passed: Sequence[torch.Tensor | None] | None = None, verdicts: bool = True) -> None:  # fmt: skip
         if not 1 <= len(items) <= _lib.MAX_JOBS:
             raise ValueError(f"a launch holds 1 to {_lib.MAX_JOBS} GEMVs, got {len(items)}")
         W0 = items[0][0]
@@ -51,6 +51,7 @@ class GemvLaunch:
         want = torch.float8_e4m3fn if self.fmt == _lib.PCK_WEIGHTS_E4M3 else torch.bfloat16
         ext = extension()
         self.lib = ext.lib
+        self.verdicts = verdicts
         self.count = len(items)
         self._descs = (_lib.CheckDesc * self.count)()
         self._jobs = (_lib.GemvJob * self.count)()
@@ -90,10 +91,17 @@ class GemvLaunch:
             job.check = ctypes.pointer(self._descs[g])
 
     def launch(self) -> None:
-        """Issue the launch on the current stream."""
+        """Issue the launch on the current stream (with ``verdicts=False``, the GEMVs and the
+        checks' partial sums only; a VerdictLaunch decides the blocks later)."""
+        fn = self.lib.pck_gemv_checked if self.verdicts else self.lib.pck_gemv_partials
         with on_device(self.device):
-            rc = self.lib.pck_gemv_checked(self._jobs, self.count, stream_handle(self.device))
+            rc = fn(self._jobs, self.count, stream_handle(self.device))
         _lib.check(rc, "checked gemv kernel")
+
+    @property
+    def check_descs(self) -> list:
+        """The descriptors of this launch's checks (for a VerdictLaunch)."""
+        return [self._descs[g] for g, res in enumerate(self.results) if res is not None]
 
     @property
     def algorithmic_bytes(self) -> int:
@@ -106,6 +114,28 @@ class GemvLaunch:
                 total += ch.c.numel() * 4 + ch.a.numel() * 2 + ch.r.numel()
                 total += res.passed.numel() * (1 + 8 + 8)
         return total
+
+
+class VerdictLaunch:
+    """One launch of the verdict kernel for the checks of up to 16 GemvLaunch objects made
+    with ``verdicts=False`` (e.g. every check of a decode layer, as the reference runs one
+    checker launch per layer). Launch it on the same stream after them; their CheckResult
+    objects then hold the verdicts."""
+
+    def __init__(self, launches: Sequence[GemvLaunch]) -> None:
+        descs = [d for gl in launches for d in gl.check_descs]
+        if not 1 <= len(descs) <= _lib.MAX_JOBS:
+            raise ValueError(f"a verdict launch covers 1 to {_lib.MAX_JOBS} checks, got {len(descs)}")
+        self.launches = list(launches)  # keeps the checks' tensors alive
+        self.device = launches[0].device
+        self.lib = launches[0].lib
+        self.count = len(descs)
+        self._descs = (_lib.CheckDesc * self.count)(*descs)
+
+    def launch(self) -> None:
+        with on_device(self.device):
+            rc = self.lib.pck_check_verdicts(self._descs, self.count, stream_handle(self.device))
+        _lib.check(rc, "verdict kernel")
 
 
 # Llama-3-8B decode-layer projections: (name, m, n) with hidden 4096, 8 KV heads of 128,

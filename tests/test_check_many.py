@@ -183,3 +183,44 @@ def test_side_stream_sees_output_even_if_freed_and_overwritten() -> None:
         garbage.add_(1)
     for p in pending:
         assert p.wait().verdict.all()
+
+
+def test_one_verdict_launch_per_layer_equals_the_fused_launches() -> None:
+    """GEMVs with deferred verdicts (pck_gemv_partials) and one verdict launch for every
+    check of a scaled Llama-3-8B layer give the bits of the fused calls, including a block
+    whose output was altered between the GEMV and the verdict."""
+    from pck.cuda import GpuBlockedChecker
+    from pck.cuda.plan import GemvLaunch, VerdictLaunch
+
+    gen = torch.Generator().manual_seed(13)
+    groups = [[(768, 4096), (128, 4096), (128, 4096)], [(512, 4096)], [(1792, 4096), (1792, 4096)],
+              [(512, 14336)]]  # fmt: skip
+    deferred, fused = [], []
+    for shapes in groups:
+        x = torch.randn(shapes[0][1], generator=gen).bfloat16().cuda()
+        items = []
+        for m, n in shapes:
+            W = (torch.randn(m, n, generator=gen) * 0.02).bfloat16().cuda()
+            items.append((W, x, GpuBlockedChecker(W, 128, tree_height(n, 256, 8), checks=2, generator=gen)))
+        deferred.append(GemvLaunch(items, 256, verdicts=False))
+        fused.append(GemvLaunch(items, 256))
+    verdict = VerdictLaunch(deferred)
+    for g in fused:
+        g.launch()
+    torch.cuda.synchronize()
+    want = [[(y.clone(), r.passed.clone(), r.rho.clone(), r.tau.clone()) for y, r in zip(g.ys, g.results, strict=True)]
+            for g in fused]  # fmt: skip
+    for g in deferred:
+        g.launch()
+    deferred[1].ys[0][300] += 1.0  # a fault after the GEMV, before the verdicts
+    verdict.launch()
+    torch.cuda.synchronize()
+    for gi, g in enumerate(deferred):
+        for j, (y, r) in enumerate(zip(g.ys, g.results, strict=True)):
+            y0, p0, rho0, tau0 = want[gi][j]
+            if gi == 1:
+                assert not bool(r.passed[:, 300 // 128].any()) and int(r.passed.sum()) == r.passed.numel() - 2
+                continue
+            assert torch.equal(y.view(torch.int32), y0.view(torch.int32))
+            assert torch.equal(r.passed, p0) and torch.equal(r.rho, rho0) and torch.equal(r.tau, tau0)
+            assert bool(r.passed.all())
