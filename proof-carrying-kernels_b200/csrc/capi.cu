@@ -103,6 +103,9 @@ int validate_check(const pck_check_desc* d) {
 constexpr int64_t kPieceTarget = 4 * 1024;  // row piece size the staged path aims for
 constexpr int kMaxSlots = 4;                // ring slots per warp
 constexpr int64_t kSegmentTarget = 2048;    // columns per checksum-bank segment
+// Time per byte of a bank segment (binary64 products and sums) relative to a weight row,
+// for the CTA split between the jobs of a launch.
+constexpr double kBankCost = 4.0;
 
 // Plans and launches the streaming kernel for `specs` (validated by the caller).
 int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
@@ -150,35 +153,50 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   }
   if (live.empty()) return ok();
 
-  // Pass 2: units and bytes of every job (one row per row unit).
+  // Pass 2: units and bytes of every job (one row per row unit). A checked GEMV becomes two
+  // jobs of the launch: its rows, and its bank rows (reduced against the same x). Their
+  // partial sums meet in the verdict kernel, so the bank work need not follow the rows of
+  // its block; as a job of its own it is spread over CTAs weighted by its cost.
   pck::Plan plan{};
   int64_t x_bytes = 0;
-  std::vector<int64_t> bytes;
+  std::vector<double> bytes;  // cost-weighted, for the CTA split
   int64_t max_row_bytes = 0;
   int nj = 0;
   for (const Spec* sp : live) {
     const Spec& s = *sp;
-    pck::JobPlan jb{};
-    jb.W = s.W;
-    jb.X = static_cast<const uint16_t*>(s.has_w ? s.X : s.check->x);
-    jb.Y = s.Y;
-    jb.has_w = s.has_w ? 1 : 0;
-    jb.has_check = s.check ? 1 : 0;
-    jb.w_exp_min = s.w_exp_min;
-    jb.w_exp_max = s.w_exp_max;
-    if (s.check) {
-      jb.m = static_cast<int64_t>(s.check->num_blocks) * s.check->block;
-      jb.n = s.check->n;
-      jb.batch = s.check->batch;
-    } else {
+    if (s.has_w) {
+      pck::JobPlan jb{};
+      jb.W = s.W;
+      jb.X = static_cast<const uint16_t*>(s.X);
+      jb.Y = s.Y;
+      jb.has_w = 1;
+      jb.w_exp_min = s.w_exp_min;
+      jb.w_exp_max = s.w_exp_max;
       jb.m = s.m;
       jb.n = s.n;
       jb.batch = s.batch;
+      jb.row_bytes = jb.n * esize;
+      jb.rows = 1;
+      jb.row_units = static_cast<int32_t>(jb.m);
+      jb.period_units = 1;
+      jb.period_bytes = jb.row_bytes;
+      jb.units = jb.m;
+      jb.total_bytes = jb.m * jb.row_bytes;
+      max_row_bytes = std::max<int64_t>(max_row_bytes, jb.row_bytes);
+      x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 2);
+      plan.jobs[nj++] = jb;
+      bytes.push_back(static_cast<double>(jb.total_bytes));
     }
-    jb.row_bytes = jb.n * esize;
-    jb.rows = 1;
     if (s.check) {
       const pck_check_desc* d = s.check;
+      pck::JobPlan jb{};
+      jb.X = static_cast<const uint16_t*>(d->x);
+      jb.has_check = 1;
+      jb.m = static_cast<int64_t>(d->num_blocks) * d->block;
+      jb.n = d->n;
+      jb.batch = d->batch;
+      jb.row_bytes = jb.n * esize;
+      jb.rows = 1;
       jb.block = d->block;
       jb.num_blocks = d->num_blocks;
       jb.checks = d->checks;
@@ -191,22 +209,15 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
       jb.a = static_cast<const uint16_t*>(d->a);
       jb.partial_cx = d->partial_cx;
       jb.partial_s = d->partial_s;
-      jb.row_units = s.has_w ? d->block : 0;
-      jb.period_units = jb.row_units + static_cast<int64_t>(d->checks + 1) * jb.segs;
-      jb.period_bytes = (s.has_w ? d->block * jb.row_bytes : 0) + (4LL * d->checks + 2) * d->n;
+      jb.row_units = 0;
+      jb.period_units = static_cast<int64_t>(d->checks + 1) * jb.segs;
+      jb.period_bytes = (4LL * d->checks + 2) * d->n;
       jb.units = jb.period_units * d->num_blocks;
       jb.total_bytes = jb.period_bytes * d->num_blocks;
-    } else {
-      jb.row_units = static_cast<int32_t>(jb.m);
-      jb.period_units = 1;
-      jb.period_bytes = jb.row_bytes;
-      jb.units = jb.m;
-      jb.total_bytes = jb.m * jb.row_bytes;
+      x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 2);
+      plan.jobs[nj++] = jb;
+      bytes.push_back(static_cast<double>(jb.total_bytes) * kBankCost);
     }
-    if (s.has_w) max_row_bytes = std::max<int64_t>(max_row_bytes, jb.row_bytes);
-    x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 2);
-    plan.jobs[nj++] = jb;
-    bytes.push_back(jb.total_bytes);
   }
 
   // Columns reduced together; a batch wider than that re-reads each row from its slot, so
@@ -247,7 +258,8 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs
   // in proportion to their bytes, at least one each and never more than their units.
   const int sms = sm_count();
-  int64_t total_units = 0, total_bytes = 0;
+  int64_t total_units = 0;
+  double total_bytes = 0.0;
   for (int j = 0; j < nj; ++j) {
     total_units += plan.jobs[j].units;
     total_bytes += bytes[j];
@@ -256,7 +268,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   std::vector<int64_t> cnt(nj);
   int64_t assigned = 0;
   for (int j = 0; j < nj; ++j) {
-    const double share = static_cast<double>(want) * static_cast<double>(bytes[j]) / static_cast<double>(total_bytes);
+    const double share = static_cast<double>(want) * bytes[j] / total_bytes;
     cnt[j] = std::min<int64_t>(std::max<int64_t>(1, static_cast<int64_t>(share)), plan.jobs[j].units);
     assigned += cnt[j];
   }
@@ -265,7 +277,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
     int best = -1;
     double load = -1.0;
     for (int j = 0; j < nj; ++j) {
-      const double l = static_cast<double>(bytes[j]) / static_cast<double>(cnt[j]);
+      const double l = bytes[j] / static_cast<double>(cnt[j]);
       if (cnt[j] < plan.jobs[j].units && l > load) {
         best = j;
         load = l;
@@ -282,7 +294,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
     int best = -1;
     double load = 1e300;
     for (int j = 0; j < nj; ++j) {
-      const double l = static_cast<double>(bytes[j]) / static_cast<double>(cnt[j] - 1 > 0 ? cnt[j] - 1 : 1);
+      const double l = bytes[j] / static_cast<double>(cnt[j] - 1 > 0 ? cnt[j] - 1 : 1);
       if (cnt[j] > 1 && l < load) {
         best = j;
         load = l;

@@ -656,8 +656,6 @@ __device__ __forceinline__ void segment_piece(double* acc, uint32_t piece, uint3
   }
 }
 
-// Exponent fields (bfloat16 bits 7-14) of the activations: smallest over nonzero values
-// (subnormals count as 1) and largest over all.
 // Copies the activations X (batch * n bfloat16, a multiple of 16 bytes, 16-byte aligned)
 // into shared memory with one 16-byte load per thread and step, through L2 (X may have been
 // written by the kernel this one waited for), and merges the smallest nonzero (subnormals
@@ -883,19 +881,26 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   PieceWalk issue;
   walk_to(issue, jb, u0, warp, count, row_piece, seg_piece);
   int64_t issued = 0;
-  for (int s = 0; s < slots && issue.pieces > 0; ++s) {
-    if (lane == 0) {
-      const Unit iu = walk_unit(issue, jb, u0);
-      const uint32_t off = static_cast<uint32_t>(issue.piece) * issue.size;
-      const uint32_t bytes = min(issue.size, iu.bytes - off);
-      mbar_arrive_expect_tx(full + s, bytes);
-      bulk_load(ring + static_cast<int64_t>(s) * slot_bytes, static_cast<const uint8_t*>(iu.src) + off, bytes,
-                full + s, once);
+  auto prime = [&](int upto) {
+    for (; issued < upto && issue.pieces > 0; ++issued) {
+      const int s = static_cast<int>(issued);
+      if (lane == 0) {
+        const Unit iu = walk_unit(issue, jb, u0);
+        const uint32_t off = static_cast<uint32_t>(issue.piece) * issue.size;
+        const uint32_t bytes = min(issue.size, iu.bytes - off);
+        mbar_arrive_expect_tx(full + s, bytes);
+        bulk_load(ring + static_cast<int64_t>(s) * slot_bytes, static_cast<const uint8_t*>(iu.src) + off, bytes,
+                  full + s, once);
+      }
+      walk_next(issue, jb, u0, count, row_piece, seg_piece);
     }
-    ++issued;
-    walk_next(issue, jb, u0, count, row_piece, seg_piece);
-  }
+  };
+  // A few slots before the producers are waited for (weights are never written by a kernel
+  // of this library); the rest after the activations, whose loads would otherwise queue
+  // behind the whole ring's worth of weight requests.
+  prime(min(slots, kPreSlots));
   const int fma_mode = before_inputs();
+  prime(slots);
   if (fma_mode < 0) {  // leave only after the copies into this warp's slots have landed
     for (int64_t i = 0; i < issued; ++i) mbar_wait(full + i, 0);
     return;

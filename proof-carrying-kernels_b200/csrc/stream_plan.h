@@ -1,16 +1,19 @@
 // Launch plan of the persistent streaming kernel (host and device view).
 //
-// A launch processes up to kMaxJobs jobs. A job is a GEMV over W (m, n) with activations
-// X (batch, n) and outputs Y (batch, m), a check of one GEMV output against its checksum
-// bank, or both (a checked GEMV). Its work is a sequence of "units", each a contiguous
-// byte range that the CTA's consumer warps reduce against the activations together:
+// A launch processes up to kMaxPlanJobs jobs. A job is a GEMV over W (m, n) with
+// activations X (batch, n) and outputs Y (batch, m), or the bank part of a check of one
+// GEMV output (a checked GEMV is planned as one job of each kind, over the same X). Its work
+// is a sequence of "units", each a contiguous byte range that the CTA's consumer warps
+// reduce against the activations together:
 //   - R consecutive W rows                         -> y[b, row] for every column b
 //   - a segment of a checksum row c[k, beta, :]    -> partial c . x_b (binary64)
 //   - a segment of a bound row a[beta, :]          -> partial a . |x_b| (binary64, up)
-// For a checked job the units of row block beta are laid out contiguously:
-//   [ceil(block / R) row units (fused only)] [checks x segs c-units] [segs a-units]
-// The segment units leave binary64 partial sums; the verdict kernel (verdict_plan.h) turns
-// them, with y as stored, into the block decisions once this kernel has finished.
+// For a check the units of row block beta are laid out contiguously:
+//   [checks x segs c-units] [segs a-units]
+// (the layout also admits a block's row units in front of them, which the host no longer
+// plans). The segment units leave binary64 partial sums; the verdict kernel
+// (verdict_plan.h) turns them, with y as stored, into the block decisions once this kernel
+// has finished.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -20,7 +23,8 @@
 
 namespace pck {
 
-constexpr int kMaxJobs = 16;
+constexpr int kMaxJobs = 16;                 // GEMVs or checks a caller passes to one launch
+constexpr int kMaxPlanJobs = 2 * kMaxJobs;   // a checked GEMV is planned as two jobs
 constexpr int kConsumerWarps = 16;
 constexpr int kTmaThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kPlainThreads = kConsumerWarps * 32;
@@ -28,6 +32,7 @@ constexpr int kMaxStages = 32;
 constexpr int kSmemCap = 232448;  // 227 KB: the opt-in dynamic shared memory per CTA
 constexpr int kMaxBatch = 16;
 constexpr int kSegBatch = 4;  // staged path: batch columns of a checked job (more: plain path)
+constexpr int kPreSlots = 1;  // staged path: ring slots a warp fills before waiting for producers
 constexpr int kWeightsBf16 = 0;
 constexpr int kWeightsE4m3 = 1;
 
@@ -70,7 +75,7 @@ struct JobPlan {
 };
 
 struct Plan {
-  JobPlan jobs[kMaxJobs];
+  JobPlan jobs[kMaxPlanJobs];
   int32_t njobs;
   int32_t stages;       // staged path: ring slots per warp
   int32_t stage_bytes;  // staged path: bytes per slot
