@@ -211,6 +211,31 @@ int pck_gemv_checked_static(const pck_gemv_job* jobs, int count, void* stream);
 int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m, int64_t n,
                    int block, int checks, double sum_up_factor, void* stream);
 
+/* ------------------------------------------------------------------------------------ */
+/* Sampled-token membership check.                                                        */
+
+#define PCK_LOGITS_F32 0
+#define PCK_LOGITS_BF16 1
+#define PCK_LOGITS_F16 2
+
+/*
+ * For every row b of logits (rows, vocab) (row b at logits + b*row_stride elements) and its
+ * sampled token tokens[b]: above[b] = #{j : l_j > l_t} (t clamped into range for the
+ * gather); ok[b] = no NaN in the row && 0 <= t < vocab && above < (greedy[b] ? 1 : k) with
+ * k = top_k[b] clamped to [1, vocab] (vocab when top_k is NULL); when top_p is not NULL,
+ * rows with p = top_p[b] < 1 also compute r = (mass of kept logits above l_t) / (mass of
+ * kept logits), kept = logits >= the k-th largest, with binary32 terms e^(l - max) from the
+ * exact TwoSum split summed in binary64, and require p >= 1 || greedy || r <
+ * nextafter(p + slack, +inf); mass_above[b] = r there, else 0. `slack` is
+ * next_up(tol + member_eps32(vocab)) (src/pck/member.py:84-102). greedy may be NULL.
+ * Replaces the torch implementation `check_members` (src/pck/member.py:118-197), which
+ * the reference runs as some 80 kernel launches; here one launch, one CTA per row.
+ */
+int pck_member_check(const void* logits, int logits_dtype, int64_t rows, int64_t vocab,
+                     int64_t row_stride, const int64_t* tokens, const int64_t* top_k,
+                     const double* top_p, const uint8_t* greedy, double slack, uint8_t* ok,
+                     int64_t* above, double* mass_above, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

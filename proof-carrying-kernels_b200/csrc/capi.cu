@@ -11,6 +11,7 @@
 #include <string>
 #include <vector>
 
+#include "member_plan.h"
 #include "pck_b200.h"
 #include "stream_plan.h"
 #include "verdict_plan.h"
@@ -508,6 +509,41 @@ int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m,
   const cudaError_t err = pck::launch_bank_build(W, r, c, a, n, block, static_cast<int>(nb), checks,
                                                  sum_up_factor, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("bank kernel", err);
+  return ok();
+}
+
+int pck_member_check(const void* logits, int logits_dtype, int64_t rows, int64_t vocab,
+                     int64_t row_stride, const int64_t* tokens, const int64_t* top_k,
+                     const double* top_p, const uint8_t* greedy, double slack, uint8_t* ok_out,
+                     int64_t* above, double* mass_above, void* stream) {
+  if (logits_dtype != PCK_LOGITS_F32 && logits_dtype != PCK_LOGITS_BF16 && logits_dtype != PCK_LOGITS_F16) {
+    return fail(PCK_ERR_ARGUMENT, "unknown logits dtype %d", logits_dtype);
+  }
+  if (rows < 0 || vocab < 1) return fail(PCK_ERR_ARGUMENT, "expected logits of shape (B, V) with V >= 1");
+  if (row_stride < vocab) return fail(PCK_ERR_ARGUMENT, "row stride %lld is below the vocabulary %lld",
+                                      static_cast<long long>(row_stride), static_cast<long long>(vocab));
+  if (rows > 0x7fffffffLL) return fail(PCK_ERR_UNSUPPORTED, "too many rows (%lld)", static_cast<long long>(rows));
+  if (!(slack >= 0)) return fail(PCK_ERR_ARGUMENT, "slack must be non-negative");
+  if (rows == 0) return ok();
+  if (!logits || !tokens || !ok_out || !above || !mass_above) {
+    return fail(PCK_ERR_ARGUMENT, "logits, tokens and the outputs must not be NULL");
+  }
+  pck::MemberArgs args{};
+  args.logits = logits;
+  args.rows = rows;
+  args.vocab = vocab;
+  args.row_stride = row_stride;
+  args.dtype = logits_dtype;
+  args.tokens = tokens;
+  args.top_k = top_k;
+  args.top_p = top_p;
+  args.greedy = greedy;
+  args.slack = slack;
+  args.ok = ok_out;
+  args.above = above;
+  args.mass_above = mass_above;
+  const cudaError_t err = pck::launch_member_check(args, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail("membership kernel", err);
   return ok();
 }
 
