@@ -212,6 +212,27 @@ int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m,
                    int block, int checks, double sum_up_factor, void* stream);
 
 /* ------------------------------------------------------------------------------------ */
+/* Top-k / top-p set check of a sampler's selection.                                       */
+
+/*
+ * For row b of logits (rows, vocab) (binary32) and the selection selected[b, :lengths[b]]
+ * (selected is (rows, max_len) int64): passed[b] = the selection is well formed (length in
+ * [1, max_len], at most vocab, distinct ids in range, and equal to k when top_p is 0), no
+ * logit is NaN, and min over selected >= max over rejected; when top_p is nonzero also
+ * mass >= p - slack and mass_without_smallest < p + slack, masses of the softmax at
+ * `temperature` from binary32 expf terms on an exact split argument summed in binary64.
+ * min_selected, max_rejected, mass and without (mass less the smallest selected term) are
+ * written per row (masses 0 unless computed). `segments` in [1, vocab] splits a row between
+ * up to 8 CTAs (one cluster); verdicts do not depend on it. `slack` comes from the caller
+ * (src/pck/cuda/sampling.py:62-90). No scratch memory. Replaces bindings.cpp:260-300
+ * (`sampling_check`) and src/pck/cuda/csrc/sampling_kernel.cu:38-229.
+ */
+int pck_sampling_check(const float* logits, const int64_t* selected, const int64_t* lengths, int64_t rows,
+                       int64_t vocab, int64_t max_len, int64_t k, int top_p, double p, double temperature,
+                       double slack, int64_t segments, uint8_t* passed, float* min_selected,
+                       float* max_rejected, double* mass, double* without, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
 /* Sampled-token membership check.                                                        */
 
 #define PCK_LOGITS_F32 0

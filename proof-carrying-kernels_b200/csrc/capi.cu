@@ -13,6 +13,7 @@
 
 #include "member_plan.h"
 #include "pck_b200.h"
+#include "sampling_plan.h"
 #include "stream_plan.h"
 #include "verdict_plan.h"
 
@@ -544,6 +545,52 @@ int pck_member_check(const void* logits, int logits_dtype, int64_t rows, int64_t
   args.mass_above = mass_above;
   const cudaError_t err = pck::launch_member_check(args, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("membership kernel", err);
+  return ok();
+}
+
+int pck_sampling_check(const float* logits, const int64_t* selected, const int64_t* lengths, int64_t rows,
+                       int64_t vocab, int64_t max_len, int64_t k, int top_p, double p, double temperature,
+                       double slack, int64_t segments, uint8_t* passed, float* min_selected,
+                       float* max_rejected, double* mass, double* without, void* stream) {
+  if (rows < 1 || vocab < 1 || max_len < 1) return fail(PCK_ERR_ARGUMENT, "empty input");
+  if (rows > 65535) return fail(PCK_ERR_ARGUMENT, "too many rows");
+  if (segments < 1 || segments > vocab) {
+    return fail(PCK_ERR_ARGUMENT, "segments must be in [1, V], got %lld", static_cast<long long>(segments));
+  }
+  if (!(temperature > 0) || !(slack >= 0)) {
+    return fail(PCK_ERR_ARGUMENT, "temperature must be positive, slack >= 0");
+  }
+  if (!logits || !selected || !lengths || !passed || !min_selected || !max_rejected || !mass || !without) {
+    return fail(PCK_ERR_ARGUMENT, "pointers must not be NULL");
+  }
+  // The segments only choose how many CTAs (at most one cluster) share a row.
+  const int64_t cluster = std::min<int64_t>({segments, pck::kSamplingMaxCluster, (vocab + 31) / 32});
+  int64_t slice = (vocab + cluster - 1) / cluster;
+  slice = (slice + 31) / 32 * 32;
+  if (pck::sampling_smem_bytes(slice) > pck::kSamplingSmemCap) {
+    return fail(PCK_ERR_UNSUPPORTED, "vocabulary of %lld is beyond this build's %d slices of shared memory",
+                static_cast<long long>(vocab), pck::kSamplingMaxCluster);
+  }
+  pck::SamplingArgs args{};
+  args.logits = logits;
+  args.selected = selected;
+  args.lengths = lengths;
+  args.rows = rows;
+  args.vocab = vocab;
+  args.max_len = max_len;
+  args.k = k;
+  args.slice = slice;
+  args.top_p = top_p ? 1 : 0;
+  args.p = p;
+  args.temperature = temperature;
+  args.slack = slack;
+  args.passed = passed;
+  args.min_selected = min_selected;
+  args.max_rejected = max_rejected;
+  args.mass = mass;
+  args.without = without;
+  const cudaError_t err = pck::launch_sampling_check(args, static_cast<int>(cluster), static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail("sampling checker", err);
   return ok();
 }
 

@@ -13,14 +13,25 @@ from pck.cuda.checker import (
     round_up_bf16,
 )
 from pck.cuda.gemv import gemv_coalesced, gemv_fp8, gemv_naive, quantize_fp8
+from pck.cuda.sampling import (
+    SamplingCheck,
+    check_topk_gpu,
+    check_topp_gpu,
+    sharded_topk_gpu,
+    topk_sample,
+    topp_select,
+)
 
 __all__ = [
     "DEFAULT_BLOCK",
     "CheckResult",
     "GpuBlockedChecker",
     "PendingCheck",
+    "SamplingCheck",
     "SideStreamChecker",
     "check_many",
+    "check_topk_gpu",
+    "check_topp_gpu",
     "checked_gemvs",
     "device_status",
     "gemv_checked",
@@ -29,4 +40,7 @@ __all__ = [
     "gemv_naive",
     "quantize_fp8",
     "round_up_bf16",
+    "sharded_topk_gpu",
+    "topk_sample",
+    "topp_select",
 ]
