@@ -127,13 +127,16 @@ def build_layer(args, rank: int, world: int, device: torch.device):
     """Sharded weights, inputs, checkers and the launch objects of one decode layer."""
     from pck.cuda import GpuBlockedChecker
     from pck.cuda.plan import LLAMA3_8B_GROUPS, GemvLaunch, VerdictLaunch
-    from pck.cuda.sharded import PackedOutputs, shard_rows
+    from pck.cuda.sharded import Exchange, shard_rows
     from pck.fp import tree_height
 
     names = [p for g in LLAMA3_8B_GROUPS for p in g]
-    ys = PackedOutputs([m for _, m, _ in names], args.block, world, rank, device, batch=args.batch)
-    vs = PackedOutputs([m // args.block for _, m, _ in names], 1, world, rank, device, batch=args.checks,
-                       dtype=torch.bool)  # fmt: skip
+    ms = [m for _, m, _ in names]
+    # one all-gather per step moves the outputs and the verdict bits of every projection
+    ex = Exchange([(ms, args.block, args.batch, torch.float32),
+                   ([m // args.block for m in ms], 1, args.checks, torch.bool)], world, rank, device)  # fmt: skip
+    ex_plain = Exchange([(ms, args.block, args.batch, torch.float32)], world, rank, device)
+    ys, vs = ex.parts
     gen = torch.Generator().manual_seed(0)
     groups, plain, xs, j = [], [], [], 0
     for group in LLAMA3_8B_GROUPS:
@@ -141,7 +144,7 @@ def build_layer(args, rank: int, world: int, device: torch.device):
         x = outlier_x(n, args.batch, gen).to(device)
         x = x[0].contiguous() if args.batch == 1 else x.contiguous()
         xs.append(x)
-        items, items_plain, y_views, p_views = [], [], [], []
+        items, items_plain, y_views, p_views, y_plain = [], [], [], [], []
         for _name, m, nn in group:
             shard = shard_rows(m, args.block, world, rank)
             dgen = torch.Generator(device=device).manual_seed(1000 + j)
@@ -153,12 +156,13 @@ def build_layer(args, rank: int, world: int, device: torch.device):
             items_plain.append((W, x, None))
             y_views.append(ys.local_view(j))
             p_views.append(vs.local_view(j))
+            y_plain.append(ex_plain.parts[0].local_view(j))
             j += 1
         groups.append(GemvLaunch(items, args.threads, ys=y_views, passed=p_views, verdicts=False))
-        plain.append(GemvLaunch(items_plain, args.threads))
+        plain.append(GemvLaunch(items_plain, args.threads, ys=y_plain))
     verdict = VerdictLaunch(groups)
     torch.cuda.synchronize()
-    return groups, verdict, plain, xs, ys, vs
+    return groups, verdict, plain, xs, ex, ex_plain
 
 
 def cuda_graph(fn) -> torch.cuda.CUDAGraph:
@@ -199,12 +203,11 @@ def timed(graph: torch.cuda.CUDAGraph, steps: int, warmup: int, world: int) -> f
     return ms / 1e3 / steps
 
 
-def e2e_step_time(groups, xs, ys, vs, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
+def e2e_step_time(groups, xs, ex, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
     """The public launch API with host buffers: every step copies the layer's activations
     from pinned host memory, launches, gathers and copies outputs and verdicts back."""
     hx = [x.cpu().pin_memory() for x in xs]
-    hy = torch.empty(ys.gathered.shape, dtype=ys.gathered.dtype, pin_memory=True)
-    hv = torch.empty(vs.gathered.shape, dtype=vs.gathered.dtype, pin_memory=True)
+    hout = torch.empty(ex.gathered.shape, dtype=ex.gathered.dtype, pin_memory=True)
 
     def step() -> None:
         for x, h in zip(xs, hx, strict=True):
@@ -212,13 +215,10 @@ def e2e_step_time(groups, xs, ys, vs, steps: int, warmup: int, world: int) -> tu
         for g in groups:
             g.launch()
         if world > 1:
-            ys.gather()
-            vs.gather()
+            ex.gather()
         else:
-            ys.gathered.copy_(ys.local)
-            vs.gathered.copy_(vs.local)
-        hy.copy_(ys.gathered, non_blocking=True)
-        hv.copy_(vs.gathered, non_blocking=True)
+            ex.gathered.copy_(ex.local)
+        hout.copy_(ex.gathered, non_blocking=True)
 
     for _ in range(warmup):
         step()
@@ -237,7 +237,7 @@ def e2e_step_time(groups, xs, ys, vs, steps: int, warmup: int, world: int) -> tu
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
     h2d = sum(h.numel() * h.element_size() for h in hx)
-    d2h = hy.numel() * hy.element_size() + hv.numel() * hv.element_size()
+    d2h = hout.numel() * hout.element_size()
     return ms / 1e3 / steps, h2d, d2h
 
 
@@ -344,7 +344,8 @@ def main() -> None:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)  # fmt: skip
 
-    groups, verdict, plain, xs, ys, vs = build_layer(args, rank, world, device)
+    groups, verdict, plain, xs, ex, ex_plain = build_layer(args, rank, world, device)
+    vs = ex.parts[1]
     launches = [*groups, verdict]
     step_bytes_local = sum(g.algorithmic_bytes for g in groups)
 
@@ -352,12 +353,13 @@ def main() -> None:
         for g in launches:
             g.launch()
         if world > 1:
-            ys.gather()
-            vs.gather()
+            ex.gather()
 
     def plain_step() -> None:
         for g in plain:
             g.launch()
+        if world > 1:
+            ex_plain.gather()
 
     graph_checked = cuda_graph(checked_step)
     graph_plain = cuda_graph(plain_step)
@@ -377,7 +379,7 @@ def main() -> None:
         t_checked = timed(graph_checked, args.steps, args.warmup, world)
         t_plain = timed(graph_plain, args.steps, args.warmup, world)
     clock = clocks.summary()
-    t_e2e, h2d, d2h = e2e_step_time(launches, xs, ys, vs, max(20, args.steps // 10), args.warmup, world)
+    t_e2e, h2d, d2h = e2e_step_time(launches, xs, ex, max(20, args.steps // 10), args.warmup, world)
 
     total_bytes = torch.tensor([float(step_bytes_local)], device=device)
     if world > 1:
