@@ -211,6 +211,18 @@ int pck_gemv_checked_static(const pck_gemv_job* jobs, int count, void* stream);
 int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m, int64_t n,
                    int block, int checks, double sum_up_factor, void* stream);
 
+/*
+ * Batched GEMV on the tensor cores (tcgen05) for decode batches of 16 to 256: Y (batch, m) =
+ * X (batch, n) W^T for up to 8 jobs sharing the batch, bfloat16 W and X (16-byte aligned,
+ * n a multiple of 8), binary32 outputs accumulated in tensor memory. Not bit-exact to the
+ * coalesced tree: the tensor core adds 16 exact products per MMA and n/16 MMAs in sequence,
+ * so a checker of these outputs takes that accumulation's declared height
+ * (pck.cuda.gemv.tc_height). `threads`, the exponent range and `check` of each job are
+ * unused (check must be NULL). The reference has no counterpart; its batched decode runs
+ * batch-1 GEMVs (harness/csrc/batched_gemv.cu:25-82 is a CUDA-core diagnostic).
+ */
+int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* Top-k / top-p set check of a sampler's selection.                                       */
 

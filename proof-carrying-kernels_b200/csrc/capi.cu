@@ -1,6 +1,8 @@
 // extern "C" entry points of libpck_b200.so (declared in include/pck_b200.h): argument
 // validation, launch planning and dispatch. Messages of rejected calls follow the
 // reference bindings' wording (src/pck/cuda/csrc/bindings.cpp) so callers can match them.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -14,6 +16,7 @@
 #include "member_plan.h"
 #include "pck_b200.h"
 #include "sampling_plan.h"
+#include "tc_plan.h"
 #include "stream_plan.h"
 #include "verdict_plan.h"
 
@@ -362,6 +365,34 @@ int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t str
   return ok();
 }
 
+// cuTensorMapEncodeTiled from the driver, through the runtime (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  }
+  return fn;
+}
+
+// A 2-D bfloat16 tensor map over rows x cols (row-major), box 64 columns x box_rows rows,
+// 128-byte swizzle, zero fill outside.
+bool encode_bf16_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(pck::kTcTileK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int check_gemv_args(const void* W, const void* x, const float* y, int64_t m, int64_t n,
                     int threads, int min_threads) {
   if (m < 0 || n < 0) return fail(PCK_ERR_ARGUMENT, "expected W of shape (m, n) with m, n >= 0");
@@ -386,7 +417,7 @@ int pck_device_status(unsigned int* status, int clear) {
   cudaError_t err = cudaDeviceSynchronize();
   if (err != cudaSuccess) return cuda_fail("device synchronize", err);
   unsigned int total = 0;
-  for (auto* reader : {pck::status_stream_bf16, pck::status_stream_e4m3}) {
+  for (auto* reader : {pck::status_stream_bf16, pck::status_stream_e4m3, pck::tc_status}) {
     unsigned int v = 0;
     err = reader(&v, clear != 0);
     if (err != cudaSuccess) return cuda_fail("status read", err);
@@ -591,6 +622,62 @@ int pck_sampling_check(const float* logits, const int64_t* selected, const int64
   args.without = without;
   const cudaError_t err = pck::launch_sampling_check(args, static_cast<int>(cluster), static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("sampling checker", err);
+  return ok();
+}
+
+int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
+  if (count < 1 || count > pck::kTcMaxJobs || !jobs) {
+    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", pck::kTcMaxJobs, count);
+  }
+  pck::TcPlan plan{};
+  const int batch = jobs[0].batch;
+  if (batch < 1 || batch > pck::kTcMaxBatch) {
+    return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %d", pck::kTcMaxBatch, batch);
+  }
+  int tiles = 0, nj = 0;
+  for (int i = 0; i < count; ++i) {
+    const pck_gemv_job& jb = jobs[i];
+    if (jb.weight_format != PCK_WEIGHTS_BF16) {
+      return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV takes bfloat16 weights only");
+    }
+    if (jb.check) return fail(PCK_ERR_ARGUMENT, "the tensor-core GEMV takes no fused check");
+    if (jb.batch != batch) return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the batch");
+    if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, 256, 1)) return rc;
+    if (jb.m == 0) continue;
+    if (jb.n % 8 != 0 || !aligned16(jb.W) || !aligned16(jb.X)) {
+      return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV needs n a multiple of 8 and 16-byte aligned W and X");
+    }
+    if (jb.m > (1LL << 31) - pck::kTcTileM || jb.n > (1LL << 31)) return fail(PCK_ERR_UNSUPPORTED, "matrix too large");
+    pck::TcJob& tj = plan.jobs[nj];
+    const int n_pad = (batch + 15) / 16 * 16;
+    if (!encode_bf16_map(&tj.w_map, jb.W, jb.m, jb.n, pck::kTcTileM) ||
+        !encode_bf16_map(&tj.x_map, jb.X, batch, jb.n, n_pad)) {
+      return fail(PCK_ERR_CUDA, "tensor map encoding failed");
+    }
+    tj.Y = jb.Y;
+    tj.m = jb.m;
+    tj.n = jb.n;
+    tj.tile_begin = tiles;
+    tj.tiles = static_cast<int32_t>((jb.m + pck::kTcTileM - 1) / pck::kTcTileM);
+    tiles += tj.tiles;
+    ++nj;
+  }
+  if (nj == 0) return ok();
+  plan.njobs = nj;
+  plan.total_tiles = tiles;
+  plan.batch = batch;
+  plan.n_pad = (batch + 15) / 16 * 16;
+  const size_t stage = pck::tc_stage_bytes(plan.n_pad);
+  plan.stages = static_cast<int32_t>(std::min<size_t>(8, (232448 - 1024 - 256) / stage));
+  // Every epilogue read takes 32 columns, so each accumulator spans a multiple of 32.
+  plan.acc_stride = (plan.n_pad + 31) / 32 * 32;
+  int cols = 32;
+  while (cols < 2 * plan.acc_stride) cols *= 2;
+  plan.tmem_cols = cols;
+  const size_t smem = 1024 + static_cast<size_t>(plan.stages) * stage + 256;
+  const unsigned grid = static_cast<unsigned>(std::min(tiles, sm_count()));
+  const cudaError_t err = pck::launch_tc(plan, grid, smem, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail("tensor-core gemv kernel", err);
   return ok();
 }
 

@@ -12,7 +12,7 @@ from pck.cuda.checker import (
     gemv_checked,
     round_up_bf16,
 )
-from pck.cuda.gemv import gemv_coalesced, gemv_fp8, gemv_naive, quantize_fp8
+from pck.cuda.gemv import gemv_coalesced, gemv_fp8, gemv_naive, gemv_tc, quantize_fp8, tc_height
 from pck.cuda.sampling import (
     SamplingCheck,
     check_topk_gpu,
@@ -38,8 +38,10 @@ __all__ = [
     "gemv_coalesced",
     "gemv_fp8",
     "gemv_naive",
+    "gemv_tc",
     "quantize_fp8",
     "round_up_bf16",
+    "tc_height",
     "sharded_topk_gpu",
     "topk_sample",
     "topp_select",

@@ -46,3 +46,53 @@ def gemv_fp8(Q: torch.Tensor, x: torch.Tensor, threads: int = 256) -> torch.Tens
     per 16-byte vector, bit-identical to `emulate_gemv_coalesced(Q, x, threads, 16)`
     (src/pck/cuda/gemv.py:51-58). The scales are applied by the caller: y = s * z."""
     return extension().gemv_fp8(Q, x, threads)
+
+
+TC_STEP_ROUNDINGS = 8
+"""Roundings charged per tensor-core MMA step in `tc_height` (see there)."""
+
+
+def tc_height(n: int) -> int:
+    """Declared height of the tensor-core accumulation of `gemv_tc`, for its checker.
+
+    Each tcgen05.mma adds 16 exact bfloat16 products to the binary32 accumulator, and the
+    n / 16 MMAs of an output run in sequence. The hardware's internal rounding of one such
+    step is not documented; this build assumes it is within ``TC_STEP_ROUNDINGS`` unit
+    roundoffs of |accumulator| + sum |products| (published measurements of earlier tensor
+    cores show at most 2 ulp of the largest addend, i.e. 4 u32, from truncating the
+    aligned sum), so the whole chain is bounded by gamma_h with
+    h = TC_STEP_ROUNDINGS * (ceil(n / 16) + 1). The GPU tests check every output against
+    that bound and the checker for zero false alarms.
+    """
+    if n < 1:
+        raise ValueError(f"n must be positive, got {n}")
+    return TC_STEP_ROUNDINGS * (-(-n // 16) + 1)
+
+
+def gemv_tc(W: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
+    """Y (B, m) = X (B, n) W^T on the tensor cores for a decode batch of 1 to 256 columns:
+    bfloat16 W (m, n) and X (B, n), both contiguous and 16-byte aligned with n a multiple of
+    8; binary32 Y. Not bit-exact to the coalesced tree (see `tc_height` for its checker)."""
+    import ctypes
+
+    from pck.cuda import _lib
+    from pck.cuda._ext import on_device, stream_handle
+
+    if not (W.is_cuda and X.is_cuda and W.device == X.device):
+        raise RuntimeError("W and X must be CUDA tensors on one device")
+    if W.dtype != torch.bfloat16 or X.dtype != torch.bfloat16:
+        raise RuntimeError("W and X must be bfloat16")
+    if W.dim() != 2 or X.dim() != 2 or X.size(1) != W.size(1):
+        raise RuntimeError("expected W of shape (m, n) and X of shape (B, n)")
+    if not (W.is_contiguous() and X.is_contiguous()):
+        raise RuntimeError("W and X must be contiguous")
+    Y = torch.empty((X.size(0), W.size(0)), dtype=torch.float32, device=W.device)
+    job = (_lib.GemvJob * 1)()
+    job[0].W, job[0].X, job[0].Y = W.data_ptr(), X.data_ptr(), Y.data_ptr()
+    job[0].m, job[0].n, job[0].batch, job[0].threads = W.size(0), W.size(1), X.size(0), 256
+    job[0].weight_format = _lib.PCK_WEIGHTS_BF16
+    job[0].check = ctypes.POINTER(_lib.CheckDesc)()
+    with on_device(W.device):
+        rc = _lib.library().pck_gemv_tc(job, 1, stream_handle(W.device))
+    _lib.check(rc, "tensor-core gemv kernel")
+    return Y

@@ -1,0 +1,106 @@
+"""The tensor-core batched GEMV (tcgen05): every output within the declared accumulation bound
+of the exact product, the blocked checker built with `tc_height` raises no false alarm on
+its outputs and catches planted faults."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from tests.golden import inputs
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
+
+U32 = 2.0**-24
+
+
+def problem(m: int, n: int, batch: int, seed: int):
+    W, _ = inputs.torch_problem(m, n, seed=seed)
+    gen = torch.Generator().manual_seed(seed + 1)
+    X = torch.randn(batch, n, generator=gen)
+    X[:, torch.randperm(n, generator=gen)[: max(1, n // 100)]] *= 20.0  # outlier channels
+    return W.cuda(), X.bfloat16().cuda()
+
+
+def bound_ratio(W: torch.Tensor, X: torch.Tensor, Y: torch.Tensor) -> float:
+    """max |Y - exact| / (gamma_h(u32) sum |w||x|) over all outputs (<= 1 within the bound)."""
+    from pck.cuda import tc_height
+    from pck.fp import gamma
+
+    W64, X64 = W.double(), X.double()
+    exact = X64 @ W64.T
+    mag = X64.abs() @ W64.abs().T
+    err = (Y.double() - exact).abs()
+    g = gamma(tc_height(W.size(1)), U32)
+    ratio = err / (g * mag).clamp(min=1e-300)
+    return float(ratio.max())
+
+
+@pytest.mark.parametrize(("m", "n", "batch"), [(128, 64, 16), (128, 4096, 64), (300, 1000, 50), (1024, 4096, 128),
+                                               (512, 4096, 256), (128, 14336, 16), (640, 2048, 1)])  # fmt: skip
+def test_outputs_within_the_declared_bound(m: int, n: int, batch: int) -> None:
+    from pck.cuda import gemv_tc
+
+    W, X = problem(m, n, batch, seed=m + n + batch)
+    Y = gemv_tc(W, X)
+    assert Y.shape == (batch, m) and torch.isfinite(Y).all()
+    ratio = bound_ratio(W, X, Y)
+    print(f"tc bound ratio m={m} n={n} batch={batch}: {ratio:.3e}")
+    assert ratio <= 1.0
+    # and close to the product in plain terms
+    ref = (X.double() @ W.double().T).float()
+    torch.testing.assert_close(Y, ref, rtol=1e-3, atol=1e-3)
+
+
+def test_decode_layer_shapes_and_repeat_calls() -> None:
+    from pck.cuda import gemv_tc
+
+    for m, n in [(6144, 4096), (4096, 14336)]:
+        W, X = problem(m, n, 128, seed=m)
+        Y1 = gemv_tc(W, X)
+        Y2 = gemv_tc(W, X)
+        assert torch.equal(Y1, Y2)  # deterministic
+        assert bound_ratio(W, X, Y1) <= 1.0
+
+
+def test_checker_with_tc_height_no_false_alarm_and_catches_faults() -> None:
+    from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
+
+    m, n, batch = 1024, 4096, 128
+    W, X = problem(m, n, batch, seed=5)
+    Y = gemv_tc(W, X)
+    checker = GpuBlockedChecker(W, 128, tc_height(n), checks=2, generator=torch.Generator().manual_seed(0))
+    for b0 in range(0, batch, 16):
+        res = checker.check(X[b0 : b0 + 16].contiguous(), Y[b0 : b0 + 16].contiguous())
+        assert res.verdict.all()
+        assert float((res.rho.abs() / res.tau).max()) < 1.0
+    honest = checker.check(X[96:112].contiguous(), Y[96:112].contiguous())
+    bad = Y.clone()
+    bad.view(torch.int32)[7, 300] ^= 1 << 30  # exponent flip
+    bad[100, 777] += 4.0 * float(honest.tau[4, :, 777 // 128].max())  # 4 tau: above the 2 tau guarantee
+    res = checker.check(X[0:16].contiguous(), bad[0:16].contiguous())
+    assert not res.verdict[7, 300 // 128]
+    res = checker.check(X[96:112].contiguous(), bad[96:112].contiguous())
+    assert not res.verdict[4, 777 // 128]
+
+
+def test_rejects_unsupported_inputs() -> None:
+    from pck.cuda import gemv_tc
+
+    W, X = problem(128, 64, 16, seed=1)
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        gemv_tc(W.float(), X)
+    with pytest.raises(RuntimeError, match="batch"):
+        gemv_tc(W, torch.zeros(257, 64, dtype=torch.bfloat16, device="cuda"))
+    W2, X2 = problem(128, 60, 16, seed=2)
+    with pytest.raises(RuntimeError, match="multiple of 8"):
+        gemv_tc(W2, X2)
+    assert gemv_tc(W[:0], X).shape == (16, 0)
+
+
+def test_tc_height_is_conservative_in_the_chain_length() -> None:
+    from pck.cuda import tc_height
+
+    assert tc_height(16) == 16 and tc_height(4096) == 8 * 257 and tc_height(4097) == 8 * 258
+    assert np.all(np.diff([tc_height(n) for n in range(1, 2000)]) >= 0)
