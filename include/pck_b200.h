@@ -217,9 +217,12 @@ int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m,
  * n a multiple of 8), binary32 outputs accumulated in tensor memory. Not bit-exact to the
  * coalesced tree: the tensor core adds 16 exact products per MMA and n/16 MMAs in sequence,
  * so a checker of these outputs takes that accumulation's declared height
- * (pck.cuda.gemv.tc_height). `threads`, the exponent range and `check` of each job are
- * unused (check must be NULL). The reference has no counterpart; its batched decode runs
- * batch-1 GEMVs (harness/csrc/batched_gemv.cu:25-82 is a CUDA-core diagnostic).
+ * (pck.cuda.gemv.tc_height). `threads` and the exponent range are unused. A job's `check`
+ * (optional; blocks of 128 rows, 1 to 8 checks, batch up to 256, the job's own X, Y and
+ * shape) is fused: the same kernel reduces each block's checksum and bound rows against the
+ * staged X tiles (binary64), and a verdict launch follows. The reference has no counterpart;
+ * its batched decode runs batch-1 GEMVs (harness/csrc/batched_gemv.cu:25-82 is a CUDA-core
+ * diagnostic).
  */
 int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream);
 

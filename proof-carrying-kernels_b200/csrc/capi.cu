@@ -329,7 +329,7 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
 
 // Launches the verdict kernel for `count` validated checks whose partial sums are (or will
 // be, earlier on the stream) in their scratch.
-int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream) {
+int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream, int fixed_segs = 0) {
   if (count < 1 || count > pck::kMaxVerdictJobs) {
     return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", pck::kMaxVerdictJobs, count);
   }
@@ -339,7 +339,11 @@ int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t str
     const pck_check_desc* d = descs[i];
     pck::VerdictJob& vj = plan.jobs[i];
     int64_t seg_len = 0;
-    pck::segment_split(d->n, d->segments, kSegmentTarget, &seg_len, &vj.segs);
+    if (fixed_segs > 0) {
+      vj.segs = fixed_segs;
+    } else {
+      pck::segment_split(d->n, d->segments, kSegmentTarget, &seg_len, &vj.segs);
+    }
     vj.y = d->y;
     vj.r = d->r;
     vj.partial_cx = d->partial_cx;
@@ -640,7 +644,6 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
     if (jb.weight_format != PCK_WEIGHTS_BF16) {
       return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV takes bfloat16 weights only");
     }
-    if (jb.check) return fail(PCK_ERR_ARGUMENT, "the tensor-core GEMV takes no fused check");
     if (jb.batch != batch) return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the batch");
     if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, 256, 1)) return rc;
     if (jb.m == 0) continue;
@@ -657,6 +660,33 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
     tj.Y = jb.Y;
     tj.m = jb.m;
     tj.n = jb.n;
+    if (jb.check) {
+      const pck_check_desc* d = jb.check;
+      if (!d->c || !d->a || !d->r || !d->partial_cx || !d->partial_s || !d->passed || !d->rho || !d->tau) {
+        return fail(PCK_ERR_ARGUMENT, "check descriptor has a NULL pointer");
+      }
+      if (d->x != jb.X || d->y != jb.Y || d->n != jb.n || d->batch != batch ||
+          static_cast<int64_t>(d->num_blocks) * d->block != jb.m) {
+        return fail(PCK_ERR_ARGUMENT, "a fused check must cover the job's own x, y and shape");
+      }
+      if (d->block != pck::kTcTileM) {
+        return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV fuses checks of %d-row blocks only", pck::kTcTileM);
+      }
+      if (d->checks < 1 || d->checks > pck::kTcMaxChecks) {
+        return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV fuses 1 to %d checks, got %d", pck::kTcMaxChecks, d->checks);
+      }
+      if (d->segments < 1) return fail(PCK_ERR_ARGUMENT, "segments must be in [1, n], got %d", d->segments);
+      if (!(d->coef > 0) || !(d->geps > 0) || !(d->tau_floor > 0)) {
+        return fail(PCK_ERR_ARGUMENT, "coef, geps and floor must be positive");
+      }
+      tj.has_check = 1;
+      tj.c = d->c;
+      tj.a = static_cast<const uint16_t*>(d->a);
+      tj.partial_cx = d->partial_cx;
+      tj.partial_s = d->partial_s;
+      tj.checks = d->checks;
+      tj.seg_alloc = d->segments;
+    }
     tj.tile_begin = tiles;
     tj.tiles = static_cast<int32_t>((jb.m + pck::kTcTileM - 1) / pck::kTcTileM);
     tiles += tj.tiles;
@@ -668,17 +698,24 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   plan.batch = batch;
   plan.n_pad = (batch + 15) / 16 * 16;
   const size_t stage = pck::tc_stage_bytes(plan.n_pad);
-  plan.stages = static_cast<int32_t>(std::min<size_t>(8, (232448 - 1024 - 256) / stage));
+  plan.stages = static_cast<int32_t>(std::min<size_t>(8, (232448 - 1024 - 256 - pck::kTcBankBytes) / stage));
   // Every epilogue read takes 32 columns, so each accumulator spans a multiple of 32.
   plan.acc_stride = (plan.n_pad + 31) / 32 * 32;
   int cols = 32;
   while (cols < 2 * plan.acc_stride) cols *= 2;
   plan.tmem_cols = cols;
-  const size_t smem = 1024 + static_cast<size_t>(plan.stages) * stage + 256;
+  const size_t smem = 1024 + static_cast<size_t>(plan.stages) * stage + 256 + pck::kTcBankBytes;
   const unsigned grid = static_cast<unsigned>(std::min(tiles, sm_count()));
   const cudaError_t err = pck::launch_tc(plan, grid, smem, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("tensor-core gemv kernel", err);
-  return ok();
+  // The block verdicts of the fused checks: one segment of partial sums per block.
+  const pck_check_desc* checks[pck::kTcMaxJobs];
+  int nc = 0;
+  for (int i = 0; i < count; ++i) {
+    if (jobs[i].check && jobs[i].m > 0) checks[nc++] = jobs[i].check;
+  }
+  if (nc == 0) return ok();
+  return run_verdicts(checks, nc, static_cast<cudaStream_t>(stream), 1);
 }
 
 }  // extern "C"

@@ -69,14 +69,20 @@ def tc_height(n: int) -> int:
     return TC_STEP_ROUNDINGS * (-(-n // 16) + 1)
 
 
-def gemv_tc(W: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
+def gemv_tc(W: torch.Tensor, X: torch.Tensor, checker=None):
     """Y (B, m) = X (B, n) W^T on the tensor cores for a decode batch of 1 to 256 columns:
     bfloat16 W (m, n) and X (B, n), both contiguous and 16-byte aligned with n a multiple of
-    8; binary32 Y. Not bit-exact to the coalesced tree (see `tc_height` for its checker)."""
+    8; binary32 Y. Not bit-exact to the coalesced tree.
+
+    With a ``checker`` (a GpuBlockedChecker of W with 128-row blocks, 1 to 8 checks, built
+    with ``height=tc_height(n)``) the check is fused: the kernel reduces every block's bank
+    rows against the same staged X tiles, a verdict launch follows, and the call returns
+    (Y, CheckResult) with results of shape (B, checks, num_blocks)."""
     import ctypes
 
     from pck.cuda import _lib
-    from pck.cuda._ext import on_device, stream_handle
+    from pck.cuda._ext import check_cuda, on_device, ptr, stream_handle
+    from pck.cuda.checker import CheckResult
 
     if not (W.is_cuda and X.is_cuda and W.device == X.device):
         raise RuntimeError("W and X must be CUDA tensors on one device")
@@ -86,13 +92,38 @@ def gemv_tc(W: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
         raise RuntimeError("expected W of shape (m, n) and X of shape (B, n)")
     if not (W.is_contiguous() and X.is_contiguous()):
         raise RuntimeError("W and X must be contiguous")
-    Y = torch.empty((X.size(0), W.size(0)), dtype=torch.float32, device=W.device)
+    batch = X.size(0)
+    dev = W.device
+    Y = torch.empty((batch, W.size(0)), dtype=torch.float32, device=dev)
     job = (_lib.GemvJob * 1)()
     job[0].W, job[0].X, job[0].Y = W.data_ptr(), X.data_ptr(), Y.data_ptr()
-    job[0].m, job[0].n, job[0].batch, job[0].threads = W.size(0), W.size(1), X.size(0), 256
+    job[0].m, job[0].n, job[0].batch, job[0].threads = W.size(0), W.size(1), batch, 256
     job[0].weight_format = _lib.PCK_WEIGHTS_BF16
     job[0].check = ctypes.POINTER(_lib.CheckDesc)()
-    with on_device(W.device):
-        rc = _lib.library().pck_gemv_tc(job, 1, stream_handle(W.device))
+    result = None
+    desc = _lib.CheckDesc()
+    if checker is not None:
+        if (checker.m, checker.n) != tuple(W.shape):
+            raise ValueError("the checker was built for another shape")
+        pcx, ps = checker.scratch(batch)
+        pcx = pcx.view(batch, checker.checks, checker.num_blocks, checker.segments)
+        ps = ps.view(batch, checker.num_blocks, checker.segments)
+        for t, name, dt in ((pcx, "partial_cx", torch.float64), (ps, "partial_s", torch.float64)):
+            check_cuda(t, name, dt, dev)
+        shape = (batch, checker.checks, checker.num_blocks)
+        passed = torch.empty(shape, dtype=torch.bool, device=dev)
+        rho = torch.empty(shape, dtype=torch.float64, device=dev)
+        tau = torch.empty(shape, dtype=torch.float64, device=dev)
+        desc.c, desc.a, desc.r = ptr(checker.c), ptr(checker.a), ptr(checker.r)
+        desc.x, desc.y = ptr(X), ptr(Y)
+        desc.partial_cx, desc.partial_s, desc.counters = ptr(pcx), ptr(ps), None
+        desc.passed, desc.rho, desc.tau = ptr(passed), ptr(rho), ptr(tau)
+        desc.n, desc.block, desc.num_blocks, desc.checks = W.size(1), checker.block, checker.num_blocks, checker.checks
+        desc.segments, desc.batch = checker.segments, batch
+        desc.coef, desc.geps, desc.tau_floor = float(checker.coef), float(checker.geps), float(checker.tau_floor)
+        job[0].check = ctypes.pointer(desc)
+        result = CheckResult(passed, rho, tau)
+    with on_device(dev):
+        rc = _lib.library().pck_gemv_tc(job, 1, stream_handle(dev))
     _lib.check(rc, "tensor-core gemv kernel")
-    return Y
+    return Y if checker is None else (Y, result)

@@ -104,3 +104,33 @@ def test_tc_height_is_conservative_in_the_chain_length() -> None:
 
     assert tc_height(16) == 16 and tc_height(4096) == 8 * 257 and tc_height(4097) == 8 * 258
     assert np.all(np.diff([tc_height(n) for n in range(1, 2000)]) >= 0)
+
+
+@pytest.mark.parametrize(("m", "n", "batch", "checks"), [(1024, 4096, 128, 1), (384, 1000, 50, 3), (512, 4096, 256, 8),
+                                                         (256, 14336, 16, 2)])  # fmt: skip
+def test_fused_check_matches_the_standalone_check(m: int, n: int, batch: int, checks: int) -> None:
+    from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
+
+    W, X = problem(m, n, batch, seed=m * 3 + batch)
+    checker = GpuBlockedChecker(W, 128, tc_height(n), checks=checks, generator=torch.Generator().manual_seed(9))
+    Y, res = gemv_tc(W, X, checker)
+    assert torch.equal(Y.view(torch.int32), gemv_tc(W, X).view(torch.int32))  # the bank warps leave Y alone
+    assert res.passed.shape == (batch, checks, m // 128) and res.verdict.all()
+    for b0 in range(0, batch, 16):
+        sep = checker.check(X[b0 : b0 + 16].contiguous(), Y[b0 : b0 + 16].contiguous())
+        assert torch.equal(sep.passed, res.passed[b0 : b0 + 16])
+        torch.testing.assert_close(res.tau[b0 : b0 + 16], sep.tau, rtol=1e-12, atol=0)
+        assert float(((res.rho[b0 : b0 + 16] - sep.rho).abs() / sep.tau).max()) < 1e-6
+
+
+def test_fused_check_catches_a_bank_for_other_weights() -> None:
+    from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
+
+    W, X = problem(512, 4096, 64, seed=77)
+    W2 = W.clone()
+    W2[5::128] += 1.0  # one row of every block changed: |delta y| ~ 100, far above 2 tau
+    checker = GpuBlockedChecker(W2, 128, tc_height(4096), checks=2, generator=torch.Generator().manual_seed(1))
+    _, res = gemv_tc(W, X, checker)
+    delta = (X.double() @ (W2.double() - W.double()).T).abs().view(64, 4, 128).amax(dim=2)
+    assert bool((delta > 2 * res.tau.amax(dim=1)).all())
+    assert not res.verdict.any()
