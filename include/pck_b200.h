@@ -218,9 +218,9 @@ int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m,
  * coalesced tree: the tensor core adds 16 exact products per MMA and n/16 MMAs in sequence,
  * so a checker of these outputs takes that accumulation's declared height
  * (pck.cuda.gemv.tc_height). `threads` and the exponent range are unused. A job's `check`
- * (optional; blocks of 128 rows, 1 to 8 checks, batch up to 256, the job's own X, Y and
- * shape) is fused: the same kernel reduces each block's checksum and bound rows against the
- * staged X tiles (binary64), and a verdict launch follows. The reference has no counterpart;
+ * (optional; the job's own X, Y and shape, batch up to 256) is decided in the same call: a
+ * launch reduces the bank rows of all checks against X on the CUDA cores in binary64 (exact
+ * products, the bound rounded up), and a verdict launch follows. The reference has no counterpart;
  * its batched decode runs batch-1 GEMVs (harness/csrc/batched_gemv.cu:25-82 is a CUDA-core
  * diagnostic).
  */

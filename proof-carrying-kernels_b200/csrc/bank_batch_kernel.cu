@@ -1,0 +1,135 @@
+// Checksum-bank partial sums for a wide decode batch (the checks of the tensor-core GEMV):
+// for every bank row (c[k, beta, :] or a[beta, :]), column b of X and column segment s,
+//   partial_cx[b, k, beta, s] = sum over the segment of c[k, beta, j] x[b, j]    (binary64)
+//   partial_s [b, beta, s]    = sum over the segment of a[beta, j] |x[b, j]|     (rounded up)
+// with exact products (binary32 x bfloat16 and bfloat16 x bfloat16 are exact in binary64).
+//
+// This is a small binary64 matrix product, bank rows x batch columns, done on the CUDA cores:
+// a CTA takes 64 bank rows of one kind, 64 batch columns and one segment, widens 32 columns
+// of the rows and of X to binary64 in shared memory at a time (each conversion serves 64
+// products), and each of its 256 threads accumulates 4 rows x 4 columns (rows ty + 16i,
+// columns tx + 16q: neighbouring threads read neighbouring words) in a fixed order. The
+// verdict kernel (verdict_kernel.cu) adds the segments and decides the blocks.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "bank_batch_plan.h"
+#include "pck_common.cuh"
+
+namespace pck {
+namespace {
+
+constexpr int kRows = 64;   // bank rows per CTA
+constexpr int kCols = 64;   // batch columns per CTA
+constexpr int kChunk = 32;  // columns of the bank (j) per shared-memory round
+
+__global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__ BankBatchPlan plan) {
+  __shared__ double rows_s[kChunk][kRows];
+  __shared__ double x_s[kChunk][kCols];
+  int j = 0;
+  while (j + 1 < plan.njobs && static_cast<int>(blockIdx.x) >= plan.jobs[j + 1].tile_begin) ++j;
+  const BankBatchJob& jb = plan.jobs[j];
+  const int tile = static_cast<int>(blockIdx.x) - jb.tile_begin;
+  const int seg = static_cast<int>(blockIdx.z);
+  if (seg >= jb.segs) return;  // uniform
+  const bool bound = tile >= jb.c_tiles;  // a rows: |x|, rounded up
+  const int64_t nrows = bound ? jb.nb : static_cast<int64_t>(jb.checks) * jb.nb;
+  const int64_t row0 = static_cast<int64_t>(bound ? tile - jb.c_tiles : tile) * kRows;
+  const int b0 = static_cast<int>(blockIdx.y) * kCols;
+  if (b0 >= jb.batch) return;
+  const int64_t j0 = static_cast<int64_t>(seg) * jb.seg_len;
+  const int64_t j1 = min(jb.n, j0 + jb.seg_len);
+  const int t = static_cast<int>(threadIdx.x);
+  const int ty = t / 16, tx = t % 16;
+  double acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[i][q] = 0.0;
+  }
+  for (int64_t jc = j0; jc < j1; jc += kChunk) {
+    // 64 x 32 values of the rows and of X per round, 8 of each per thread, coalesced in j
+    const int jj = t % kChunk;
+    const int64_t col = jc + jj;
+    const bool in = col < j1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = t / kChunk + 8 * i;
+      const int64_t row = row0 + r;
+      double v = 0.0;
+      if (in && row < nrows) {
+        v = bound ? static_cast<double>(bf16_bits_to_float(__ldg(jb.a + row * jb.n + col)))
+                  : static_cast<double>(__ldg(jb.c + row * jb.n + col));
+      }
+      rows_s[jj][r] = v;
+      const int b = b0 + r;
+      double xv = 0.0;
+      if (in && b < jb.batch) {
+        xv = static_cast<double>(bf16_bits_to_float(__ldg(jb.X + static_cast<int64_t>(b) * jb.n + col)));
+        if (bound) xv = fabs(xv);
+      }
+      x_s[jj][r] = xv;
+    }
+    __syncthreads();
+    if (bound) {
+#pragma unroll 4
+      for (int k = 0; k < kChunk; ++k) {
+        double rv[4], xv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          rv[i] = rows_s[k][ty + 16 * i];
+          xv[i] = x_s[k][tx + 16 * i];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[i][q] = __fma_ru(rv[i], xv[q], acc[i][q]);
+        }
+      }
+    } else {
+#pragma unroll 4
+      for (int k = 0; k < kChunk; ++k) {
+        double rv[4], xv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          rv[i] = rows_s[k][ty + 16 * i];
+          xv[i] = x_s[k][tx + 16 * i];
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[i][q] = __fma_rn(rv[i], xv[q], acc[i][q]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = row0 + ty + 16 * i;
+    if (row >= nrows) continue;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int b = b0 + tx + 16 * q;
+      if (b >= jb.batch) continue;
+      if (bound) {
+        jb.partial_s[(static_cast<int64_t>(b) * jb.nb + row) * jb.seg_alloc + seg] = acc[i][q];
+      } else {
+        // row = k * nb + beta, and partial_cx is (batch, checks, nb, seg_alloc)
+        jb.partial_cx[(static_cast<int64_t>(b) * jb.checks * jb.nb + row) * jb.seg_alloc + seg] = acc[i][q];
+      }
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_bank_batch(const BankBatchPlan& plan, int col_groups, int max_segs, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>(plan.total_tiles), static_cast<unsigned>(col_groups),
+                  static_cast<unsigned>(max_segs));
+  bank_batch_kernel<<<grid, 256, 0, stream>>>(plan);
+  return cudaGetLastError();
+}
+
+}  // namespace pck

@@ -17,6 +17,7 @@
 #include "pck_b200.h"
 #include "sampling_plan.h"
 #include "tc_plan.h"
+#include "bank_batch_plan.h"
 #include "stream_plan.h"
 #include "verdict_plan.h"
 
@@ -329,7 +330,8 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
 
 // Launches the verdict kernel for `count` validated checks whose partial sums are (or will
 // be, earlier on the stream) in their scratch.
-int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream, int fixed_segs = 0) {
+int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream,
+                 const int32_t* fixed_segs = nullptr) {
   if (count < 1 || count > pck::kMaxVerdictJobs) {
     return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", pck::kMaxVerdictJobs, count);
   }
@@ -339,8 +341,8 @@ int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t str
     const pck_check_desc* d = descs[i];
     pck::VerdictJob& vj = plan.jobs[i];
     int64_t seg_len = 0;
-    if (fixed_segs > 0) {
-      vj.segs = fixed_segs;
+    if (fixed_segs) {
+      vj.segs = fixed_segs[i];
     } else {
       pck::segment_split(d->n, d->segments, kSegmentTarget, &seg_len, &vj.segs);
     }
@@ -669,23 +671,13 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
           static_cast<int64_t>(d->num_blocks) * d->block != jb.m) {
         return fail(PCK_ERR_ARGUMENT, "a fused check must cover the job's own x, y and shape");
       }
-      if (d->block != pck::kTcTileM) {
-        return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV fuses checks of %d-row blocks only", pck::kTcTileM);
+      if (d->checks < 1) return fail(PCK_ERR_ARGUMENT, "empty checker");
+      if (d->segments < 1 || d->segments > d->n) {
+        return fail(PCK_ERR_ARGUMENT, "segments must be in [1, n], got %d", d->segments);
       }
-      if (d->checks < 1 || d->checks > pck::kTcMaxChecks) {
-        return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV fuses 1 to %d checks, got %d", pck::kTcMaxChecks, d->checks);
-      }
-      if (d->segments < 1) return fail(PCK_ERR_ARGUMENT, "segments must be in [1, n], got %d", d->segments);
       if (!(d->coef > 0) || !(d->geps > 0) || !(d->tau_floor > 0)) {
         return fail(PCK_ERR_ARGUMENT, "coef, geps and floor must be positive");
       }
-      tj.has_check = 1;
-      tj.c = d->c;
-      tj.a = static_cast<const uint16_t*>(d->a);
-      tj.partial_cx = d->partial_cx;
-      tj.partial_s = d->partial_s;
-      tj.checks = d->checks;
-      tj.seg_alloc = d->segments;
     }
     tj.tile_begin = tiles;
     tj.tiles = static_cast<int32_t>((jb.m + pck::kTcTileM - 1) / pck::kTcTileM);
@@ -698,24 +690,51 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   plan.batch = batch;
   plan.n_pad = (batch + 15) / 16 * 16;
   const size_t stage = pck::tc_stage_bytes(plan.n_pad);
-  plan.stages = static_cast<int32_t>(std::min<size_t>(8, (232448 - 1024 - 256 - pck::kTcBankBytes) / stage));
+  plan.stages = static_cast<int32_t>(std::min<size_t>(8, (232448 - 1024 - 256) / stage));
   // Every epilogue read takes 32 columns, so each accumulator spans a multiple of 32.
   plan.acc_stride = (plan.n_pad + 31) / 32 * 32;
   int cols = 32;
   while (cols < 2 * plan.acc_stride) cols *= 2;
   plan.tmem_cols = cols;
-  const size_t smem = 1024 + static_cast<size_t>(plan.stages) * stage + 256 + pck::kTcBankBytes;
+  const size_t smem = 1024 + static_cast<size_t>(plan.stages) * stage + 256;
   const unsigned grid = static_cast<unsigned>(std::min(tiles, sm_count()));
-  const cudaError_t err = pck::launch_tc(plan, grid, smem, static_cast<cudaStream_t>(stream));
+  cudaError_t err = pck::launch_tc(plan, grid, smem, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("tensor-core gemv kernel", err);
-  // The block verdicts of the fused checks: one segment of partial sums per block.
+  // The checks: the wide-batch bank kernel (bank rows x batch columns in binary64), then the
+  // block verdicts.
   const pck_check_desc* checks[pck::kTcMaxJobs];
+  int32_t segs[pck::kTcMaxJobs];
   int nc = 0;
+  pck::BankBatchPlan bank{};
+  int max_segs = 1;
   for (int i = 0; i < count; ++i) {
-    if (jobs[i].check && jobs[i].m > 0) checks[nc++] = jobs[i].check;
+    const pck_check_desc* d = jobs[i].check;
+    if (!d || jobs[i].m == 0) continue;
+    pck::BankBatchJob& bj = bank.jobs[nc];
+    bj.c = d->c;
+    bj.a = static_cast<const uint16_t*>(d->a);
+    bj.X = static_cast<const uint16_t*>(d->x);
+    bj.partial_cx = d->partial_cx;
+    bj.partial_s = d->partial_s;
+    bj.n = d->n;
+    bj.nb = d->num_blocks;
+    bj.checks = d->checks;
+    bj.batch = d->batch;
+    bj.seg_alloc = d->segments;
+    bj.segs = pck::bank_batch_segments(d->n, d->segments, &bj.seg_len);
+    bj.tile_begin = bank.total_tiles;
+    bj.c_tiles = static_cast<int32_t>((static_cast<int64_t>(d->checks) * d->num_blocks + 63) / 64);
+    bj.a_tiles = (d->num_blocks + 63) / 64;
+    bank.total_tiles += bj.c_tiles + bj.a_tiles;
+    max_segs = std::max(max_segs, bj.segs);
+    segs[nc] = bj.segs;
+    checks[nc++] = d;
   }
   if (nc == 0) return ok();
-  return run_verdicts(checks, nc, static_cast<cudaStream_t>(stream), 1);
+  bank.njobs = nc;
+  err = pck::launch_bank_batch(bank, (batch + 63) / 64, max_segs, static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail("bank kernel", err);
+  return run_verdicts(checks, nc, static_cast<cudaStream_t>(stream), segs);
 }
 
 }  // extern "C"

@@ -13,12 +13,7 @@
 //               stage into one of two accumulators, committing each stage back to the producer
 //               and each finished tile to the epilogue;
 //   warps 2..5  copy a finished accumulator out of tensor memory (warp w reads lanes
-//               32 (w % 4) ...) and store it as columns of Y, while the next tile accumulates;
-//   warps 6..9  for a checked job, reduce the tile's checker block against the same staged X
-//               tiles: c[k, beta] . x_b and a[beta] . |x_b| in binary64 (exact products; the
-//               bound rounded up), one column b per thread, the stage's bank rows widened to
-//               binary64 once in shared memory. A stage is released when the MMAs and these
-//               warps are done with it.
+//               32 (w % 4) ...) and store it as columns of Y, while the next tile accumulates.
 // Every mbarrier wait is bounded; a wait that gives up records the status bit and the roles
 // stop issuing work.
 #include <cuda.h>
@@ -101,15 +96,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
   uint64_t* tfull = empty + stages;   // [2]
   uint64_t* tempty = tfull + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  int* bank_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  double* bank_rows = reinterpret_cast<double*>(reinterpret_cast<uint8_t*>(full) + 256);  // [checks + 1][64]
   const int warp = static_cast<int>(threadIdx.x) / kWarp;
   const int lane = static_cast<int>(threadIdx.x) % kWarp;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, 5);  // the MMA commit and the four bank warps
+      mbar_init(empty + s, 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull + a, 1);
@@ -180,80 +173,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
           umma_commit(empty + s);  // the stage is free once these MMAs have read it
         }
         if (ok) umma_commit(tfull + acc);
-      }
-    }
-  } else if (warp >= 6) {  // bank warps 6..9
-    const int bt = static_cast<int>(threadIdx.x) - 6 * kWarp;  // 0..127
-    uint32_t it = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < plan.total_tiles; tile += gridDim.x) {
-      const TcJob& jb = plan.jobs[job_of(plan, tile)];
-      const int kblocks = static_cast<int>((jb.n + kTcTileK - 1) / kTcTileK);
-      const int64_t beta = tile - jb.tile_begin;
-      const int K = jb.checks;
-      double acc_c[2][kTcMaxChecks];
-      double acc_s[2] = {0.0, 0.0};
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-#pragma unroll
-        for (int r = 0; r < kTcMaxChecks; ++r) acc_c[q][r] = 0.0;
-      }
-      for (int kb = 0; kb < kblocks; ++kb, ++it) {
-        const int s = static_cast<int>(it % stages);
-        // one thread waits, so the four warps take the same branch at every named barrier
-        if (bt == 0) *bank_flag = mbar_wait(full + s, (it / stages) & 1u) ? 1 : 0;
-        named_barrier(1, 128);
-        if (!*bank_flag) {
-          ok = false;
-          break;
-        }
-        if (jb.has_check) {
-          const int64_t j0 = static_cast<int64_t>(kb) * kTcTileK;
-          for (int i = bt; i < (K + 1) * kTcTileK; i += 128) {
-            const int r = i / kTcTileK;
-            const int64_t j = j0 + i % kTcTileK;
-            double v = 0.0;
-            if (j < jb.n) {
-              v = r < K ? static_cast<double>(__ldg(jb.c + (static_cast<int64_t>(r) * jb.tiles + beta) * jb.n + j))
-                        : static_cast<double>(bf16_bits_to_float(__ldg(jb.a + beta * jb.n + j)));
-            }
-            bank_rows[i] = v;
-          }
-          named_barrier(1, 128);
-          const uint8_t* xt = smem + static_cast<size_t>(s) * stage_bytes + a_bytes;
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int b = bt + 128 * q;
-            if (b < plan.batch) {
-              for (int k = 0; k < kTcTileK; ++k) {  // the 128-byte swizzle: 16-byte chunk ^ (row % 8)
-                const uint32_t off = static_cast<uint32_t>(b) * 128u + ((static_cast<uint32_t>((k >> 3) ^ (b & 7))) << 4) +
-                                     (static_cast<uint32_t>(k & 7) << 1);
-                const double x = static_cast<double>(bf16_bits_to_float(*reinterpret_cast<const uint16_t*>(xt + off)));
-#pragma unroll
-                for (int r = 0; r < kTcMaxChecks; ++r) {
-                  if (r < K) acc_c[q][r] = __fma_rn(bank_rows[r * kTcTileK + k], x, acc_c[q][r]);
-                }
-                acc_s[q] = __fma_ru(bank_rows[K * kTcTileK + k], fabs(x), acc_s[q]);
-              }
-            }
-          }
-          named_barrier(1, 128);  // bank_rows is rewritten for the next stage
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty + s);
-      }
-      if (ok && jb.has_check) {
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int b = bt + 128 * q;
-          if (b < plan.batch) {
-#pragma unroll
-            for (int r = 0; r < kTcMaxChecks; ++r) {
-              if (r < K) jb.partial_cx[((static_cast<int64_t>(b) * K + r) * jb.tiles + beta) * jb.seg_alloc] = acc_c[q][r];
-            }
-            jb.partial_s[(static_cast<int64_t>(b) * jb.tiles + beta) * jb.seg_alloc] = acc_s[q];
-          }
-        }
       }
     }
   } else {  // epilogue warps 2..5

@@ -12,9 +12,7 @@ namespace pck {
 constexpr int kTcMaxJobs = 8;
 constexpr int kTcTileM = 128;     // W rows per tile (the MMA's M)
 constexpr int kTcTileK = 64;      // bfloat16 columns per pipeline stage (one 128-byte swizzle row)
-constexpr int kTcThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue, 6-9 bank
-constexpr int kTcMaxChecks = 8;   // sign draws of a fused check
-constexpr int kTcBankBytes = (kTcMaxChecks + 1) * kTcTileK * 8;  // a stage's bank rows in binary64
+constexpr int kTcThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kTcMaxBatch = 256;  // the MMA's largest N
 
 struct TcJob {
@@ -25,16 +23,6 @@ struct TcJob {
   int64_t n;
   int32_t tile_begin;  // first tile of this job in the launch's tile sequence
   int32_t tiles;
-  // fused check (has_check): a 128-row tile is one checker block; the bank rows of the block
-  // are reduced against the staged X tiles into segment 0 of the partial sums
-  const float* c;       // (checks, tiles, n)
-  const uint16_t* a;    // (tiles, n) bfloat16
-  double* partial_cx;   // (batch, checks, tiles, seg_alloc)
-  double* partial_s;    // (batch, tiles, seg_alloc)
-  int32_t has_check;
-  int32_t checks;
-  int32_t seg_alloc;
-  int32_t reserved;
 };
 
 struct alignas(64) TcPlan {

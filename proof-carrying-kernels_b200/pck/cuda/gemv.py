@@ -74,10 +74,10 @@ def gemv_tc(W: torch.Tensor, X: torch.Tensor, checker=None):
     bfloat16 W (m, n) and X (B, n), both contiguous and 16-byte aligned with n a multiple of
     8; binary32 Y. Not bit-exact to the coalesced tree.
 
-    With a ``checker`` (a GpuBlockedChecker of W with 128-row blocks, 1 to 8 checks, built
-    with ``height=tc_height(n)``) the check is fused: the kernel reduces every block's bank
-    rows against the same staged X tiles, a verdict launch follows, and the call returns
-    (Y, CheckResult) with results of shape (B, checks, num_blocks)."""
+    With a ``checker`` (a GpuBlockedChecker of W built with ``height=tc_height(n)``) the
+    call also checks Y: a binary64 launch reduces the bank rows against X (every batch
+    column), a verdict launch decides the blocks, and the call returns (Y, CheckResult) with
+    results of shape (B, checks, num_blocks)."""
     import ctypes
 
     from pck.cuda import _lib

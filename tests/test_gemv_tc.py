@@ -108,13 +108,13 @@ def test_tc_height_is_conservative_in_the_chain_length() -> None:
 
 @pytest.mark.parametrize(("m", "n", "batch", "checks"), [(1024, 4096, 128, 1), (384, 1000, 50, 3), (512, 4096, 256, 8),
                                                          (256, 14336, 16, 2)])  # fmt: skip
-def test_fused_check_matches_the_standalone_check(m: int, n: int, batch: int, checks: int) -> None:
+def test_checked_call_matches_the_standalone_check(m: int, n: int, batch: int, checks: int) -> None:
     from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
 
     W, X = problem(m, n, batch, seed=m * 3 + batch)
     checker = GpuBlockedChecker(W, 128, tc_height(n), checks=checks, generator=torch.Generator().manual_seed(9))
     Y, res = gemv_tc(W, X, checker)
-    assert torch.equal(Y.view(torch.int32), gemv_tc(W, X).view(torch.int32))  # the bank warps leave Y alone
+    assert torch.equal(Y.view(torch.int32), gemv_tc(W, X).view(torch.int32))  # the check leaves Y alone
     assert res.passed.shape == (batch, checks, m // 128) and res.verdict.all()
     for b0 in range(0, batch, 16):
         sep = checker.check(X[b0 : b0 + 16].contiguous(), Y[b0 : b0 + 16].contiguous())
@@ -123,7 +123,7 @@ def test_fused_check_matches_the_standalone_check(m: int, n: int, batch: int, ch
         assert float(((res.rho[b0 : b0 + 16] - sep.rho).abs() / sep.tau).max()) < 1e-6
 
 
-def test_fused_check_catches_a_bank_for_other_weights() -> None:
+def test_checked_call_catches_a_bank_for_other_weights() -> None:
     from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
 
     W, X = problem(512, 4096, 64, seed=77)
