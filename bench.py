@@ -150,8 +150,13 @@ def build_layer(args, rank: int, world: int, device: torch.device):
             dgen = torch.Generator(device=device).manual_seed(1000 + j)
             W = (torch.randn(m, nn, generator=dgen, device=device) * 0.02).bfloat16()
             W = W[shard.row0 : shard.row1].contiguous()
-            checker = GpuBlockedChecker(W, args.block, tree_height(nn, args.threads, 8), checks=args.checks,
-                                        generator=torch.Generator().manual_seed(2000 + j))  # fmt: skip
+            vec = 8
+            if args.weights == "e4m3":  # config 3: per-row E4M3 quantisation, checked against Q
+                from pck.cuda import quantize_fp8
+
+                W, vec = quantize_fp8(W)[0], 16
+            checker = GpuBlockedChecker(W.to(torch.bfloat16), args.block, tree_height(nn, args.threads, vec),
+                                        checks=args.checks, generator=torch.Generator().manual_seed(2000 + j))  # fmt: skip
             items.append((W, x, checker))
             items_plain.append((W, x, None))
             y_views.append(ys.local_view(j))
@@ -323,6 +328,8 @@ def main() -> None:
     parser.add_argument("--batch", type=int, default=1)
     parser.add_argument("--block", type=int, default=128)
     parser.add_argument("--checks", type=int, default=1)
+    parser.add_argument("--weights", choices=["bf16", "e4m3"], default="bf16",
+                        help="weight format (e4m3: config 3, per-row quantised weights)")
     parser.add_argument("--threads", type=int, default=256)
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     parser.add_argument("--no-cpu-baseline", action="store_true")
@@ -391,7 +398,7 @@ def main() -> None:
     traffic = profile_traffic()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.weights == "bf16":
         from oracle.cpu_baseline import time_checked_layer
 
         mats = host_layer(args, groups)
@@ -405,10 +412,11 @@ def main() -> None:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(t_checked * 1e3, 5), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if args.weights == "bf16" else "e4m3 x bf16",
             "data": "synthetic (seeded; weights N(0,0.02^2), activations N(0,1) with 1% outliers x20)",
             "config": {
                 "workload": "llama3-8b decode layer GEMV set (q,k,v,o,gate,up,down) + fused blocked check",
+                "weights": args.weights,
                 "batch": args.batch, "block": args.block, "checks": args.checks, "threads": args.threads,
                 "launches_per_step": len(launches),
                 "verdicts": "one verdict-kernel launch per layer after the four GEMV launches", "parallelism": f"row-shard x{world}" if world > 1 else "single",

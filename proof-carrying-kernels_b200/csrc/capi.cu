@@ -691,14 +691,25 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   plan.n_pad = (batch + 15) / 16 * 16;
   const size_t stage = pck::tc_stage_bytes(plan.n_pad);
   plan.stages = static_cast<int32_t>(std::min<size_t>(8, (232448 - 1024 - 256) / stage));
-  // Every epilogue read takes 32 columns, so each accumulator spans a multiple of 32.
-  plan.acc_stride = (plan.n_pad + 31) / 32 * 32;
+  // Few tiles with a small batch or a long K: split the K range of every tile over a cluster
+  // of CTAs while the launch still fits in one wave (one CTA per SM), keeping at least 4 K
+  // blocks (256 columns) per split. Otherwise the persistent kernel, whose two accumulators
+  // overlap one tile's epilogue with the next tile's loads.
+  int64_t kmin = INT64_MAX;
+  for (int j = 0; j < nj; ++j) kmin = std::min<int64_t>(kmin, (plan.jobs[j].n + pck::kTcTileK - 1) / pck::kTcTileK);
+  int splits = 1;
+  if (tiles * 2 <= sm_count() && (batch <= 32 || kmin >= 128)) {
+    while (splits < pck::kTcMaxSplits && static_cast<int64_t>(tiles) * splits * 2 <= sm_count() &&
+           kmin / (2 * splits) >= 4) {
+      splits *= 2;
+    }
+  }
+  plan.acc_stride = (plan.n_pad + 31) / 32 * 32;  // every epilogue read takes 32 columns
   int cols = 32;
-  while (cols < 2 * plan.acc_stride) cols *= 2;
+  while (cols < (splits == 1 ? 2 * plan.acc_stride : plan.n_pad)) cols *= 2;
   plan.tmem_cols = cols;
   const size_t smem = 1024 + static_cast<size_t>(plan.stages) * stage + 256;
-  const unsigned grid = static_cast<unsigned>(std::min(tiles, sm_count()));
-  cudaError_t err = pck::launch_tc(plan, grid, smem, static_cast<cudaStream_t>(stream));
+  cudaError_t err = pck::launch_tc(plan, splits, smem, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("tensor-core gemv kernel", err);
   // The checks: the wide-batch bank kernel (bank rows x batch columns in binary64), then the
   // block verdicts.

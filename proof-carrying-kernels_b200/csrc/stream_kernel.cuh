@@ -24,6 +24,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -272,6 +273,38 @@ __device__ __forceinline__ void chain_e4m3(float& acc, const uint4 w, const uint
   chain_e4m3_word<kFma>(acc, w.y, xa.z, xa.w);
   chain_e4m3_word<kFma>(acc, w.z, xb.x, xb.y);
   chain_e4m3_word<kFma>(acc, w.w, xb.z, xb.w);
+}
+
+// One vector of 16 E4M3 weights against 16 binary16 activations (xa: columns 0-7, xb: 8-15),
+// each product added with one mixed-precision FMA. Used only when every activation is
+// exactly a binary16 value: an E4M3 x binary16 product then has at most 12 significant bits
+// and lies in [2^-33, 2^25], so it is exact in binary32 and the FMA equals product-then-sum.
+__device__ __forceinline__ void chain_e4m3_half(float& acc, const uint4 w, const uint4 xa, const uint4 xb) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  const uint32_t xs[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    asm("{\n\t.reg .b16 p0, p1, w0, w1, w2, w3, x0, x1, x2, x3;\n\t.reg .b32 h01, h23;\n\t"
+        "mov.b32 {p0, p1}, %1;\n\t"
+        "cvt.rn.f16x2.e4m3x2 h01, p0;\n\tcvt.rn.f16x2.e4m3x2 h23, p1;\n\t"
+        "mov.b32 {w0, w1}, h01;\n\tmov.b32 {w2, w3}, h23;\n\t"
+        "mov.b32 {x0, x1}, %2;\n\tmov.b32 {x2, x3}, %3;\n\t"
+        "fma.rn.f32.f16 %0, w0, x0, %0;\n\tfma.rn.f32.f16 %0, w1, x1, %0;\n\t"
+        "fma.rn.f32.f16 %0, w2, x2, %0;\n\tfma.rn.f32.f16 %0, w3, x3, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(ws[i]), "r"(xs[2 * i]), "r"(xs[2 * i + 1]));
+  }
+}
+
+// kMode: 0 product then sum, 1 one FMA per product (exact products), 2 the E4M3 weights
+// against binary16 activations (chain_e4m3_half).
+template <int kMode>
+__device__ __forceinline__ void chain_e4m3_mode(float& acc, const uint4 w, const uint4 xa, const uint4 xb) {
+  if constexpr (kMode == 2) {
+    chain_e4m3_half(acc, w, xa, xb);
+  } else {
+    chain_e4m3<kMode != 0>(acc, w, xa, xb);
+  }
 }
 
 template <int WFMT>
@@ -550,7 +583,7 @@ __device__ __forceinline__ uint32_t word(const uint4& v, int i) {
 // holds the row bytes from vector v_lo * T on; vector q of the row is at
 // piece + (q - v_lo * T) * 16. nvec = n / V (n % V == 0 on this path). The shared-memory
 // loads of an iteration are issued together, before its arithmetic.
-template <int WFMT, int NV, int BG, bool kFma>
+template <int WFMT, int NV, int BG, int kMode>
 __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uint32_t piece, uint32_t xs,
                                                  uint32_t xcol, int g0, int batch, int v_lo, int v_hi,
                                                  int nvec, int lane) {
@@ -577,9 +610,9 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
           }
           const uint32_t xaddr = xcol_addr[b] + xoff + g * (kWarp * kXV);
           if constexpr (WFMT == kWeightsBf16) {
-            chain8_bf16<kFma>(st.acc[b][g], wv, lds128(xaddr));
+            chain8_bf16<kMode != 0>(st.acc[b][g], wv, lds128(xaddr));
           } else {
-            chain_e4m3<kFma>(st.acc[b][g], wv, lds128(xaddr), lds128(xaddr + 16));
+            chain_e4m3_mode<kMode>(st.acc[b][g], wv, lds128(xaddr), lds128(xaddr + 16));
           }
         }
       }
@@ -601,9 +634,9 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
 #pragma unroll
-            for (int g = 0; g < kStep; ++g) term_bf16<kFma, 0>(st.acc[b][g0w + g], word(wv[g], i), word(xv[g], i));
+            for (int g = 0; g < kStep; ++g) term_bf16<kMode != 0, 0>(st.acc[b][g0w + g], word(wv[g], i), word(xv[g], i));
 #pragma unroll
-            for (int g = 0; g < kStep; ++g) term_bf16<kFma, 1>(st.acc[b][g0w + g], word(wv[g], i), word(xv[g], i));
+            for (int g = 0; g < kStep; ++g) term_bf16<kMode != 0, 1>(st.acc[b][g0w + g], word(wv[g], i), word(xv[g], i));
           }
         } else {
           uint4 xa[kStep], xb[kStep];
@@ -613,7 +646,7 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
             xb[g] = lds128(xcol_addr[b] + xoff + (g0w + g) * (kWarp * kXV) + 16);
           }
 #pragma unroll
-          for (int g = 0; g < kStep; ++g) chain_e4m3<kFma>(st.acc[b][g0w + g], wv[g], xa[g], xb[g]);
+          for (int g = 0; g < kStep; ++g) chain_e4m3_mode<kMode>(st.acc[b][g0w + g], wv[g], xa[g], xb[g]);
         }
       }
     }
@@ -688,6 +721,25 @@ __device__ __forceinline__ void load_activations(const JobPlan& jb, uint8_t* xs,
       atomicMin(xexp, mn);
       atomicMax(xexp + 1, mx);
     }
+  }
+}
+
+// Rewrites the bfloat16 activations in shared memory as binary16 (each value exact: the
+// caller has checked every exponent field is in [110, 142]; zeros stay zeros).
+__device__ __forceinline__ void activations_to_half(const JobPlan& jb, uint8_t* xs, int tid) {
+  const int64_t words = static_cast<int64_t>(jb.batch) * jb.n / 8;
+  uint4* p = reinterpret_cast<uint4*>(xs);
+  for (int64_t i = tid; i < words; i += kPlainThreads) {
+    uint4 v = p[i];
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float lo = __uint_as_float(w[h] << 16);
+      const float hi = __uint_as_float(w[h] & 0xffff0000u);
+      const __half2 pair = __floats2half2_rn(lo, hi);
+      w[h] = *reinterpret_cast<const uint32_t*>(&pair);
+    }
+    p[i] = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -768,7 +820,7 @@ __device__ __forceinline__ void walk_next(PieceWalk& w, const JobPlan& jb, int64
 
 // The consuming half of staged_warp (see there); `issue` and `issued` continue the walk
 // that primed the ring.
-template <int WFMT, int NV, int BG, bool kFma>
+template <int WFMT, int NV, int BG, int kMode>
 __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, int64_t count, int slots,
                                                uint32_t slot_bytes, uint32_t row_piece, uint8_t* ring,
                                                uint64_t* full, uint32_t xs, int warp, int lane,
@@ -816,7 +868,7 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
       const int v_hi = min(static_cast<int>((off + bytes + T * 16u - 1) / (T * 16u)), vtotal);
       for (int g0 = 0; g0 < jb.batch; g0 += BG) {
         if (first) row.reset();
-        reduce_row_piece<WFMT, NV, BG, kFma>(row, piece, xs, xcol, g0, jb.batch, v_lo, v_hi, nvec, lane);
+        reduce_row_piece<WFMT, NV, BG, kMode>(row, piece, xs, xcol, g0, jb.batch, v_lo, v_hi, nvec, lane);
         if (last) {
 #pragma unroll
           for (int b = 0; b < BG; ++b) {
@@ -870,7 +922,8 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
 // A warp's stream: primes its ring with weight pieces (weights are never written by a
 // kernel of this library, so this may overlap the previous kernel), then calls
 // `before_inputs` (which waits for the producers and brings in the activations; it returns
-// -1 if that failed, else whether the FMA form is exact), then reduces its units.
+// -1 if that failed, else the arithmetic mode: 0 product then sum, 1 one FMA per exact
+// product, 2 E4M3 weights against binary16 activations), then reduces its units.
 template <int WFMT, int NV, int BG, typename Inputs>
 __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots,
                                             uint32_t slot_bytes, uint32_t row_piece, uint8_t* ring,
@@ -905,12 +958,19 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
     for (int64_t i = 0; i < issued; ++i) mbar_wait(full + i, 0);
     return;
   }
+  if constexpr (WFMT == kWeightsE4m3) {
+    if (fma_mode == 2) {
+      staged_consume<WFMT, NV, BG, 2>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs, warp, lane,
+                                      issue, issued);
+      return;
+    }
+  }
   if (fma_mode) {
-    staged_consume<WFMT, NV, BG, true>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs, warp, lane,
-                                       issue, issued);
+    staged_consume<WFMT, NV, BG, 1>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs, warp, lane,
+                                    issue, issued);
   } else {
-    staged_consume<WFMT, NV, BG, false>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs, warp, lane,
-                                        issue, issued);
+    staged_consume<WFMT, NV, BG, 0>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs, warp, lane,
+                                    issue, issued);
   }
 }
 
@@ -955,6 +1015,15 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
       wait_for_producers();
       load_activations(jb, xs, xexp, static_cast<int>(threadIdx.x), lane);
       __syncthreads();
+      if constexpr (WFMT == kWeightsE4m3) {
+        // Every nonzero activation with an exponent field in [110, 142] is exactly a binary16
+        // value: convert the copy in shared memory once and take the binary16 FMA form.
+        if (jb.has_w && xexp[0] >= 110u && xexp[1] <= 142u) {
+          activations_to_half(jb, xs, static_cast<int>(threadIdx.x));
+          __syncthreads();
+          return 2;
+        }
+      }
       return jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]) ? 1 : 0;
     };
     staged_warp<WFMT, NV, BG>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane, inputs);

@@ -32,11 +32,14 @@ struct alignas(64) TcPlan {
   int32_t batch;   // columns of X and Y
   int32_t n_pad;   // batch rounded up to a multiple of 16 (the MMA's N)
   int32_t stages;      // shared-memory pipeline depth
-  int32_t acc_stride;  // tensor-memory columns per accumulator: n_pad rounded up to 32
-  int32_t tmem_cols;   // allocated columns: a power of two >= 2 * acc_stride
+  int32_t acc_stride;  // persistent form: tensor-memory columns per accumulator (n_pad up to 32s)
+  int32_t tmem_cols;   // allocated columns: a power of two >= 2 * acc_stride (persistent) or n_pad
 };
 
-cudaError_t launch_tc(const TcPlan& plan, unsigned grid, size_t smem, cudaStream_t stream);
+constexpr int kTcMaxSplits = 8;  // CTAs of a tile's cluster (K ranges), the portable cluster size
+
+// splits == 1: the persistent kernel; else total_tiles * splits CTAs in clusters of `splits`
+cudaError_t launch_tc(const TcPlan& plan, int splits, size_t smem, cudaStream_t stream);
 size_t tc_stage_bytes(int n_pad);
 cudaError_t tc_status(unsigned int* value, bool clear);
 
