@@ -5,11 +5,11 @@
 // with exact products (binary32 x bfloat16 and bfloat16 x bfloat16 are exact in binary64).
 //
 // This is a small binary64 matrix product, bank rows x batch columns, done on the CUDA cores:
-// a CTA takes 64 bank rows of one kind, 64 batch columns and one segment, widens 32 columns
-// of the rows and of X to binary64 in shared memory at a time (each conversion serves 64
-// products), and each of its 256 threads accumulates 4 rows x 4 columns (rows ty + 16i,
-// columns tx + 16q: neighbouring threads read neighbouring words) in a fixed order. The
-// verdict kernel (verdict_kernel.cu) adds the segments and decides the blocks.
+// a CTA takes 32 bank rows of one kind, 32 batch columns and one segment, widens 32 columns
+// of the rows and of X to binary64 in shared memory at a time (the global loads of the next
+// round are in flight meanwhile), and each of its 256 threads accumulates 2 rows x 2 columns
+// (rows ty + 16i, columns tx + 16q: neighbouring threads read neighbouring words) in a fixed
+// order. The verdict kernel (verdict_kernel.cu) adds the segments and decides the blocks.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -20,13 +20,42 @@
 namespace pck {
 namespace {
 
-constexpr int kRows = 64;   // bank rows per CTA
-constexpr int kCols = 64;   // batch columns per CTA
+constexpr int kRows = 32;   // bank rows per CTA
+constexpr int kCols = 32;   // batch columns per CTA
 constexpr int kChunk = 32;  // columns of the bank (j) per shared-memory round
 
+// One round's raw values: each thread fetches 4 bank values (rows t/32 + 8i, column t%32)
+// and 4 activations (batch columns t/32 + 8i), fetched a round ahead of their use.
+struct Round {
+  uint32_t row[4];
+  uint16_t x[4];
+};
+
+__device__ __forceinline__ void fetch_round(const BankBatchJob& jb, bool bound, int64_t nrows, int64_t row0,
+                                            int b0, int64_t jc, int64_t j1, int t, Round& rd) {
+  const int jj = t % kChunk;
+  const int64_t col = jc + jj;
+  const bool in = col < j1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = row0 + t / kChunk + 8 * i;
+    rd.row[i] = 0u;
+    if (in && row < nrows) {
+      rd.row[i] = bound ? static_cast<uint32_t>(__ldg(jb.a + row * jb.n + col))
+                        : __float_as_uint(__ldg(jb.c + row * jb.n + col));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int b = b0 + t / kChunk + 8 * i;
+    rd.x[i] = (in && b < jb.batch) ? __ldg(jb.X + static_cast<int64_t>(b) * jb.n + col) : static_cast<uint16_t>(0);
+  }
+}
+
 __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__ BankBatchPlan plan) {
-  __shared__ double rows_s[kChunk][kRows];
-  __shared__ double x_s[kChunk][kCols];
+  // one padding word per line: the 32 lanes of a warp store one bank column j each
+  __shared__ double rows_s[kChunk][kRows + 1];
+  __shared__ double x_s[kChunk][kCols + 1];
   int j = 0;
   while (j + 1 < plan.njobs && static_cast<int>(blockIdx.x) >= plan.jobs[j + 1].tile_begin) ++j;
   const BankBatchJob& jb = plan.jobs[j];
@@ -41,76 +70,66 @@ __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__
   const int64_t j0 = static_cast<int64_t>(seg) * jb.seg_len;
   const int64_t j1 = min(jb.n, j0 + jb.seg_len);
   const int t = static_cast<int>(threadIdx.x);
-  const int ty = t / 16, tx = t % 16;
-  double acc[4][4];
+  const int ty = t / 16, tx = t % 16;  // rows ty + 16i (i < 2), columns tx + 16q (q < 2)
+  double acc[2][2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 2; ++i) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc[i][q] = 0.0;
+    for (int q = 0; q < 2; ++q) acc[i][q] = 0.0;
   }
+  Round rd;
+  fetch_round(jb, bound, nrows, row0, b0, j0, j1, t, rd);
   for (int64_t jc = j0; jc < j1; jc += kChunk) {
-    // 64 x 32 values of the rows and of X per round, 8 of each per thread, coalesced in j
     const int jj = t % kChunk;
-    const int64_t col = jc + jj;
-    const bool in = col < j1;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = t / kChunk + 8 * i;
-      const int64_t row = row0 + r;
-      double v = 0.0;
-      if (in && row < nrows) {
-        v = bound ? static_cast<double>(bf16_bits_to_float(__ldg(jb.a + row * jb.n + col)))
-                  : static_cast<double>(__ldg(jb.c + row * jb.n + col));
-      }
-      rows_s[jj][r] = v;
-      const int b = b0 + r;
-      double xv = 0.0;
-      if (in && b < jb.batch) {
-        xv = static_cast<double>(bf16_bits_to_float(__ldg(jb.X + static_cast<int64_t>(b) * jb.n + col)));
-        if (bound) xv = fabs(xv);
-      }
-      x_s[jj][r] = xv;
+    for (int i = 0; i < 4; ++i) {
+      rows_s[jj][t / kChunk + 8 * i] = bound ? static_cast<double>(bf16_bits_to_float(static_cast<uint16_t>(rd.row[i])))
+                                             : static_cast<double>(__uint_as_float(rd.row[i]));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const double xv = static_cast<double>(bf16_bits_to_float(rd.x[i]));
+      x_s[jj][t / kChunk + 8 * i] = bound ? fabs(xv) : xv;
     }
     __syncthreads();
+    if (jc + kChunk < j1) fetch_round(jb, bound, nrows, row0, b0, jc + kChunk, j1, t, rd);  // next round in flight
     if (bound) {
-#pragma unroll 4
+#pragma unroll 8
       for (int k = 0; k < kChunk; ++k) {
-        double rv[4], xv[4];
+        double rv[2], xv[2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          rv[i] = rows_s[k][ty + 16 * i];
-          xv[i] = x_s[k][tx + 16 * i];
-        }
+        for (int i = 0; i < 2; ++i) rv[i] = rows_s[k][ty + 16 * i];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int q = 0; q < 2; ++q) xv[q] = x_s[k][tx + 16 * q];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc[i][q] = __fma_ru(rv[i], xv[q], acc[i][q]);
+        for (int i = 0; i < 2; ++i) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) acc[i][q] = __fma_ru(rv[i], xv[q], acc[i][q]);
         }
       }
     } else {
-#pragma unroll 4
+#pragma unroll 8
       for (int k = 0; k < kChunk; ++k) {
-        double rv[4], xv[4];
+        double rv[2], xv[2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          rv[i] = rows_s[k][ty + 16 * i];
-          xv[i] = x_s[k][tx + 16 * i];
-        }
+        for (int i = 0; i < 2; ++i) rv[i] = rows_s[k][ty + 16 * i];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int q = 0; q < 2; ++q) xv[q] = x_s[k][tx + 16 * q];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc[i][q] = __fma_rn(rv[i], xv[q], acc[i][q]);
+        for (int i = 0; i < 2; ++i) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) acc[i][q] = __fma_rn(rv[i], xv[q], acc[i][q]);
         }
       }
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 2; ++i) {
     const int64_t row = row0 + ty + 16 * i;
     if (row >= nrows) continue;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 2; ++q) {
       const int b = b0 + tx + 16 * q;
       if (b >= jb.batch) continue;
       if (bound) {

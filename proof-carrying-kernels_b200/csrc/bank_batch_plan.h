@@ -23,7 +23,7 @@ struct BankBatchJob {
   int32_t batch;
   int32_t seg_alloc;
   int32_t segs;
-  int32_t tile_begin;   // first row tile: ceil(checks*nb / 64) c tiles, then ceil(nb / 64) a tiles
+  int32_t tile_begin;   // first row tile: ceil(checks*nb / 32) c tiles, then ceil(nb / 32) a tiles
   int32_t c_tiles;
   int32_t a_tiles;
 };

@@ -734,8 +734,8 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
     bj.seg_alloc = d->segments;
     bj.segs = pck::bank_batch_segments(d->n, d->segments, &bj.seg_len);
     bj.tile_begin = bank.total_tiles;
-    bj.c_tiles = static_cast<int32_t>((static_cast<int64_t>(d->checks) * d->num_blocks + 63) / 64);
-    bj.a_tiles = (d->num_blocks + 63) / 64;
+    bj.c_tiles = static_cast<int32_t>((static_cast<int64_t>(d->checks) * d->num_blocks + 31) / 32);  // 32-row tiles
+    bj.a_tiles = (d->num_blocks + 31) / 32;
     bank.total_tiles += bj.c_tiles + bj.a_tiles;
     max_segs = std::max(max_segs, bj.segs);
     segs[nc] = bj.segs;
@@ -743,7 +743,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   }
   if (nc == 0) return ok();
   bank.njobs = nc;
-  err = pck::launch_bank_batch(bank, (batch + 63) / 64, max_segs, static_cast<cudaStream_t>(stream));
+  err = pck::launch_bank_batch(bank, (batch + 31) / 32, max_segs, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("bank kernel", err);
   return run_verdicts(checks, nc, static_cast<cudaStream_t>(stream), segs);
 }
