@@ -246,6 +246,46 @@ def e2e_step_time(groups, xs, ex, steps: int, warmup: int, world: int) -> tuple[
     return ms / 1e3 / steps, h2d, d2h
 
 
+def batch128_reading(args, groups, device, steps: int, warmup: int) -> dict:
+    """The same decode layer (same weights) at a decode batch of 128 on the tensor cores
+    (config 2's batched reading): unchecked, and checked with checkers of the tensor-core
+    accumulation's declared height. CUDA graphs of one step each, device time."""
+    from pck.cuda import GpuBlockedChecker, tc_height
+    from pck.cuda.plan import TcLaunch
+
+    gen = torch.Generator().manual_seed(128)
+    plain, checked, flops, wbytes = [], [], 0, 0
+    for gi, g in enumerate(groups):
+        n = g.items[0][0].size(1)
+        X = outlier_x(n, 128, gen).to(device).contiguous()
+        items_p, items_c = [], []
+        for k, (W, _, _) in enumerate(g.items):
+            ch = GpuBlockedChecker(W, args.block, tc_height(n), checks=args.checks,
+                                   generator=torch.Generator().manual_seed(3000 + 10 * gi + k))  # fmt: skip
+            items_p.append((W, X, None))
+            items_c.append((W, X, ch))
+            flops += 2 * W.numel() * 128
+            wbytes += W.numel() * 2
+        plain.append(TcLaunch(items_p))
+        checked.append(TcLaunch(items_c))
+    g_plain = cuda_graph(lambda: [t.launch() for t in plain])
+    g_checked = cuda_graph(lambda: [t.launch() for t in checked])
+    g_checked.replay()
+    torch.cuda.synchronize()
+    passed = all(bool(r.passed.all()) for t in checked for r in t.results if r is not None)
+    t_plain = timed(g_plain, steps, warmup, 1)
+    t_checked = timed(g_checked, steps, warmup, 1)
+    del g_plain, g_checked
+    return {
+        "batch": 128, "path": "tcgen05 (tc_kernel) + binary64 bank kernel + verdicts", "all_blocks_passed": passed,
+        "unchecked_ms_per_step": round(t_plain * 1e3, 4), "checked_ms_per_step": round(t_checked * 1e3, 4),
+        "tokens_per_s_checked": round(128 / t_checked), "tokens_per_s_unchecked": round(128 / t_plain),
+        "weight_GB_per_s_unchecked": round(wbytes / t_plain / 1e9, 1),
+        "tflops_unchecked": round(flops / t_plain / 1e12, 1),
+        "checker_overhead_pct": round((t_checked / t_plain - 1) * 100, 1),
+    }  # fmt: skip
+
+
 def host_layer(args, gpu_groups=None):
     """The layer on the host for the CPU legs: same seeds, same checker banks (copied from
     the GPU when it exists, built on the CPU otherwise)."""
@@ -333,6 +373,7 @@ def main() -> None:
     parser.add_argument("--threads", type=int, default=256)
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-batch128", action="store_true", help="skip the batch-128 tensor-core reading")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -386,6 +427,9 @@ def main() -> None:
         t_checked = timed(graph_checked, args.steps, args.warmup, world)
         t_plain = timed(graph_plain, args.steps, args.warmup, world)
     clock = clocks.summary()
+    batch128 = None
+    if world == 1 and args.weights == "bf16" and args.batch == 1 and not args.no_batch128:
+        batch128 = batch128_reading(args, groups, device, max(20, args.steps // 10), args.warmup)
     t_e2e, h2d, d2h = e2e_step_time(launches, xs, ex, max(20, args.steps // 10), args.warmup, world)
 
     total_bytes = torch.tensor([float(step_bytes_local)], device=device)
@@ -437,6 +481,7 @@ def main() -> None:
             "gpu_launches": len(launches) * args.steps,
             "clocks": clock,
             "cpu_baseline": cpu,
+            "batch128": batch128,
         }  # fmt: skip
         print(json.dumps(line), flush=True)
     del graph_checked, graph_plain

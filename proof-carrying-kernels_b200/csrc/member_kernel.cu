@@ -60,7 +60,7 @@ __device__ __forceinline__ float logit_at(const void* row, int64_t j) {
 }
 
 // Calls fn(value) for every logit of the row, each thread a strided share, with 16-byte
-// loads when the row start allows. `cached`: read through L2 only (second passes).
+// loads (four in flight per thread) when the row start allows.
 template <int DT, typename Fn>
 __device__ __forceinline__ void for_each_logit(const void* row, int64_t vocab, Fn fn) {
   constexpr int kPer = DT == kLogitsF32 ? 4 : 8;  // logits per 16 bytes
@@ -69,8 +69,7 @@ __device__ __forceinline__ void for_each_logit(const void* row, int64_t vocab, F
   if ((reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
     const int64_t vecs = vocab / kPer;
     const uint4* v4 = static_cast<const uint4*>(row);
-    for (int64_t i = tid; i < vecs; i += kMemberThreads) {
-      const uint4 q = __ldg(v4 + i);
+    auto take = [&](const uint4 q) {
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
       if constexpr (DT == kLogitsF32) {
 #pragma unroll
@@ -86,7 +85,18 @@ __device__ __forceinline__ void for_each_logit(const void* row, int64_t vocab, F
           }
         }
       }
+    };
+    // four 16-byte loads in flight per thread, then their values
+    constexpr int kAhead = 4;
+    int64_t i = tid;
+    for (; i + (kAhead - 1) * kMemberThreads < vecs; i += kAhead * kMemberThreads) {
+      uint4 q[kAhead];
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u) q[u] = __ldg(v4 + i + u * kMemberThreads);
+#pragma unroll
+      for (int u = 0; u < kAhead; ++u) take(q[u]);
     }
+    for (; i < vecs; i += kMemberThreads) take(__ldg(v4 + i));
     head = vecs * kPer;
   }
   for (int64_t j = head + tid; j < vocab; j += kMemberThreads) fn(logit_at<DT>(row, j));

@@ -128,8 +128,7 @@ __global__ void __launch_bounds__(kSamplingThreads) sampling_kernel(const __grid
   // One pass over the slice.
   float mn = INFINITY, mx_rej = -INFINITY, mx_all = -INFINITY;
   bool nan = false;
-  for (int64_t j = j0 + tid; j < j1; j += kSamplingThreads) {
-    const float x = __ldg(l + j);
+  auto take = [&](int64_t j, float x) {
     nan |= isnan(x);
     mx_all = fmaxf(mx_all, x);
     const int64_t o = j - j0;
@@ -138,7 +137,17 @@ __global__ void __launch_bounds__(kSamplingThreads) sampling_kernel(const __grid
     } else {
       mx_rej = fmaxf(mx_rej, x);
     }
+  };
+  constexpr int kAhead = 4;  // loads in flight per thread
+  int64_t j = j0 + tid;
+  for (; j + (kAhead - 1) * kSamplingThreads < j1; j += kAhead * kSamplingThreads) {
+    float xs[kAhead];
+#pragma unroll
+    for (int u = 0; u < kAhead; ++u) xs[u] = __ldg(l + j + u * kSamplingThreads);
+#pragma unroll
+    for (int u = 0; u < kAhead; ++u) take(j + u * kSamplingThreads, xs[u]);
   }
+  for (; j < j1; j += kSamplingThreads) take(j, __ldg(l + j));
   nan = __syncthreads_or(nan);
   block_minmax3(mn, mx_rej, mx_all, sh);
   if (tid == 0) sh.part = SlicePartial{mn, mx_rej, mx_all, nan ? 1 : 0, bad ? 1 : 0, 0, 0.0, 0.0};

@@ -146,3 +146,57 @@ LLAMA3_8B_GROUPS: list[list[tuple[str, int, int]]] = [
     [("gate", 14336, 4096), ("up", 14336, 4096)],
     [("down", 4096, 14336)],
 ]
+
+
+class TcLaunch:
+    """One call of the tensor-core GEMV (`pck_gemv_tc`) for up to 8 bfloat16 matrices that
+    share a batch of activations, each optionally checked (a GpuBlockedChecker built with
+    ``height=tc_height(n)``): Y_i (B, m_i) = X_i (B, n_i) W_i^T. Reusable launch after launch
+    (e.g. captured in a CUDA graph); outputs in ``ys``, check results in ``results``."""
+
+    def __init__(self, items: Sequence[tuple[torch.Tensor, torch.Tensor, GpuBlockedChecker | None]]) -> None:
+        if not 1 <= len(items) <= 8:
+            raise ValueError(f"a tensor-core launch holds 1 to 8 GEMVs, got {len(items)}")
+        self.device = items[0][0].device
+        self.lib = extension().lib
+        self.count = len(items)
+        self.items = list(items)
+        self._descs = (_lib.CheckDesc * self.count)()
+        self._jobs = (_lib.GemvJob * self.count)()
+        self.ys: list[torch.Tensor] = []
+        self.results: list[CheckResult | None] = []
+        batch = items[0][1].size(0)
+        for g, (W, X, ch) in enumerate(items):
+            if W.dtype != torch.bfloat16 or X.dtype != torch.bfloat16 or X.dim() != 2 or X.size(0) != batch:
+                raise RuntimeError("W and X must be bfloat16, X (B, n) with one B for the launch")
+            if not (W.is_contiguous() and X.is_contiguous()) or X.size(1) != W.size(1):
+                raise RuntimeError("expected contiguous W (m, n) and X (B, n)")
+            y = torch.empty((batch, W.size(0)), dtype=torch.float32, device=self.device)
+            self.ys.append(y)
+            job = self._jobs[g]
+            job.W, job.X, job.Y = W.data_ptr(), X.data_ptr(), y.data_ptr()
+            job.m, job.n, job.batch, job.threads = W.size(0), W.size(1), batch, 256
+            job.weight_format = _lib.PCK_WEIGHTS_BF16
+            if ch is None:
+                job.check = None
+                self.results.append(None)
+                continue
+            pcx, ps = ch.scratch(batch)
+            shape = (batch, ch.checks, ch.num_blocks)
+            out = (torch.empty(shape, dtype=torch.bool, device=self.device),
+                   torch.empty(shape, dtype=torch.float64, device=self.device),
+                   torch.empty(shape, dtype=torch.float64, device=self.device))  # fmt: skip
+            d = self._descs[g]
+            d.c, d.a, d.r, d.x, d.y = ch.c.data_ptr(), ch.a.data_ptr(), ch.r.data_ptr(), X.data_ptr(), y.data_ptr()
+            d.partial_cx, d.partial_s, d.counters = pcx.data_ptr(), ps.data_ptr(), None
+            d.passed, d.rho, d.tau = (t.data_ptr() for t in out)
+            d.n, d.block, d.num_blocks, d.checks = W.size(1), ch.block, ch.num_blocks, ch.checks
+            d.segments, d.batch = ch.segments, batch
+            d.coef, d.geps, d.tau_floor = float(ch.coef), float(ch.geps), float(ch.tau_floor)
+            job.check = ctypes.pointer(d)
+            self.results.append(CheckResult(*out))
+
+    def launch(self) -> None:
+        with on_device(self.device):
+            rc = self.lib.pck_gemv_tc(self._jobs, self.count, stream_handle(self.device))
+        _lib.check(rc, "tensor-core gemv kernel")
