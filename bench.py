@@ -5,8 +5,11 @@ gate/up 14336x4096, down 4096x14336), bfloat16 weights ~N(0, 0.02^2), activation
 with 1% outlier channels x20, every output checked by the trusted blocked checker
 (b = 128, K = 1). A step is one decode layer: four launches of the persistent streaming
 kernel (q/k/v share their input, o, gate/up share theirs, down), each with its checks'
-bank rows fused into the same pass over memory, then one verdict-kernel launch for all
-seven checks (the reference runs one checker launch per layer), captured in a CUDA graph.
+bank rows fused into the same pass over memory. The block verdicts are decided inside the
+next streaming launch (`pck_gemv_pipelined`: o's launch decides q/k/v's blocks, ..., the next
+layer's q/k/v launch decides down's), so a step still decides all seven checks, with no
+launch of its own; `--verdicts launch` instead ends the step with one verdict-kernel launch
+for all seven (the reference runs one checker launch per layer). Captured in a CUDA graph.
 With N GPUs every matrix is row-sharded by whole checker blocks and one NCCL all-gather
 per step assembles the outputs and verdict bits.
 
@@ -37,6 +40,13 @@ import torch  # noqa: E402
 
 METRIC = "checked GEMV HBM GB/s (Llama-3-8B decode layer, b=128 blocks, K=1)"
 UNIT = "GB/s"
+VERDICTS = {
+    "carried": "decided inside the next streaming launch (pck_gemv_pipelined); the next layer's first launch "
+               "decides down's blocks",
+    "launch": "one verdict-kernel launch per layer after the four GEMV launches",
+}  # fmt: skip
+SCOPE = {"carried": "4 stream_kernel launches, each deciding the previous launch's checks",
+         "launch": "4 stream_kernel launches + 1 verdict_kernel launch"}  # fmt: skip
 L2_BYTES = 126 * 2**20
 
 
@@ -374,6 +384,8 @@ def main() -> None:
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-batch128", action="store_true", help="skip the batch-128 tensor-core reading")
+    parser.add_argument("--verdicts", choices=sorted(VERDICTS), default="carried",
+                        help="carried: each launch decides the previous launch's checks; launch: a verdict launch per step")
     args = parser.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -394,14 +406,26 @@ def main() -> None:
 
     groups, verdict, plain, xs, ex, ex_plain = build_layer(args, rank, world, device)
     vs = ex.parts[1]
-    launches = [*groups, verdict]
     step_bytes_local = sum(g.algorithmic_bytes for g in groups)
 
-    def checked_step() -> None:
-        for g in launches:
-            g.launch()
-        if world > 1:
-            ex.gather()
+    def step_of(launches):
+        def checked_step() -> None:
+            for g in launches:
+                g.launch()
+            if world > 1:
+                ex.gather()
+
+        return checked_step
+
+    # the other verdict form, for comparison (captured before the launches are re-planned)
+    graph_other = cuda_graph(step_of([*groups, verdict])) if args.verdicts == "carried" else None
+    if args.verdicts == "carried":  # each launch decides the previous one's checks
+        for i, g in enumerate(groups):
+            g.set_prior([groups[i - 1]])
+        launches = list(groups)
+    else:
+        launches = [*groups, verdict]
+    checked_step = step_of(launches)
 
     def plain_step() -> None:
         for g in plain:
@@ -426,6 +450,7 @@ def main() -> None:
     with ClockSampler(gpu_index) as clocks:
         t_checked = timed(graph_checked, args.steps, args.warmup, world)
         t_plain = timed(graph_plain, args.steps, args.warmup, world)
+        t_other = timed(graph_other, args.steps, args.warmup, world) if graph_other is not None else None
     clock = clocks.summary()
     batch128 = None
     if world == 1 and args.weights == "bf16" and args.batch == 1 and not args.no_batch128:
@@ -463,17 +488,18 @@ def main() -> None:
                 "weights": args.weights,
                 "batch": args.batch, "block": args.block, "checks": args.checks, "threads": args.threads,
                 "launches_per_step": len(launches),
-                "verdicts": "one verdict-kernel launch per layer after the four GEMV launches", "parallelism": f"row-shard x{world}" if world > 1 else "single",
+                "verdicts": VERDICTS[args.verdicts], "parallelism": f"row-shard x{world}" if world > 1 else "single",
                 "l2": "inputs larger than L2 (436 MB of weights per step, 126 MB L2)",
                 "graph": "CUDA graph of one step, replayed",
             },
             "checker_overhead_pct": round((t_checked / t_plain - 1) * 100, 2),
             "unchecked_ms_per_step": round(t_plain * 1e3, 5),
+            "verdict_launch_ms_per_step": round(t_other * 1e3, 5) if t_other is not None else None,
             "all_blocks_passed": all_passed,
             "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / world / peak, 4),
                          "traffic": traffic,
-                         "scope": "one step = 4 stream_kernel launches + 1 verdict_kernel launch; "
+                         "scope": f"one step = {SCOPE[args.verdicts]}; "
                                   "achieved and traffic are per step (ncu summary in profiles/)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"},
             "e2e": {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -484,7 +510,7 @@ def main() -> None:
             "batch128": batch128,
         }  # fmt: skip
         print(json.dumps(line), flush=True)
-    del graph_checked, graph_plain
+    del graph_checked, graph_plain, graph_other
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -35,7 +35,7 @@ extern "C" {
 /* Message of the last failing call on this thread ("" if none). */
 const char* pck_last_error(void);
 
-/* ABI version of this library (increases when a declaration here changes): 2. */
+/* ABI version of this library (increases when a declaration here changes): 3. */
 int pck_abi_version(void);
 
 /*
@@ -171,6 +171,21 @@ int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream);
  * reference runs one checker launch per layer. No reference counterpart.
  */
 int pck_gemv_partials(const pck_gemv_job* jobs, int count, void* stream);
+
+/*
+ * pck_gemv_partials that also decides up to PCK_MAX_JOBS `prior` checks whose partial sums
+ * and outputs earlier kernels on this stream produced (typically the previous
+ * pck_gemv_pipelined call of a decode layer): the same decisions, bit for bit, as
+ * pck_check_verdicts on those descriptors, without a launch of their own — each warp of the
+ * streaming kernel decides its share of the prior blocks while its first weight copies are in
+ * flight. The prior checks' y, scratch and verdict arrays must not overlap the outputs or
+ * scratch of this call's jobs (rejected with PCK_ERR_ARGUMENT); nprior = 0 is
+ * pck_gemv_partials. The last launch of a sequence leaves its own checks to
+ * pck_check_verdicts (or to the next sequence). No reference counterpart: the reference
+ * decides every layer's checks in a checker launch of their own.
+ */
+int pck_gemv_pipelined(const pck_gemv_job* jobs, int count, const pck_check_desc* prior, int nprior,
+                       void* stream);
 
 /*
  * The block verdicts of up to PCK_MAX_JOBS checks whose partial sums an earlier

@@ -112,9 +112,18 @@ constexpr int64_t kSegmentTarget = 2048;    // columns per checksum-bank segment
 // Time per byte of a bank segment (binary64 products and sums) relative to a weight row,
 // for the CTA split between the jobs of a launch.
 constexpr double kBankCost = 4.0;
+constexpr int kVerdictTasksPerWarp = 4;  // prior verdicts a warp decides, about
+constexpr int kMaxVerdictCtas = 8;
 
-// Plans and launches the streaming kernel for `specs` (validated by the caller).
-int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
+int64_t fill_verdicts(const pck_check_desc* const* descs, int count, const int32_t* fixed_segs,
+                      pck::VerdictPlan& plan);
+int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream,
+                 const int32_t* fixed_segs);
+
+// Plans and launches the streaming kernel for `specs` (validated by the caller); `prior`
+// (validated, at most kMaxVerdictJobs) are checks of earlier launches that this one decides.
+int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
+               const std::vector<const pck_check_desc*>& prior = {}) {
   if (specs.empty() || specs.size() > static_cast<size_t>(pck::kMaxJobs)) {
     return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %zu", pck::kMaxJobs, specs.size());
   }
@@ -157,7 +166,9 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
       if (d->batch > pck::kSegBatch) tma = false;
     }
   }
-  if (live.empty()) return ok();
+  if (live.empty()) {  // nothing to stream: the prior verdicts alone
+    return prior.empty() ? ok() : run_verdicts(prior.data(), static_cast<int>(prior.size()), stream, nullptr);
+  }
 
   // Pass 2: units and bytes of every job (one row per row unit). A checked GEMV becomes two
   // jobs of the launch: its rows, and its bank rows (reduced against the same x). Their
@@ -263,7 +274,17 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
 
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs
   // in proportion to their bytes, at least one each and never more than their units.
-  const int sms = sm_count();
+  // Prior verdicts: CTAs of their own past the streaming ones, about kVerdictTasksPerWarp
+  // tasks per warp (each a round trip to L2, so a few microseconds per CTA in all).
+  int64_t prior_tasks = 0;
+  int verdict_ctas = 0;
+  if (!prior.empty()) {
+    prior_tasks = fill_verdicts(prior.data(), static_cast<int>(prior.size()), nullptr, plan.prior);
+    const int64_t per_cta = static_cast<int64_t>(pck::kConsumerWarps) * kVerdictTasksPerWarp;
+    verdict_ctas = static_cast<int>(std::min<int64_t>(kMaxVerdictCtas, (prior_tasks + per_cta - 1) / per_cta));
+    verdict_ctas = std::max(verdict_ctas, 1);
+  }
+  const int sms = std::max(1, sm_count() - verdict_ctas);
   int64_t total_units = 0;
   double total_bytes = 0.0;
   for (int j = 0; j < nj; ++j) {
@@ -318,9 +339,12 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   }
   plan.njobs = nj;
   plan.threads = threads;
+  plan.verdict_cta_begin = static_cast<int32_t>(begin);
+  plan.verdict_ctas = verdict_ctas;
+  plan.prior_tasks = prior_tasks;
 
   if (!tma) bg = 1;
-  const unsigned grid = static_cast<unsigned>(begin);
+  const unsigned grid = static_cast<unsigned>(begin + verdict_ctas);
   const cudaError_t err = wfmt == pck::kWeightsBf16
                               ? pck::launch_stream_bf16(plan, nv, bg, tma, grid, smem, stream)
                               : pck::launch_stream_e4m3(plan, nv, bg, tma, grid, smem, stream);
@@ -328,14 +352,10 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream) {
   return ok();
 }
 
-// Launches the verdict kernel for `count` validated checks whose partial sums are (or will
-// be, earlier on the stream) in their scratch.
-int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream,
-                 const int32_t* fixed_segs = nullptr) {
-  if (count < 1 || count > pck::kMaxVerdictJobs) {
-    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", pck::kMaxVerdictJobs, count);
-  }
-  pck::VerdictPlan plan{};
+// The verdict plan of `count` validated checks (count in [1, kMaxVerdictJobs]); returns its
+// number of tasks (one warp each).
+int64_t fill_verdicts(const pck_check_desc* const* descs, int count, const int32_t* fixed_segs,
+                      pck::VerdictPlan& plan) {
   int64_t tasks = 0;
   for (int i = 0; i < count; ++i) {
     const pck_check_desc* d = descs[i];
@@ -366,6 +386,18 @@ int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t str
     tasks += vj.tasks;
   }
   plan.njobs = count;
+  return tasks;
+}
+
+// Launches the verdict kernel for `count` validated checks whose partial sums are (or will
+// be, earlier on the stream) in their scratch.
+int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream,
+                 const int32_t* fixed_segs) {
+  if (count < 1 || count > pck::kMaxVerdictJobs) {
+    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", pck::kMaxVerdictJobs, count);
+  }
+  pck::VerdictPlan plan{};
+  const int64_t tasks = fill_verdicts(descs, count, fixed_segs, plan);
   const cudaError_t err = pck::launch_verdicts(plan, tasks, stream);
   if (err != cudaSuccess) return cuda_fail("verdict kernel", err);
   return ok();
@@ -399,6 +431,18 @@ bool encode_bf16_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t co
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A byte range of device memory (NULL or empty: nothing).
+struct Range {
+  const void* p;
+  int64_t bytes;
+};
+
+bool overlaps(const Range& a, const Range& b) {
+  if (!a.p || !b.p || a.bytes <= 0 || b.bytes <= 0) return false;
+  const auto a0 = reinterpret_cast<uintptr_t>(a.p), b0 = reinterpret_cast<uintptr_t>(b.p);
+  return a0 < b0 + static_cast<uintptr_t>(b.bytes) && b0 < a0 + static_cast<uintptr_t>(a.bytes);
+}
+
 int check_gemv_args(const void* W, const void* x, const float* y, int64_t m, int64_t n,
                     int threads, int min_threads) {
   if (m < 0 || n < 0) return fail(PCK_ERR_ARGUMENT, "expected W of shape (m, n) with m, n >= 0");
@@ -416,7 +460,7 @@ extern "C" {
 
 const char* pck_last_error(void) { return g_error.c_str(); }
 
-int pck_abi_version(void) { return 2; }
+int pck_abi_version(void) { return 3; }
 
 int pck_device_status(unsigned int* status, int clear) {
   if (!status) return fail(PCK_ERR_ARGUMENT, "status must not be NULL");
@@ -480,12 +524,20 @@ int pck_blocked_check(const pck_check_desc* descs, int count, void* stream) {
   if (int rc = run_stream(specs, static_cast<cudaStream_t>(stream))) return rc;
   const pck_check_desc* checks[PCK_MAX_JOBS];
   for (int i = 0; i < count; ++i) checks[i] = descs + i;
-  return run_verdicts(checks, count, static_cast<cudaStream_t>(stream));
+  return run_verdicts(checks, count, static_cast<cudaStream_t>(stream), nullptr);
 }
 
 int pck_gemv_partials(const pck_gemv_job* jobs, int count, void* stream) {
+  return pck_gemv_pipelined(jobs, count, nullptr, 0, stream);
+}
+
+int pck_gemv_pipelined(const pck_gemv_job* jobs, int count, const pck_check_desc* prior, int nprior,
+                       void* stream) {
   if (count < 1 || count > PCK_MAX_JOBS || !jobs) {
     return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", PCK_MAX_JOBS, count);
+  }
+  if (nprior < 0 || nprior > PCK_MAX_JOBS || (nprior > 0 && !prior)) {
+    return fail(PCK_ERR_ARGUMENT, "prior checks must number [0, %d], got %d", PCK_MAX_JOBS, nprior);
   }
   std::vector<Spec> specs;
   for (int i = 0; i < count; ++i) {
@@ -508,7 +560,39 @@ int pck_gemv_partials(const pck_gemv_job* jobs, int count, void* stream) {
     specs.push_back(Spec{jb.W, jb.X, jb.Y, jb.m, jb.n, jb.batch, jb.threads, jb.weight_format,
                          true, jb.check, jb.w_exp_min, jb.w_exp_max});
   }
-  return run_stream(specs, static_cast<cudaStream_t>(stream));
+  std::vector<const pck_check_desc*> before;
+  for (int i = 0; i < nprior; ++i) {
+    const pck_check_desc* d = prior + i;
+    if (int rc = validate_check(d)) return rc;
+    // The prior checks' inputs must be final and their outputs untouched by this launch.
+    const int64_t nb = d->num_blocks, rows = nb * d->block;
+    const Range reads_writes[] = {
+        {d->y, 4 * d->batch * rows},
+        {d->partial_cx, 8 * d->batch * d->checks * nb * d->segments},
+        {d->partial_s, 8 * d->batch * nb * d->segments},
+        {d->passed, d->batch * d->checks * nb},
+        {d->rho, 8 * d->batch * d->checks * nb},
+        {d->tau, 8 * d->batch * d->checks * nb},
+    };
+    for (int j = 0; j < count; ++j) {
+      const pck_gemv_job& jb = jobs[j];
+      const pck_check_desc* c = jb.check;
+      const Range writes[] = {
+          {jb.Y, 4 * jb.batch * jb.m},
+          {c ? c->partial_cx : nullptr, c ? 8LL * c->batch * c->checks * c->num_blocks * c->segments : 0},
+          {c ? c->partial_s : nullptr, c ? 8LL * c->batch * c->num_blocks * c->segments : 0},
+      };
+      for (const Range& a : reads_writes) {
+        for (const Range& b : writes) {
+          if (overlaps(a, b)) {
+            return fail(PCK_ERR_ARGUMENT, "prior check %d shares memory with what job %d writes", i, j);
+          }
+        }
+      }
+    }
+    before.push_back(d);
+  }
+  return run_stream(specs, static_cast<cudaStream_t>(stream), before);
 }
 
 int pck_check_verdicts(const pck_check_desc* descs, int count, void* stream) {
@@ -520,7 +604,7 @@ int pck_check_verdicts(const pck_check_desc* descs, int count, void* stream) {
     if (int rc = validate_check(descs + i)) return rc;
     checks[i] = descs + i;
   }
-  return run_verdicts(checks, count, static_cast<cudaStream_t>(stream));
+  return run_verdicts(checks, count, static_cast<cudaStream_t>(stream), nullptr);
 }
 
 int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream) {
@@ -531,7 +615,7 @@ int pck_gemv_checked(const pck_gemv_job* jobs, int count, void* stream) {
     if (jobs[i].check && jobs[i].m > 0) checks[n++] = jobs[i].check;
   }
   if (n == 0) return ok();
-  return run_verdicts(checks, n, static_cast<cudaStream_t>(stream));
+  return run_verdicts(checks, n, static_cast<cudaStream_t>(stream), nullptr);
 }
 
 int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m, int64_t n,

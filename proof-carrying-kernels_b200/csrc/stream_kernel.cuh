@@ -1,6 +1,8 @@
 // The persistent streaming kernel: GEMV rows and the checksum-bank segments of the trusted
 // checker, for every job of a launch plan (stream_plan.h). The block verdicts follow in the
-// verdict kernel (verdict_kernel.cu).
+// verdict kernel (verdict_kernel.cu), or in the next streaming launch (Plan::prior: a few
+// CTAs of that launch, past the streaming ones, decide the earlier launch's blocks while the
+// others stream; the streaming warps run no verdict code).
 //
 // Staged path (kTma): each of the 16 consumer warps of a CTA owns the units w, w + 16, ... of the
 // CTA's range and streams them through its own ring of `slots` shared-memory pieces with
@@ -31,6 +33,7 @@
 
 #include "pck_common.cuh"
 #include "stream_plan.h"
+#include "verdict_task.cuh"
 
 namespace pck {
 
@@ -587,9 +590,12 @@ template <int WFMT, int NV, int BG, int kMode>
 __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uint32_t piece, uint32_t xs,
                                                  uint32_t xcol, int g0, int batch, int v_lo, int v_hi,
                                                  int nvec, int lane) {
-  constexpr int V = Format<WFMT>::kVec;
   constexpr int T = NV * kWarp;
-  constexpr uint32_t kXV = V * 2;  // bytes of one activation vector
+  // bytes between the activations of consecutive vectors: bfloat16 rows keep columns in
+  // order (16 bytes a vector); E4M3 rows keep each column in halves (load_activations), the
+  // second half xcol / 2 bytes after the first
+  constexpr uint32_t kXV = 16;
+  const uint32_t xhalf = xcol / 2;
   uint32_t xcol_addr[BG];
 #pragma unroll
   for (int b = 0; b < BG; ++b) xcol_addr[b] = xs + static_cast<uint32_t>(min(g0 + b, batch - 1)) * xcol;
@@ -612,7 +618,7 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
           if constexpr (WFMT == kWeightsBf16) {
             chain8_bf16<kMode != 0>(st.acc[b][g], wv, lds128(xaddr));
           } else {
-            chain_e4m3_mode<kMode>(st.acc[b][g], wv, lds128(xaddr), lds128(xaddr + 16));
+            chain_e4m3_mode<kMode>(st.acc[b][g], wv, lds128(xaddr), lds128(xaddr + xhalf));
           }
         }
       }
@@ -643,7 +649,7 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
 #pragma unroll
           for (int g = 0; g < kStep; ++g) {
             xa[g] = lds128(xcol_addr[b] + xoff + (g0w + g) * (kWarp * kXV));
-            xb[g] = lds128(xcol_addr[b] + xoff + (g0w + g) * (kWarp * kXV) + 16);
+            xb[g] = lds128(xcol_addr[b] + xoff + (g0w + g) * (kWarp * kXV) + xhalf);
           }
 #pragma unroll
           for (int g = 0; g < kStep; ++g) chain_e4m3_mode<kMode>(st.acc[b][g0w + g], wv[g], xa[g], xb[g]);
@@ -693,15 +699,26 @@ __device__ __forceinline__ void segment_piece(double* acc, uint32_t piece, uint3
 // into shared memory with one 16-byte load per thread and step, through L2 (X may have been
 // written by the kernel this one waited for), and merges the smallest nonzero (subnormals
 // counted as 1) and the largest exponent field into xexp[0..1].
+// E4M3 rows (16 weights, 32 bytes of activations per vector) keep each column in halves:
+// the first 16 bytes of every vector, then the second 16 bytes (n bytes on), so a warp's
+// 16-byte loads of one half are contiguous and free of bank conflicts.
+template <int WFMT>
 __device__ __forceinline__ void load_activations(const JobPlan& jb, uint8_t* xs, uint32_t* xexp, int tid,
                                                  int lane) {
   const int64_t words = static_cast<int64_t>(jb.batch) * jb.n / 8;
   const uint4* src = reinterpret_cast<const uint4*>(jb.X);
   uint4* dst = reinterpret_cast<uint4*>(xs);
+  const bool split = WFMT == kWeightsE4m3 && jb.has_w;  // n % 16 == 0 on the staged path
+  const uint32_t cw = static_cast<uint32_t>(jb.n / 8);  // 16-byte words per column
   unsigned mn = 1000, mx = 0;
   for (int64_t i = tid; i < words; i += kPlainThreads) {
     const uint4 v = __ldcg(src + i);
-    dst[i] = v;
+    if (split) {
+      const uint32_t b = static_cast<uint32_t>(i) / cw, w = static_cast<uint32_t>(i) - b * cw;
+      dst[b * cw + (w & 1u) * (cw / 2) + (w >> 1)] = v;
+    } else {
+      dst[i] = v;
+    }
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int h = 0; h < 8; ++h) {
@@ -919,6 +936,18 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
   for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
 }
 
+// This warp's share of the prior launch's verdict tasks, on the launch's last
+// plan.verdict_ctas CTAs (which stream nothing): task t goes to verdict CTA t % C, warp
+// (t / C) % 16. The caller has waited for the producing kernels.
+__device__ __forceinline__ void prior_verdicts(const Plan& plan, int warp, int lane) {
+  const int64_t ctas = plan.verdict_ctas;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) - plan.verdict_cta_begin + ctas * warp;
+  for (int64_t t = first; t < plan.prior_tasks; t += ctas * kConsumerWarps) {
+    const int j = verdict::job_of(plan.prior, t);
+    if (j >= 0) verdict::run_task(plan.prior.jobs[j], t - plan.prior.jobs[j].task_begin, lane);
+  }
+}
+
 // A warp's stream: primes its ring with weight pieces (weights are never written by a
 // kernel of this library, so this may overlap the previous kernel), then calls
 // `before_inputs` (which waits for the producers and brings in the activations; it returns
@@ -977,6 +1006,12 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
 template <int WFMT, int NV, int BG, bool kTma>
 __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_constant__ Plan plan) {
   extern __shared__ __align__(128) uint8_t smem[];
+  if (static_cast<int>(blockIdx.x) >= plan.verdict_cta_begin) {  // a CTA of the prior verdicts
+    allow_dependents();
+    wait_for_producers();
+    prior_verdicts(plan, static_cast<int>(threadIdx.x) / kWarp, static_cast<int>(threadIdx.x) % kWarp);
+    return;
+  }
   int j = 0;
   while (j + 1 < plan.njobs && static_cast<int>(blockIdx.x) >= plan.jobs[j + 1].cta_begin) ++j;
   const JobPlan& jb = plan.jobs[j];
@@ -1013,7 +1048,7 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
     // behind the weight pieces already requested) and take their exponent range.
     auto inputs = [&]() -> int {
       wait_for_producers();
-      load_activations(jb, xs, xexp, static_cast<int>(threadIdx.x), lane);
+      load_activations<WFMT>(jb, xs, xexp, static_cast<int>(threadIdx.x), lane);
       __syncthreads();
       if constexpr (WFMT == kWeightsE4m3) {
         // Every nonzero activation with an exponent field in [110, 142] is exactly a binary16

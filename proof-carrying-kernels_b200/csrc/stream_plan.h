@@ -13,13 +13,17 @@
 // (the layout also admits a block's row units in front of them, which the host no longer
 // plans). The segment units leave binary64 partial sums; the verdict kernel
 // (verdict_plan.h) turns them, with y as stored, into the block decisions once this kernel
-// has finished.
+// has finished — or the next streaming launch does, as its `prior` verdicts: the CTAs from
+// verdict_cta_begin on stream nothing; after griddepcontrol.wait (the previous kernels
+// complete) their warps decide the prior launch's blocks while the other CTAs stream.
 #pragma once
 
 #include <cuda_runtime.h>
 
 #include <cstddef>
 #include <cstdint>
+
+#include "verdict_plan.h"
 
 namespace pck {
 
@@ -82,6 +86,10 @@ struct Plan {
   int32_t x_bytes;
   int32_t threads;      // tree parameter T (all W jobs share it)
   int32_t sum_bytes;    // staged path: bytes per row piece (whole vector iterations)
+  int32_t verdict_cta_begin;  // CTAs [verdict_cta_begin, + verdict_ctas) decide `prior`
+  int32_t verdict_ctas;       // (the grid's last CTAs; 0 and grid size: none)
+  int64_t prior_tasks;        // verdict tasks of `prior`
+  VerdictPlan prior;          // checks of an earlier launch decided by this one
 };
 
 // Host-side launch of one instantiation family (stream_bf16.cu, stream_e4m3.cu). nv is

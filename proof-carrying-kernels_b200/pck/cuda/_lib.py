@@ -64,6 +64,7 @@ _SIGNATURES = {
     "pck_gemv_tc": ([ctypes.POINTER(GemvJob), _int, _p], _int),
     "pck_gemv_partials": ([ctypes.POINTER(GemvJob), _int, _p], _int),
     "pck_check_verdicts": ([ctypes.POINTER(CheckDesc), _int, _p], _int),
+    "pck_gemv_pipelined": ([ctypes.POINTER(GemvJob), _int, ctypes.POINTER(CheckDesc), _int, _p], _int),
     "pck_sampling_check": ([_p, _p, _p, _i64, _i64, _i64, _i64, _int, _f64, _f64, _f64, _i64, _p, _p, _p, _p,
                             _p, _p], _int),
     "pck_member_check": ([_p, _int, _i64, _i64, _i64, _p, _p, _p, _p, _f64, _p, _p, _p, _p], _int),

@@ -42,7 +42,8 @@ class GemvLaunch:
 
     def __init__(self, items: Sequence[tuple[torch.Tensor, torch.Tensor, GpuBlockedChecker | None]],
                  threads: int = 256, ys: Sequence[torch.Tensor] | None = None,
-                 passed: Sequence[torch.Tensor | None] | None = None, verdicts: bool = True) -> None:  # fmt: skip
+                 passed: Sequence[torch.Tensor | None] | None = None, verdicts: bool = True,
+                 prior: Sequence[GemvLaunch] = ()) -> None:  # fmt: skip
         if not 1 <= len(items) <= _lib.MAX_JOBS:
             raise ValueError(f"a launch holds 1 to {_lib.MAX_JOBS} GEMVs, got {len(items)}")
         W0 = items[0][0]
@@ -89,13 +90,37 @@ class GemvLaunch:
                 out = (p.view(out[0].shape), out[1], out[2])
             self.results.append(CheckResult(*out))
             job.check = ctypes.pointer(self._descs[g])
+        self.prior: list[GemvLaunch] = []
+        self._prior = None
+        self.set_prior(prior)
+
+    def set_prior(self, launches: Sequence[GemvLaunch]) -> None:
+        """Decide the checks of earlier launches (made with ``verdicts=False`` and launched
+        before this one on the same stream) inside this launch (`pck_gemv_pipelined`): no
+        verdict launch of their own. Their CheckResult objects then hold the verdicts once
+        this launch has run."""
+        descs = [d for gl in launches for d in gl.check_descs]
+        if len(descs) > _lib.MAX_JOBS:
+            raise ValueError(f"a launch decides at most {_lib.MAX_JOBS} prior checks, got {len(descs)}")
+        if any(gl.verdicts for gl in launches):
+            raise ValueError("prior launches must be made with verdicts=False")
+        if descs and self.verdicts:
+            raise ValueError("a launch that decides prior checks leaves its own to a later launch (verdicts=False)")
+        self.prior = list(launches)  # keeps the checks' tensors alive
+        self._prior = (_lib.CheckDesc * len(descs))(*descs) if descs else None
 
     def launch(self) -> None:
         """Issue the launch on the current stream (with ``verdicts=False``, the GEMVs and the
-        checks' partial sums only; a VerdictLaunch decides the blocks later)."""
-        fn = self.lib.pck_gemv_checked if self.verdicts else self.lib.pck_gemv_partials
+        checks' partial sums only; a VerdictLaunch, or a later launch given this one as
+        ``prior``, decides the blocks)."""
         with on_device(self.device):
-            rc = fn(self._jobs, self.count, stream_handle(self.device))
+            stream = stream_handle(self.device)
+            if self.verdicts:
+                rc = self.lib.pck_gemv_checked(self._jobs, self.count, stream)
+            elif self._prior is not None:
+                rc = self.lib.pck_gemv_pipelined(self._jobs, self.count, self._prior, len(self._prior), stream)
+            else:
+                rc = self.lib.pck_gemv_partials(self._jobs, self.count, stream)
         _lib.check(rc, "checked gemv kernel")
 
     @property

@@ -224,3 +224,79 @@ def test_one_verdict_launch_per_layer_equals_the_fused_launches() -> None:
             assert torch.equal(y.view(torch.int32), y0.view(torch.int32))
             assert torch.equal(r.passed, p0) and torch.equal(r.rho, rho0) and torch.equal(r.tau, tau0)
             assert bool(r.passed.all())
+
+
+def test_verdicts_carried_by_the_next_launch_equal_the_fused_launches() -> None:
+    """pck_gemv_pipelined: every launch of a scaled Llama-3-8B layer decides the previous
+    launch's checks (the first launch of the next layer decides the last), captured in a
+    CUDA graph and replayed: the bits of the fused calls, and a fault planted between two
+    launches is caught by the launch that decides it."""
+    from pck.cuda import GpuBlockedChecker
+    from pck.cuda.plan import GemvLaunch
+
+    gen = torch.Generator().manual_seed(17)
+    groups = [[(768, 4096), (128, 4096), (128, 4096)], [(512, 4096)], [(1792, 4096), (1792, 4096)],
+              [(512, 14336)]]  # fmt: skip
+    piped, fused = [], []
+    for shapes in groups:
+        x = torch.randn(shapes[0][1], generator=gen).bfloat16().cuda()
+        items = []
+        for m, n in shapes:
+            W = (torch.randn(m, n, generator=gen) * 0.02).bfloat16().cuda()
+            items.append((W, x, GpuBlockedChecker(W, 128, tree_height(n, 256, 8), checks=2, generator=gen)))
+        piped.append(GemvLaunch(items, 256, verdicts=False))
+        fused.append(GemvLaunch(items, 256))
+    for i, g in enumerate(piped):
+        g.set_prior([piped[i - 1]])  # the first launch decides the last one's checks
+    for g in fused:
+        g.launch()
+    torch.cuda.synchronize()
+    want = [[(y.clone(), r.passed.clone(), r.rho.clone(), r.tau.clone()) for y, r in zip(g.ys, g.results, strict=True)]
+            for g in fused]  # fmt: skip
+
+    def compare(skip_fault: bool) -> None:
+        for gi, g in enumerate(piped):
+            for j, (y, r) in enumerate(zip(g.ys, g.results, strict=True)):
+                y0, p0, rho0, tau0 = want[gi][j]
+                if skip_fault and gi == 1:
+                    continue
+                assert torch.equal(y.view(torch.int32), y0.view(torch.int32))
+                assert torch.equal(r.passed, p0) and torch.equal(r.rho, rho0) and torch.equal(r.tau, tau0)
+                assert bool(r.passed.all())
+
+    # eager: a layer, then the next layer's first launch for the last verdicts
+    for r in (res for g in piped for res in g.results):
+        r.passed.zero_()
+    for g in piped:
+        g.launch()
+    piped[0].launch()
+    torch.cuda.synchronize()
+    compare(False)
+
+    # a fault between o's GEMV and the gate/up launch that decides o's blocks
+    for g in piped[:2]:
+        g.launch()
+    piped[1].ys[0][300] += 1.0
+    piped[2].launch()
+    torch.cuda.synchronize()
+    r = piped[1].results[0]
+    assert not bool(r.passed[:, 300 // 128].any()) and int(r.passed.sum()) == r.passed.numel() - 2
+
+    # graph: the cycle of four launches, replayed twice after a warm layer
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for g in piped:
+            g.launch()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for g in piped:
+                g.launch()
+    torch.cuda.current_stream().wait_stream(stream)
+    for _ in range(2):
+        for r in (res for g in piped for res in g.results):
+            r.passed.zero_()
+        graph.replay()
+        piped[0].launch()
+        torch.cuda.synchronize()
+        compare(False)

@@ -46,7 +46,7 @@ def test_library_exports_every_declared_symbol(lib) -> None:
 
 
 def test_abi_version(lib) -> None:
-    assert lib.pck_abi_version() == 2
+    assert lib.pck_abi_version() == 3
 
 
 def _err(lib) -> str:
@@ -100,6 +100,23 @@ def test_fused_check_must_cover_its_job(lib) -> None:
     jobs[0].batch, jobs[0].threads, jobs[0].weight_format = 1, 256, 0
     jobs[0].check = ctypes.pointer(desc)
     assert lib.pck_gemv_checked(jobs, 1, None) == 1 and "cover" in _err(lib)
+
+
+def test_pipelined_rejects_prior_checks_sharing_its_outputs(lib) -> None:
+    from pck.cuda import _lib
+
+    prior = (_lib.CheckDesc * 1)()
+    d = prior[0]
+    for f in ("c", "a", "r", "x", "y", "partial_cx", "partial_s", "counters", "passed", "rho", "tau"):
+        setattr(d, f, 4096)
+    d.n, d.block, d.num_blocks, d.checks, d.segments, d.batch = 64, 8, 2, 1, 1, 1
+    d.coef, d.geps, d.tau_floor = 1e-6, 1e-12, 1e-40
+    jobs = (_lib.GemvJob * 1)()
+    jobs[0].W, jobs[0].X, jobs[0].Y, jobs[0].m, jobs[0].n = 16, 32, 4096 + 32, 16, 64
+    jobs[0].batch, jobs[0].threads, jobs[0].weight_format = 1, 256, 0
+    assert lib.pck_gemv_pipelined(jobs, 1, prior, 1, None) == 1 and "shares memory" in _err(lib)
+    assert lib.pck_gemv_pipelined(jobs, 1, prior, 17, None) == 1 and "prior" in _err(lib)
+    assert lib.pck_gemv_pipelined(jobs, 1, None, 1, None) == 1 and "prior" in _err(lib)
 
 
 def test_bank_build_rejects_bad_blocks(lib) -> None:
