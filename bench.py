@@ -180,7 +180,13 @@ def build_layer(args, rank: int, world: int, device: torch.device):
     return groups, verdict, plain, xs, ex, ex_plain
 
 
-def cuda_graph(fn) -> torch.cuda.CUDAGraph:
+# Consecutive layer steps captured in one CUDA graph (a decode graph holds every layer of the
+# model, so only one step in this many pays the graph launch boundary).
+GRAPH_STEPS = 8
+
+
+def cuda_graph(fn, steps: int = 1) -> tuple[torch.cuda.CUDAGraph, int]:
+    """A graph of ``steps`` consecutive calls of ``fn`` (run once eagerly first)."""
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -189,23 +195,28 @@ def cuda_graph(fn) -> torch.cuda.CUDAGraph:
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        fn()
+        for _ in range(steps):
+            fn()
     torch.cuda.synchronize()
-    return g
+    return g, steps
 
 
-def timed(graph: torch.cuda.CUDAGraph, steps: int, warmup: int, world: int) -> float:
-    """Seconds per step: max over ranks of the CUDA-event time of ``steps`` replays."""
-    for _ in range(warmup):
-        graph.replay()
+def timed(graph: tuple[torch.cuda.CUDAGraph, int], steps: int, warmup: int, world: int) -> float:
+    """Seconds per step: max over ranks of the CUDA-event time of exactly ``steps`` steps
+    (``steps`` a multiple of the graph's steps), after at least ``warmup`` steps."""
+    g, per = graph
+    if steps % per:
+        raise ValueError(f"steps ({steps}) must be a multiple of the graph's {per} steps")
+    for _ in range(-(-warmup // per)):
+        g.replay()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(steps):
-        graph.replay()
+    for _ in range(steps // per):
+        g.replay()
     end.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -280,7 +291,7 @@ def batch128_reading(args, groups, device, steps: int, warmup: int) -> dict:
         checked.append(TcLaunch(items_c))
     g_plain = cuda_graph(lambda: [t.launch() for t in plain])
     g_checked = cuda_graph(lambda: [t.launch() for t in checked])
-    g_checked.replay()
+    g_checked[0].replay()
     torch.cuda.synchronize()
     passed = all(bool(r.passed.all()) for t in checked for r in t.results if r is not None)
     t_plain = timed(g_plain, steps, warmup, 1)
@@ -418,7 +429,8 @@ def main() -> None:
         return checked_step
 
     # the other verdict form, for comparison (captured before the launches are re-planned)
-    graph_other = cuda_graph(step_of([*groups, verdict])) if args.verdicts == "carried" else None
+    per_graph = GRAPH_STEPS if args.steps % GRAPH_STEPS == 0 else 1
+    graph_other = cuda_graph(step_of([*groups, verdict]), per_graph) if args.verdicts == "carried" else None
     if args.verdicts == "carried":  # each launch decides the previous one's checks
         for i, g in enumerate(groups):
             g.set_prior([groups[i - 1]])
@@ -433,10 +445,10 @@ def main() -> None:
         if world > 1:
             ex_plain.gather()
 
-    graph_checked = cuda_graph(checked_step)
-    graph_plain = cuda_graph(plain_step)
+    graph_checked = cuda_graph(checked_step, per_graph)
+    graph_plain = cuda_graph(plain_step, per_graph)
     # correctness of the timed path: every block of the honest layer passes
-    graph_checked.replay()
+    graph_checked[0].replay()
     torch.cuda.synchronize()
     all_passed = bool(vs.local.all()) if world == 1 else None
 
@@ -490,7 +502,7 @@ def main() -> None:
                 "launches_per_step": len(launches),
                 "verdicts": VERDICTS[args.verdicts], "parallelism": f"row-shard x{world}" if world > 1 else "single",
                 "l2": "inputs larger than L2 (436 MB of weights per step, 126 MB L2)",
-                "graph": "CUDA graph of one step, replayed",
+                "graph": f"CUDA graph of {per_graph} consecutive steps, replayed",
             },
             "checker_overhead_pct": round((t_checked / t_plain - 1) * 100, 2),
             "unchecked_ms_per_step": round(t_plain * 1e3, 5),

@@ -111,7 +111,7 @@ constexpr int kMaxSlots = 4;                // ring slots per warp
 constexpr int64_t kSegmentTarget = 2048;    // columns per checksum-bank segment
 // Time per byte of a bank segment (binary64 products and sums) relative to a weight row,
 // for the CTA split between the jobs of a launch.
-constexpr double kBankCost = 4.0;
+constexpr double kBankCost = 2.5;
 constexpr int kVerdictTasksPerWarp = 4;  // prior verdicts a warp decides, about
 constexpr int kMaxVerdictCtas = 8;
 
@@ -255,6 +255,8 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
       } else {
         row_piece = std::max<int64_t>(viter, kPieceTarget / viter * viter);
       }
+    } else {
+      row_piece = kPieceTarget;  // checks only: bank pieces of the usual size
     }
     slot_bytes = (std::max<int64_t>(row_piece, 512) + 127) / 128 * 128;
     const int64_t room = pck::kSmemCap - x_bytes - 8 * (pck::kConsumerWarps * kMaxSlots + 1) - 64;
@@ -332,9 +334,24 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
     --assigned;
   }
   int64_t begin = 0;
+  for (int j = 0; j < nj; ++j) begin += cnt[j];
+  if (begin + verdict_ctas > pck::kMaxCtas) {
+    return fail(PCK_ERR_ARGUMENT, "streaming grid of %lld CTAs exceeds %d", static_cast<long long>(begin + verdict_ctas),
+                pck::kMaxCtas);
+  }
+  begin = 0;
   for (int j = 0; j < nj; ++j) {
-    plan.jobs[j].cta_begin = static_cast<int32_t>(begin);
-    plan.jobs[j].cta_count = static_cast<int32_t>(cnt[j]);
+    pck::JobPlan& jb = plan.jobs[j];
+    jb.cta_begin = static_cast<int32_t>(begin);
+    jb.cta_count = static_cast<int32_t>(cnt[j]);
+    if (jb.units > INT32_MAX) return fail(PCK_ERR_ARGUMENT, "a job of %lld units is too large", static_cast<long long>(jb.units));
+    // Each CTA's unit range, from its share of the job's bytes.
+    for (int64_t c = 0; c < cnt[j]; ++c) {
+      const int64_t u0 = pck::first_unit_at(jb, c * jb.total_bytes / cnt[j]);
+      const int64_t u1 = pck::first_unit_at(jb, (c + 1) * jb.total_bytes / cnt[j]);
+      plan.cta_units[begin + c] = make_int2(static_cast<int>(u0), static_cast<int>(u1));
+      plan.cta_job[begin + c] = static_cast<uint8_t>(j);
+    }
     begin += cnt[j];
   }
   plan.njobs = nj;

@@ -65,9 +65,6 @@ struct Unit {
   uint32_t bytes;
 };
 
-__host__ __device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) {
-  return (a + b - 1) / b;
-}
 
 // Unit o of row block beta of a checked job.
 __device__ __forceinline__ Unit decode_checked(const JobPlan& jb, int64_t beta, int64_t o) {
@@ -146,32 +143,6 @@ __device__ __forceinline__ Unit decode_unit(const JobPlan& jb, int64_t u) {
   x.src = jb.a + beta * jb.n + x.col0;
   x.bytes = static_cast<uint32_t>(x.len * 2);
   return x;
-}
-
-// First unit whose starting byte is >= target; units are partitioned between the CTAs of
-// a job by their starting byte, so every CTA finds the same boundaries.
-__device__ __forceinline__ int64_t first_unit_at(const JobPlan& jb, int64_t target) {
-  if (target <= 0) return 0;
-  if (target >= jb.total_bytes) return jb.units;
-  const int64_t unit_bytes = jb.rows * jb.row_bytes;
-  if (!jb.has_check) return ceil_div64(target, unit_bytes);
-  const int64_t beta = target / jb.period_bytes;
-  int64_t rem = target - beta * jb.period_bytes;
-  const int64_t base = beta * jb.period_units;
-  if (rem == 0) return base;
-  const int64_t ru = jb.has_w ? jb.row_units : 0;
-  const int64_t wbytes = jb.has_w ? jb.block * jb.row_bytes : 0;
-  if (rem <= wbytes) return base + ceil_div64(rem, unit_bytes);
-  rem -= wbytes;
-  const int64_t crow = 4 * jb.n;
-  const int64_t cbytes = jb.checks * crow;
-  if (rem <= cbytes) {
-    const int64_t k = rem / crow;
-    const int64_t r3 = rem - k * crow;
-    return base + ru + k * jb.segs + ceil_div64(r3, 4 * jb.seg_len);
-  }
-  rem -= cbytes;
-  return base + ru + static_cast<int64_t>(jb.checks) * jb.segs + ceil_div64(rem, 2 * jb.seg_len);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -936,6 +907,158 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
   for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
 }
 
+// ---------------------------------------------------------------------------------------
+// Bank CTAs: the staged path of a check-only job, with its own lean walk. A warp's units are
+// u0 + warp, + 16, ...; a cursor keeps the unit it stands on decoded and steps to the next
+// without divisions, so a piece costs its arithmetic and little else. Same pieces, same
+// element order and the same partial sums as the generic walk.
+struct BankCursor {
+  int64_t beta;        // row block of the unit
+  int o;               // unit within the block: [checks x segs c-units][segs a-units]
+  int piece;
+  int pieces;          // 0: the walk is over
+  int64_t left;        // units of this warp still to visit, this one included
+  int kind;            // kUnitC or kUnitA
+  int k;               // c-units: check
+  int s;               // segment
+  int col0;
+  int len;             // columns of the segment
+  const uint8_t* src;  // the unit's bytes
+  uint32_t bytes;
+};
+
+__device__ __forceinline__ void bank_load(BankCursor& c, const JobPlan& jb, uint32_t piece_bytes) {
+  c.piece = 0;
+  if (c.left <= 0) {
+    c.pieces = 0;
+    return;
+  }
+  const int segs = jb.segs;
+  const int cs = jb.checks * segs;
+  int o = c.o;
+  if (o < cs) {
+    c.kind = kUnitC;
+    c.k = 0;
+    while (o >= segs) {  // checks is small
+      o -= segs;
+      ++c.k;
+    }
+    c.s = o;
+  } else {
+    c.kind = kUnitA;
+    c.s = o - cs;
+  }
+  c.col0 = c.s * static_cast<int>(jb.seg_len);
+  c.len = static_cast<int>(min(jb.seg_len, jb.n - c.col0));
+  if (c.kind == kUnitC) {
+    c.src = reinterpret_cast<const uint8_t*>(jb.c + (static_cast<int64_t>(c.k) * jb.num_blocks + c.beta) * jb.n + c.col0);
+    c.bytes = static_cast<uint32_t>(c.len) * 4u;
+  } else {
+    c.src = reinterpret_cast<const uint8_t*>(jb.a + c.beta * jb.n + c.col0);
+    c.bytes = static_cast<uint32_t>(c.len) * 2u;
+  }
+  c.pieces = static_cast<int>((c.bytes + piece_bytes - 1) / piece_bytes);
+}
+
+__device__ __forceinline__ void bank_start(BankCursor& c, const JobPlan& jb, int64_t u0, int64_t count, int warp,
+                                           uint32_t piece_bytes) {
+  const int64_t u = u0 + warp;
+  c.beta = u / jb.period_units;
+  c.o = static_cast<int>(u - c.beta * jb.period_units);
+  c.left = warp < count ? (count - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
+  bank_load(c, jb, piece_bytes);
+}
+
+__device__ __forceinline__ void bank_next(BankCursor& c, const JobPlan& jb, uint32_t piece_bytes) {
+  if (++c.piece < c.pieces) return;
+  --c.left;
+  c.o += kConsumerWarps;
+  const int period = static_cast<int>(jb.period_units);
+  while (c.o >= period) {
+    c.o -= period;
+    ++c.beta;
+  }
+  bank_load(c, jb, piece_bytes);
+}
+
+// The bank warp: primes its ring, calls `before_inputs` (producer wait and activations; a
+// negative return means leave), fills the ring, then reduces its units piece by piece.
+template <typename Inputs>
+__device__ __forceinline__ void bank_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots,
+                                          uint32_t slot_bytes, uint8_t* ring, uint64_t* full, uint32_t xs,
+                                          int warp, int lane, Inputs before_inputs) {
+  const uint64_t once = policy_evict_first();
+  const uint32_t piece_bytes = slot_bytes / 512u * 512u;  // a multiple of 128 elements
+  const uint32_t ring_addr = smem_addr(ring);
+  const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
+  BankCursor issue, take;
+  bank_start(issue, jb, u0, count, warp, piece_bytes);
+  take = issue;
+  int64_t issued = 0, taken = 0;
+  auto issue_one = [&]() {
+    const int slot = static_cast<int>(issued % slots);
+    if (lane == 0) {
+      const uint32_t off = static_cast<uint32_t>(issue.piece) * piece_bytes;
+      const uint32_t bytes = min(piece_bytes, issue.bytes - off);
+      mbar_arrive_expect_tx(full + slot, bytes);
+      bulk_load(ring + static_cast<int64_t>(slot) * slot_bytes, issue.src + off, bytes, full + slot, once);
+    }
+    ++issued;
+    bank_next(issue, jb, piece_bytes);
+  };
+  while (issued < min(slots, kPreSlots) && issue.pieces > 0) issue_one();
+  const int mode = before_inputs();
+  while (issued < slots && issue.pieces > 0) issue_one();
+  if (mode < 0) {
+    for (int64_t i = 0; i < issued; ++i) mbar_wait(full + i, 0);
+    return;
+  }
+  double dacc[kSegBatch];  // indexed only by unrolled loops: registers
+  const int64_t nb = jb.num_blocks;
+  while (take.pieces > 0) {
+    const int slot = static_cast<int>(taken % slots);
+    if (!mbar_wait(full + slot, static_cast<uint32_t>((taken / slots) & 1))) break;
+    const uint32_t piece = ring_addr + static_cast<uint32_t>(slot) * slot_bytes;
+    if (take.piece == 0) {
+#pragma unroll
+      for (int b = 0; b < kSegBatch; ++b) dacc[b] = 0.0;
+    }
+    const bool is_c = take.kind == kUnitC;
+    const int per_piece = static_cast<int>(piece_bytes >> (is_c ? 2 : 1));
+    const int e_lo = take.piece * per_piece;
+    const int e_hi = min(e_lo + per_piece, take.len);
+    if (is_c) {
+      segment_piece<false>(dacc, piece, xs, xcol, take.col0, jb.batch, e_lo, e_hi, lane);
+    } else {
+      segment_piece<true>(dacc, piece, xs, xcol, take.col0, jb.batch, e_lo, e_hi, lane);
+    }
+    if (take.piece + 1 == take.pieces) {
+#pragma unroll
+      for (int b = 0; b < kSegBatch; ++b) {
+        if (b >= jb.batch) break;
+        if (is_c) {
+          const double t = warp_sum_rn(dacc[b]);
+          if (lane == 0) {
+            jb.partial_cx[((static_cast<int64_t>(b) * jb.checks + take.k) * nb + take.beta) * jb.seg_alloc + take.s] = t;
+          }
+        } else {
+          const double t = warp_sum_ru(dacc[b]);
+          if (lane == 0) jb.partial_s[(static_cast<int64_t>(b) * nb + take.beta) * jb.seg_alloc + take.s] = t;
+        }
+      }
+    }
+    __syncwarp();
+    ++taken;
+    if (issue.pieces > 0) {  // refill the slot just consumed
+      if (lane == 0) fence_proxy_async_smem();
+      issue_one();
+    }
+    bank_next(take, jb, piece_bytes);
+  }
+  // Leave only after every copy into this warp's slots has landed.
+  for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
+}
+
 // This warp's share of the prior launch's verdict tasks, on the launch's last
 // plan.verdict_ctas CTAs (which stream nothing): task t goes to verdict CTA t % C, warp
 // (t / C) % 16. The caller has waited for the producing kernels.
@@ -1012,14 +1135,11 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
     prior_verdicts(plan, static_cast<int>(threadIdx.x) / kWarp, static_cast<int>(threadIdx.x) % kWarp);
     return;
   }
-  int j = 0;
-  while (j + 1 < plan.njobs && static_cast<int>(blockIdx.x) >= plan.jobs[j + 1].cta_begin) ++j;
-  const JobPlan& jb = plan.jobs[j];
-  const int64_t local = static_cast<int64_t>(blockIdx.x) - jb.cta_begin;
-  if (local >= jb.cta_count) return;
-  const int64_t u0 = first_unit_at(jb, local * jb.total_bytes / jb.cta_count);
-  const int64_t u1 = first_unit_at(jb, (local + 1) * jb.total_bytes / jb.cta_count);
-  const int64_t count = u1 - u0;
+  // The CTA's job and unit range come precomputed (one parameter read, no divisions).
+  const int2 range = plan.cta_units[blockIdx.x];
+  const JobPlan& jb = plan.jobs[plan.cta_job[blockIdx.x]];
+  const int64_t u0 = range.x;
+  const int64_t count = range.y - range.x;
   if (count <= 0) return;  // uniform for the whole CTA
   const int warp = static_cast<int>(threadIdx.x) / kWarp;
   const int lane = static_cast<int>(threadIdx.x) % kWarp;
@@ -1032,10 +1152,12 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
     uint8_t* rings = smem + plan.x_bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(rings + static_cast<int64_t>(kConsumerWarps) * slots * slot_bytes);
     uint32_t* xexp = reinterpret_cast<uint32_t*>(bars + kConsumerWarps * slots);  // [0] smallest, [1] largest exponent of x
-    if (threadIdx.x == 0) {
-      for (int s = 0; s < kConsumerWarps * slots; ++s) mbar_init(bars + s, 1);
-      xexp[0] = 1000;
-      xexp[1] = 0;
+    if (lane == 0) {  // each warp its own ring's barriers
+      for (int s = 0; s < slots; ++s) mbar_init(bars + warp * slots + s, 1);
+      if (warp == 0) {
+        xexp[0] = 1000;
+        xexp[1] = 0;
+      }
       fence_barrier_init();
     }
     __syncthreads();
@@ -1061,7 +1183,11 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
       }
       return jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]) ? 1 : 0;
     };
-    staged_warp<WFMT, NV, BG>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane, inputs);
+    if (jb.has_check && !jb.has_w) {  // a bank CTA (uniform for the CTA)
+      bank_warp(jb, u0, count, slots, slot_bytes, ring, full, xs_addr, warp, lane, inputs);
+    } else {
+      staged_warp<WFMT, NV, BG>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane, inputs);
+    }
   } else {
     // Plain path: every warp takes whole units and reads global memory directly, one
     // element at a time (product, then sum: the same values as the staged path's).

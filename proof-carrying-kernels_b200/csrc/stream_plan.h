@@ -74,9 +74,39 @@ struct JobPlan {
   int64_t period_units;  // units per row block (checked) or 1 (unchecked)
   int64_t period_bytes;  // bytes per period (checked)
   int64_t total_bytes;
-  int32_t cta_begin;
+  int32_t cta_begin;  // the job's CTAs (host bookkeeping; the kernel reads Plan::cta_units)
   int32_t cta_count;
 };
+
+constexpr int kMaxCtas = 320;  // grid limit of a streaming launch (2 per SM without staging)
+
+__host__ __device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// First unit whose starting byte is >= target; units are partitioned between the CTAs of
+// a job by their starting byte (the host fills Plan::cta_units with these boundaries).
+__host__ __device__ __forceinline__ int64_t first_unit_at(const JobPlan& jb, int64_t target) {
+  if (target <= 0) return 0;
+  if (target >= jb.total_bytes) return jb.units;
+  const int64_t unit_bytes = jb.rows * jb.row_bytes;
+  if (!jb.has_check) return ceil_div64(target, unit_bytes);
+  const int64_t beta = target / jb.period_bytes;
+  int64_t rem = target - beta * jb.period_bytes;
+  const int64_t base = beta * jb.period_units;
+  if (rem == 0) return base;
+  const int64_t ru = jb.has_w ? jb.row_units : 0;
+  const int64_t wbytes = jb.has_w ? jb.block * jb.row_bytes : 0;
+  if (rem <= wbytes) return base + ceil_div64(rem, unit_bytes);
+  rem -= wbytes;
+  const int64_t crow = 4 * jb.n;
+  const int64_t cbytes = jb.checks * crow;
+  if (rem <= cbytes) {
+    const int64_t k = rem / crow;
+    const int64_t r3 = rem - k * crow;
+    return base + ru + k * jb.segs + ceil_div64(r3, 4 * jb.seg_len);
+  }
+  rem -= cbytes;
+  return base + ru + static_cast<int64_t>(jb.checks) * jb.segs + ceil_div64(rem, 2 * jb.seg_len);
+}
 
 struct Plan {
   JobPlan jobs[kMaxPlanJobs];
@@ -90,6 +120,8 @@ struct Plan {
   int32_t verdict_ctas;       // (the grid's last CTAs; 0 and grid size: none)
   int64_t prior_tasks;        // verdict tasks of `prior`
   VerdictPlan prior;          // checks of an earlier launch decided by this one
+  int2 cta_units[kMaxCtas];   // CTA c reduces units [x, y) of job cta_job[c]
+  uint8_t cta_job[kMaxCtas];
 };
 
 // Host-side launch of one instantiation family (stream_bf16.cu, stream_e4m3.cu). nv is
