@@ -61,7 +61,7 @@ def measured_peaks() -> dict:
 
 
 def profile_traffic() -> float | None:
-    """DRAM bytes per launch of the streaming kernel from the committed ncu summary."""
+    """DRAM bytes per step (the four streaming launches) from the committed ncu summary."""
     path = ROOT / "profiles" / "stream_kernel_decode_layer.md"
     if not path.exists():
         return None

@@ -272,6 +272,9 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
     plan.stage_bytes = static_cast<int32_t>(slot_bytes);
     plan.x_bytes = static_cast<int32_t>(x_bytes);
     plan.sum_bytes = static_cast<int32_t>(row_piece);
+    bool checked = !prior.empty();
+    for (const Spec* sp : live) checked = checked || sp->check != nullptr;
+    plan.pre_slots = checked ? pck::kPreSlotsChecked : pck::kPreSlotsPlain;
   }
 
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs

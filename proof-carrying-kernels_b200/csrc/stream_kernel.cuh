@@ -984,7 +984,7 @@ __device__ __forceinline__ void bank_next(BankCursor& c, const JobPlan& jb, uint
 // The bank warp: primes its ring, calls `before_inputs` (producer wait and activations; a
 // negative return means leave), fills the ring, then reduces its units piece by piece.
 template <typename Inputs>
-__device__ __forceinline__ void bank_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots,
+__device__ __forceinline__ void bank_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots, int pre_slots,
                                           uint32_t slot_bytes, uint8_t* ring, uint64_t* full, uint32_t xs,
                                           int warp, int lane, Inputs before_inputs) {
   const uint64_t once = policy_evict_first();
@@ -1006,7 +1006,7 @@ __device__ __forceinline__ void bank_warp(const JobPlan& jb, int64_t u0, int64_t
     ++issued;
     bank_next(issue, jb, piece_bytes);
   };
-  while (issued < min(slots, kPreSlots) && issue.pieces > 0) issue_one();
+  while (issued < min(slots, pre_slots) && issue.pieces > 0) issue_one();
   const int mode = before_inputs();
   while (issued < slots && issue.pieces > 0) issue_one();
   if (mode < 0) {
@@ -1077,7 +1077,7 @@ __device__ __forceinline__ void prior_verdicts(const Plan& plan, int warp, int l
 // -1 if that failed, else the arithmetic mode: 0 product then sum, 1 one FMA per exact
 // product, 2 E4M3 weights against binary16 activations), then reduces its units.
 template <int WFMT, int NV, int BG, typename Inputs>
-__device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots,
+__device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots, int pre_slots,
                                             uint32_t slot_bytes, uint32_t row_piece, uint8_t* ring,
                                             uint64_t* full, uint32_t xs, int warp, int lane,
                                             Inputs before_inputs) {
@@ -1100,10 +1100,10 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
       walk_next(issue, jb, u0, count, row_piece, seg_piece);
     }
   };
-  // A few slots before the producers are waited for (weights are never written by a kernel
-  // of this library); the rest after the activations, whose loads would otherwise queue
-  // behind the whole ring's worth of weight requests.
-  prime(min(slots, kPreSlots));
+  // pre_slots slots before the producers are waited for (weights are never written by a
+  // kernel of this library); the rest after the activations, whose loads would otherwise
+  // queue behind the whole ring's worth of weight requests.
+  prime(min(slots, pre_slots));
   const int fma_mode = before_inputs();
   prime(slots);
   if (fma_mode < 0) {  // leave only after the copies into this warp's slots have landed
@@ -1184,9 +1184,10 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
       return jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]) ? 1 : 0;
     };
     if (jb.has_check && !jb.has_w) {  // a bank CTA (uniform for the CTA)
-      bank_warp(jb, u0, count, slots, slot_bytes, ring, full, xs_addr, warp, lane, inputs);
+      bank_warp(jb, u0, count, slots, plan.pre_slots, slot_bytes, ring, full, xs_addr, warp, lane, inputs);
     } else {
-      staged_warp<WFMT, NV, BG>(jb, u0, count, slots, slot_bytes, row_piece, ring, full, xs_addr, warp, lane, inputs);
+      staged_warp<WFMT, NV, BG>(jb, u0, count, slots, plan.pre_slots, slot_bytes, row_piece, ring, full, xs_addr,
+                                warp, lane, inputs);
     }
   } else {
     // Plain path: every warp takes whole units and reads global memory directly, one

@@ -36,7 +36,12 @@ constexpr int kMaxStages = 32;
 constexpr int kSmemCap = 232448;  // 227 KB: the opt-in dynamic shared memory per CTA
 constexpr int kMaxBatch = 16;
 constexpr int kSegBatch = 4;  // staged path: batch columns of a checked job (more: plain path)
-constexpr int kPreSlots = 1;  // staged path: ring slots a warp fills before waiting for producers
+// Staged path: ring slots a warp fills before waiting for the producers. Deeper prefetch keeps
+// HBM busy through the previous launch's tail but delays this launch's activation loads; it
+// pays where the previous launch ends raggedly (launches with checks, whose bank and verdict
+// CTAs finish early), so the host picks per launch (Plan::pre_slots).
+constexpr int kPreSlotsPlain = 1;
+constexpr int kPreSlotsChecked = 2;
 constexpr int kWeightsBf16 = 0;
 constexpr int kWeightsE4m3 = 1;
 
@@ -116,6 +121,7 @@ struct Plan {
   int32_t x_bytes;
   int32_t threads;      // tree parameter T (all W jobs share it)
   int32_t sum_bytes;    // staged path: bytes per row piece (whole vector iterations)
+  int32_t pre_slots;    // staged path: ring slots a warp fills before the producer wait
   int32_t verdict_cta_begin;  // CTAs [verdict_cta_begin, + verdict_ctas) decide `prior`
   int32_t verdict_ctas;       // (the grid's last CTAs; 0 and grid size: none)
   int64_t prior_tasks;        // verdict tasks of `prior`
