@@ -824,8 +824,7 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
   PieceWalk take;
   walk_to(take, jb, u0, warp, count, row_piece, seg_piece);
   int64_t taken = 0;
-  auto issue_one = [&]() {
-    const int slot = static_cast<int>(issued % slots);
+  auto issue_one = [&](int slot) {  // into `slot`, the one just consumed
     if (lane == 0) {
       const Unit iu = walk_unit(issue, jb, u0);
       const uint32_t off = static_cast<uint32_t>(issue.piece) * issue.size;
@@ -840,9 +839,10 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
 
   RowState<WFMT, NV, BG> row;
   double dacc[kSegBatch];  // indexed only by unrolled loops: registers
+  int slot = 0;  // the slot of piece `taken`, and its phase parity
+  uint32_t phase = 0;
   while (take.pieces > 0) {
-    const int slot = static_cast<int>(taken % slots);
-    if (!mbar_wait(full + slot, static_cast<uint32_t>((taken / slots) & 1))) break;
+    if (!mbar_wait(full + slot, phase)) break;
     const uint32_t piece = ring_addr + static_cast<uint32_t>(slot) * slot_bytes;
     const Unit un = walk_unit(take, jb, u0);
     const bool first = take.piece == 0;
@@ -899,7 +899,11 @@ __device__ __forceinline__ void staged_consume(const JobPlan& jb, int64_t u0, in
     ++taken;
     if (issue.pieces > 0) {  // refill the slot just consumed
       if (lane == 0) fence_proxy_async_smem();
-      issue_one();
+      issue_one(slot);
+    }
+    if (++slot == slots) {
+      slot = 0;
+      phase ^= 1u;
     }
     walk_next(take, jb, u0, count, row_piece, seg_piece);
   }
@@ -995,8 +999,7 @@ __device__ __forceinline__ void bank_warp(const JobPlan& jb, int64_t u0, int64_t
   bank_start(issue, jb, u0, count, warp, piece_bytes);
   take = issue;
   int64_t issued = 0, taken = 0;
-  auto issue_one = [&]() {
-    const int slot = static_cast<int>(issued % slots);
+  auto issue_one = [&](int slot) {
     if (lane == 0) {
       const uint32_t off = static_cast<uint32_t>(issue.piece) * piece_bytes;
       const uint32_t bytes = min(piece_bytes, issue.bytes - off);
@@ -1006,18 +1009,19 @@ __device__ __forceinline__ void bank_warp(const JobPlan& jb, int64_t u0, int64_t
     ++issued;
     bank_next(issue, jb, piece_bytes);
   };
-  while (issued < min(slots, pre_slots) && issue.pieces > 0) issue_one();
+  while (issued < min(slots, pre_slots) && issue.pieces > 0) issue_one(static_cast<int>(issued));
   const int mode = before_inputs();
-  while (issued < slots && issue.pieces > 0) issue_one();
+  while (issued < slots && issue.pieces > 0) issue_one(static_cast<int>(issued));
   if (mode < 0) {
     for (int64_t i = 0; i < issued; ++i) mbar_wait(full + i, 0);
     return;
   }
   double dacc[kSegBatch];  // indexed only by unrolled loops: registers
   const int64_t nb = jb.num_blocks;
+  int slot = 0;  // the slot of piece `taken`, and its phase parity
+  uint32_t phase = 0;
   while (take.pieces > 0) {
-    const int slot = static_cast<int>(taken % slots);
-    if (!mbar_wait(full + slot, static_cast<uint32_t>((taken / slots) & 1))) break;
+    if (!mbar_wait(full + slot, phase)) break;
     const uint32_t piece = ring_addr + static_cast<uint32_t>(slot) * slot_bytes;
     if (take.piece == 0) {
 #pragma unroll
@@ -1051,12 +1055,140 @@ __device__ __forceinline__ void bank_warp(const JobPlan& jb, int64_t u0, int64_t
     ++taken;
     if (issue.pieces > 0) {  // refill the slot just consumed
       if (lane == 0) fence_proxy_async_smem();
-      issue_one();
+      issue_one(slot);
+    }
+    if (++slot == slots) {
+      slot = 0;
+      phase ^= 1u;
     }
     bank_next(take, jb, piece_bytes);
   }
   // Leave only after every copy into this warp's slots has landed.
   for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
+}
+
+// ---------------------------------------------------------------------------------------
+// Row CTAs: the staged path of a GEMV job without checks (one row per unit), with a lean walk.
+// A warp's rows are u0 + warp, + 16, ...; every row is `ppr` pieces of row_piece bytes (the
+// last one shorter), so a piece costs its arithmetic plus a few additions. Same pieces, same
+// vector iterations per piece and the same chains as the generic walk.
+struct RowCursor {
+  int64_t row;
+  int piece;
+  int64_t left;  // rows of this warp still to visit, this one included
+};
+
+__device__ __forceinline__ void row_next(RowCursor& c, int ppr) {
+  if (++c.piece < ppr) return;
+  c.piece = 0;
+  c.row += kConsumerWarps;
+  --c.left;
+}
+
+template <int WFMT, int NV, int BG, int kMode>
+__device__ __forceinline__ void row_consume(const JobPlan& jb, int slots, uint32_t slot_bytes, uint32_t row_piece,
+                                            int ppr, uint8_t* ring, uint64_t* full, uint32_t xs, int lane,
+                                            RowCursor issue, RowCursor take, int64_t issued) {
+  constexpr int V = Format<WFMT>::kVec;
+  constexpr int T = NV * kWarp;
+  const uint64_t once = policy_evict_first();
+  const uint32_t ring_addr = smem_addr(ring);
+  const uint32_t xcol = static_cast<uint32_t>(jb.n * 2);
+  const uint32_t row_bytes = static_cast<uint32_t>(jb.row_bytes);
+  const int nvec = static_cast<int>(jb.n / V);
+  const int vtotal = (nvec + T - 1) / T;
+  const uint8_t* W = static_cast<const uint8_t*>(jb.W);
+  RowState<WFMT, NV, BG> st;
+  int64_t taken = 0;
+  int slot = 0;  // the slot of piece `taken`, and its phase parity
+  uint32_t phase = 0;
+  while (take.left > 0) {
+    if (!mbar_wait(full + slot, phase)) break;
+    const uint32_t piece = ring_addr + static_cast<uint32_t>(slot) * slot_bytes;
+    const uint32_t off = static_cast<uint32_t>(take.piece) * row_piece;
+    const uint32_t bytes = min(row_piece, row_bytes - off);
+    const int v_lo = static_cast<int>(off / (T * 16u));
+    const int v_hi = min(static_cast<int>((off + bytes + T * 16u - 1) / (T * 16u)), vtotal);
+    const bool first = take.piece == 0;
+    const bool last = take.piece + 1 == ppr;
+    for (int g0 = 0; g0 < jb.batch; g0 += BG) {
+      if (first) st.reset();
+      reduce_row_piece<WFMT, NV, BG, kMode>(st, piece, xs, xcol, g0, jb.batch, v_lo, v_hi, nvec, lane);
+      if (last) {
+#pragma unroll
+        for (int b = 0; b < BG; ++b) {
+          const float yv = halve_groups<NV>(st.acc[b], lane);
+          if (lane == 0 && g0 + b < jb.batch) jb.Y[static_cast<int64_t>(g0 + b) * jb.m + take.row] = yv;
+        }
+      }
+    }
+    __syncwarp();
+    ++taken;
+    if (issue.left > 0) {  // refill the slot just consumed
+      if (lane == 0) {
+        fence_proxy_async_smem();
+        const uint32_t ioff = static_cast<uint32_t>(issue.piece) * row_piece;
+        const uint32_t ibytes = min(row_piece, row_bytes - ioff);
+        mbar_arrive_expect_tx(full + slot, ibytes);
+        bulk_load(ring + static_cast<int64_t>(slot) * slot_bytes, W + issue.row * jb.row_bytes + ioff, ibytes,
+                  full + slot, once);
+      }
+      ++issued;
+      row_next(issue, ppr);
+    }
+    if (++slot == slots) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    row_next(take, ppr);
+  }
+  // Leave only after every copy into this warp's slots has landed.
+  for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
+}
+
+// The row warp: primes its ring (pre_slots pieces), calls `before_inputs` (producer wait and
+// activations; it returns the arithmetic mode, or -1 to leave), fills the ring, then reduces.
+template <int WFMT, int NV, int BG, typename Inputs>
+__device__ __forceinline__ void row_warp(const JobPlan& jb, int64_t u0, int64_t count, int slots, int pre_slots,
+                                         uint32_t slot_bytes, uint32_t row_piece, uint8_t* ring, uint64_t* full,
+                                         uint32_t xs, int warp, int lane, Inputs before_inputs) {
+  const uint64_t once = policy_evict_first();
+  const int ppr = static_cast<int>((jb.row_bytes + row_piece - 1) / row_piece);
+  const uint8_t* W = static_cast<const uint8_t*>(jb.W);
+  RowCursor issue{u0 + warp, 0, warp < count ? (count - warp + kConsumerWarps - 1) / kConsumerWarps : 0};
+  const RowCursor take = issue;
+  int64_t issued = 0;
+  auto prime = [&](int upto) {
+    for (; issued < upto && issue.left > 0; ++issued) {
+      const int s = static_cast<int>(issued);
+      if (lane == 0) {
+        const uint32_t off = static_cast<uint32_t>(issue.piece) * row_piece;
+        const uint32_t bytes = min(row_piece, static_cast<uint32_t>(jb.row_bytes) - off);
+        mbar_arrive_expect_tx(full + s, bytes);
+        bulk_load(ring + static_cast<int64_t>(s) * slot_bytes, W + issue.row * jb.row_bytes + off, bytes, full + s,
+                  once);
+      }
+      row_next(issue, ppr);
+    }
+  };
+  prime(min(slots, pre_slots));
+  const int mode = before_inputs();
+  prime(slots);
+  if (mode < 0) {  // leave only after the copies into this warp's slots have landed
+    for (int64_t i = 0; i < issued; ++i) mbar_wait(full + i, 0);
+    return;
+  }
+  if constexpr (WFMT == kWeightsE4m3) {
+    if (mode == 2) {
+      row_consume<WFMT, NV, BG, 2>(jb, slots, slot_bytes, row_piece, ppr, ring, full, xs, lane, issue, take, issued);
+      return;
+    }
+  }
+  if (mode) {
+    row_consume<WFMT, NV, BG, 1>(jb, slots, slot_bytes, row_piece, ppr, ring, full, xs, lane, issue, take, issued);
+  } else {
+    row_consume<WFMT, NV, BG, 0>(jb, slots, slot_bytes, row_piece, ppr, ring, full, xs, lane, issue, take, issued);
+  }
 }
 
 // This warp's share of the prior launch's verdict tasks, on the launch's last
@@ -1185,6 +1317,9 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
     };
     if (jb.has_check && !jb.has_w) {  // a bank CTA (uniform for the CTA)
       bank_warp(jb, u0, count, slots, plan.pre_slots, slot_bytes, ring, full, xs_addr, warp, lane, inputs);
+    } else if (!jb.has_check && jb.rows == 1) {  // a row CTA
+      row_warp<WFMT, NV, BG>(jb, u0, count, slots, plan.pre_slots, slot_bytes, row_piece, ring, full, xs_addr, warp,
+                             lane, inputs);
     } else {
       staged_warp<WFMT, NV, BG>(jb, u0, count, slots, plan.pre_slots, slot_bytes, row_piece, ring, full, xs_addr,
                                 warp, lane, inputs);
