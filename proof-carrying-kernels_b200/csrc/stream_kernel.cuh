@@ -1085,6 +1085,69 @@ __device__ __forceinline__ void row_next(RowCursor& c, int ppr) {
   --c.left;
 }
 
+// row_consume for E4M3 rows of exactly one vector iteration (n = 16 * T: the 4096-column
+// projections at 256 threads), batch 1, binary16 activations, one piece per row: chain g of a
+// lane always meets the same 16 activations (vector 32g + lane), so the lane keeps them in
+// registers for all its rows and a row costs one shared load per vector. The terms and their
+// order are those of reduce_row_piece's single iteration.
+template <int NV>
+__device__ __forceinline__ void row_consume_e4m3_xreg(const JobPlan& jb, int slots, uint32_t slot_bytes,
+                                                      uint8_t* ring, uint64_t* full, uint32_t xs, int lane,
+                                                      RowCursor issue, RowCursor take, int64_t issued) {
+  const uint64_t once = policy_evict_first();
+  const uint32_t ring_addr = smem_addr(ring);
+  const uint32_t xhalf = static_cast<uint32_t>(jb.n);  // second halves, n bytes on (load_activations)
+  const uint32_t row_bytes = static_cast<uint32_t>(jb.row_bytes);
+  const uint8_t* W = static_cast<const uint8_t*>(jb.W);
+  uint4 xa[NV], xb[NV];
+#pragma unroll
+  for (int g = 0; g < NV; ++g) {
+    const uint32_t q = static_cast<uint32_t>(g * kWarp + lane) * 16u;
+    xa[g] = lds128(xs + q);
+    xb[g] = lds128(xs + xhalf + q);
+  }
+  int64_t taken = 0;
+  int slot = 0;  // the slot of piece `taken`, and its phase parity
+  uint32_t phase = 0;
+  while (take.left > 0) {
+    if (!mbar_wait(full + slot, phase)) break;
+    const uint32_t piece = ring_addr + static_cast<uint32_t>(slot) * slot_bytes;
+    float acc[NV];
+#pragma unroll
+    for (int g = 0; g < NV; ++g) acc[g] = -0.0f;  // -0 + p == p for every p
+    constexpr int kStep = NV < 4 ? NV : 4;
+#pragma unroll
+    for (int g0 = 0; g0 < NV; g0 += kStep) {
+      uint4 wv[kStep];
+#pragma unroll
+      for (int g = 0; g < kStep; ++g) wv[g] = lds128(piece + static_cast<uint32_t>((g0 + g) * kWarp + lane) * 16u);
+#pragma unroll
+      for (int g = 0; g < kStep; ++g) chain_e4m3_half(acc[g0 + g], wv[g], xa[g0 + g], xb[g0 + g]);
+    }
+    const float yv = halve_groups<NV>(acc, lane);
+    if (lane == 0) jb.Y[take.row] = yv;
+    __syncwarp();
+    ++taken;
+    if (issue.left > 0) {  // refill the slot just consumed
+      if (lane == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(full + slot, row_bytes);
+        bulk_load(ring + static_cast<int64_t>(slot) * slot_bytes, W + issue.row * jb.row_bytes, row_bytes,
+                  full + slot, once);
+      }
+      ++issued;
+      row_next(issue, 1);
+    }
+    if (++slot == slots) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    row_next(take, 1);
+  }
+  // Leave only after every copy into this warp's slots has landed.
+  for (int64_t i = taken; i < issued; ++i) mbar_wait(full + i % slots, static_cast<uint32_t>((i / slots) & 1));
+}
+
 template <int WFMT, int NV, int BG, int kMode>
 __device__ __forceinline__ void row_consume(const JobPlan& jb, int slots, uint32_t slot_bytes, uint32_t row_piece,
                                             int ppr, uint8_t* ring, uint64_t* full, uint32_t xs, int lane,
@@ -1180,7 +1243,11 @@ __device__ __forceinline__ void row_warp(const JobPlan& jb, int64_t u0, int64_t 
   }
   if constexpr (WFMT == kWeightsE4m3) {
     if (mode == 2) {
-      row_consume<WFMT, NV, BG, 2>(jb, slots, slot_bytes, row_piece, ppr, ring, full, xs, lane, issue, take, issued);
+      if (jb.batch == 1 && ppr == 1 && jb.n == 16 * NV * kWarp) {
+        row_consume_e4m3_xreg<NV>(jb, slots, slot_bytes, ring, full, xs, lane, issue, take, issued);
+      } else {
+        row_consume<WFMT, NV, BG, 2>(jb, slots, slot_bytes, row_piece, ppr, ring, full, xs, lane, issue, take, issued);
+      }
       return;
     }
   }
