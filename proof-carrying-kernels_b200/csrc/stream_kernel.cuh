@@ -573,7 +573,12 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
   for (int v = v_lo; v < v_hi; ++v) {
     const uint32_t wbase = piece + static_cast<uint32_t>((v - v_lo) * T + lane) * 16u;
     const uint32_t xoff = static_cast<uint32_t>(v * T + lane) * kXV;
-    if ((v + 1) * T > nvec) {  // the last, partial iteration: padding past n adds +0
+    // Vectors of this iteration inside the row (all T but in the last one). Chains past the
+    // row's end add +0. A partial iteration whose valid vectors fill whole blocks of kStep
+    // groups (the 14336-column E4M3 rows: 4 of 8 groups) takes the grouped path below.
+    constexpr int kStep = NV < 4 ? NV : 4;
+    const int valid = nvec - v * T;
+    if (valid < T && valid % (kStep * kWarp) != 0) {  // a ragged last iteration, lane by lane
       const int qbase = v * T + lane;
 #pragma unroll
       for (int g = 0; g < NV; ++g) {
@@ -596,9 +601,15 @@ __device__ __forceinline__ void reduce_row_piece(RowState<WFMT, NV, BG>& st, uin
       continue;
     }
     // chain groups four at a time: their loads together, then their terms interleaved
-    constexpr int kStep = NV < 4 ? NV : 4;
 #pragma unroll
     for (int g0w = 0; g0w < NV; g0w += kStep) {
+      if (g0w * kWarp >= valid) {  // past the row's end (uniform for the warp)
+#pragma unroll
+        for (int b = 0; b < BG; ++b)
+#pragma unroll
+          for (int g = 0; g < kStep; ++g) st.acc[b][g0w + g] = __fadd_rn(st.acc[b][g0w + g], 0.0f);
+        continue;
+      }
       uint4 wv[kStep];
 #pragma unroll
       for (int g = 0; g < kStep; ++g) wv[g] = lds128(wbase + (g0w + g) * (kWarp * 16u));
