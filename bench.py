@@ -60,9 +60,11 @@ def measured_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
 
 
-def profile_traffic() -> float | None:
-    """DRAM bytes per step (the four streaming launches) from the committed ncu summary."""
-    path = ROOT / "profiles" / "stream_kernel_decode_layer.md"
+def profile_traffic(weights: str = "bf16") -> float | None:
+    """DRAM bytes per step (the four streaming launches) from the committed ncu summary of
+    the same weight format."""
+    name = "stream_kernel_decode_layer.md" if weights == "bf16" else f"stream_kernel_decode_layer_{weights}.md"
+    path = ROOT / "profiles" / name
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
@@ -476,7 +478,7 @@ def main() -> None:
     value = step_bytes / t_checked / 1e9
     peaks = measured_peaks()
     peak = float(peaks["hbm_gbs"])
-    traffic = profile_traffic()
+    traffic = profile_traffic(args.weights)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.weights == "bf16":
