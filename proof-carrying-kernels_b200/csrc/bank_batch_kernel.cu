@@ -5,11 +5,15 @@
 // with exact products (binary32 x bfloat16 and bfloat16 x bfloat16 are exact in binary64).
 //
 // This is a small binary64 matrix product, bank rows x batch columns, done on the CUDA cores:
-// a CTA takes 32 bank rows of one kind, 32 batch columns and one segment, widens 32 columns
-// of the rows and of X to binary64 in shared memory at a time (the global loads of the next
-// round are in flight meanwhile), and each of its 256 threads accumulates 2 rows x 2 columns
-// (rows ty + 16i, columns tx + 16q: neighbouring threads read neighbouring words) in a fixed
-// order. The verdict kernel (verdict_kernel.cu) adds the segments and decides the blocks.
+// a CTA takes 32 bank rows of one kind, 32 batch columns and one segment, and widens 32
+// columns j of the rows and of X to binary64 in shared memory at a time (the global loads of
+// the next round are in flight meanwhile). Its 256 threads form four groups of 64; group g
+// takes the columns j = 8g .. 8g+7 of every round, and each thread accumulates 4 rows x 4
+// batch columns (rows 4ty + i, columns tx + 8q) over them, j ascending: 8 shared loads per 16
+// binary64 FMAs. At the end the four group sums of every output are added in group order
+// (rounded up for bound rows), a fixed order like the rest; the binary64 bound holds for any
+// split of a segment no deeper than its serial sum. The verdict kernel (verdict_kernel.cu)
+// adds the segments and decides the blocks.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -23,6 +27,8 @@ namespace {
 constexpr int kRows = 32;   // bank rows per CTA
 constexpr int kCols = 32;   // batch columns per CTA
 constexpr int kChunk = 32;  // columns of the bank (j) per shared-memory round
+constexpr int kGroups = 4;  // thread groups splitting a round's columns
+constexpr int kPerGroup = kChunk / kGroups;
 
 // One round's raw values: each thread fetches 4 bank values (rows t/32 + 8i, column t%32)
 // and 4 activations (batch columns t/32 + 8i), fetched a round ahead of their use.
@@ -56,6 +62,7 @@ __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__
   // one padding word per line: the 32 lanes of a warp store one bank column j each
   __shared__ double rows_s[kChunk][kRows + 1];
   __shared__ double x_s[kChunk][kCols + 1];
+  __shared__ double red[kGroups - 1][kRows][kCols + 1];  // sums of groups 1..3
   int j = 0;
   while (j + 1 < plan.njobs && static_cast<int>(blockIdx.x) >= plan.jobs[j + 1].tile_begin) ++j;
   const BankBatchJob& jb = plan.jobs[j];
@@ -70,12 +77,13 @@ __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__
   const int64_t j0 = static_cast<int64_t>(seg) * jb.seg_len;
   const int64_t j1 = min(jb.n, j0 + jb.seg_len);
   const int t = static_cast<int>(threadIdx.x);
-  const int ty = t / 16, tx = t % 16;  // rows ty + 16i (i < 2), columns tx + 16q (q < 2)
-  double acc[2][2];
+  const int grp = t / 64, u = t % 64;
+  const int ty = u / 8, tx = u % 8;  // rows 4ty + i, columns tx + 8q (i, q < 4)
+  double acc[4][4];
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
+  for (int i = 0; i < 4; ++i) {
 #pragma unroll
-    for (int q = 0; q < 2; ++q) acc[i][q] = 0.0;
+    for (int q = 0; q < 4; ++q) acc[i][q] = 0.0;
   }
   Round rd;
   fetch_round(jb, bound, nrows, row0, b0, j0, j1, t, rd);
@@ -93,50 +101,57 @@ __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__
     }
     __syncthreads();
     if (jc + kChunk < j1) fetch_round(jb, bound, nrows, row0, b0, jc + kChunk, j1, t, rd);  // next round in flight
-    if (bound) {
-#pragma unroll 8
-      for (int k = 0; k < kChunk; ++k) {
-        double rv[2], xv[2];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) rv[i] = rows_s[k][ty + 16 * i];
+    for (int kk = 0; kk < kPerGroup; ++kk) {
+      const int k = grp * kPerGroup + kk;
+      double rv[4], xv[4];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) xv[q] = x_s[k][tx + 16 * q];
+      for (int i = 0; i < 4; ++i) rv[i] = rows_s[k][4 * ty + i];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
+      for (int q = 0; q < 4; ++q) xv[q] = x_s[k][tx + 8 * q];
+      if (bound) {
 #pragma unroll
-          for (int q = 0; q < 2; ++q) acc[i][q] = __fma_ru(rv[i], xv[q], acc[i][q]);
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[i][q] = __fma_ru(rv[i], xv[q], acc[i][q]);
         }
-      }
-    } else {
-#pragma unroll 8
-      for (int k = 0; k < kChunk; ++k) {
-        double rv[2], xv[2];
+      } else {
 #pragma unroll
-        for (int i = 0; i < 2; ++i) rv[i] = rows_s[k][ty + 16 * i];
+        for (int i = 0; i < 4; ++i) {
 #pragma unroll
-        for (int q = 0; q < 2; ++q) xv[q] = x_s[k][tx + 16 * q];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-#pragma unroll
-          for (int q = 0; q < 2; ++q) acc[i][q] = __fma_rn(rv[i], xv[q], acc[i][q]);
+          for (int q = 0; q < 4; ++q) acc[i][q] = __fma_rn(rv[i], xv[q], acc[i][q]);
         }
       }
     }
     __syncthreads();
   }
+  // Groups 1..3 hand their sums to group 0, which adds them in group order.
+  if (grp > 0) {
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int64_t row = row0 + ty + 16 * i;
-    if (row >= nrows) continue;
+    for (int i = 0; i < 4; ++i) {
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int b = b0 + tx + 16 * q;
-      if (b >= jb.batch) continue;
+      for (int q = 0; q < 4; ++q) red[grp - 1][4 * ty + i][tx + 8 * q] = acc[i][q];
+    }
+  }
+  __syncthreads();
+  if (grp > 0) return;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = row0 + 4 * ty + i;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      double v = acc[i][q];
+#pragma unroll
+      for (int g = 0; g < kGroups - 1; ++g) {
+        v = bound ? __dadd_ru(v, red[g][4 * ty + i][tx + 8 * q]) : __dadd_rn(v, red[g][4 * ty + i][tx + 8 * q]);
+      }
+      const int b = b0 + tx + 8 * q;
+      if (row >= nrows || b >= jb.batch) continue;
       if (bound) {
-        jb.partial_s[(static_cast<int64_t>(b) * jb.nb + row) * jb.seg_alloc + seg] = acc[i][q];
+        jb.partial_s[(static_cast<int64_t>(b) * jb.nb + row) * jb.seg_alloc + seg] = v;
       } else {
         // row = k * nb + beta, and partial_cx is (batch, checks, nb, seg_alloc)
-        jb.partial_cx[(static_cast<int64_t>(b) * jb.checks * jb.nb + row) * jb.seg_alloc + seg] = acc[i][q];
+        jb.partial_cx[(static_cast<int64_t>(b) * jb.checks * jb.nb + row) * jb.seg_alloc + seg] = v;
       }
     }
   }
