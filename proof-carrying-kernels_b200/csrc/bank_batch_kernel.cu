@@ -14,6 +14,11 @@
 // (rounded up for bound rows), a fixed order like the rest; the binary64 bound holds for any
 // split of a segment no deeper than its serial sum. The verdict kernel (verdict_kernel.cu)
 // adds the segments and decides the blocks.
+//
+// It is launched as a programmatic dependent of the tensor-core kernel, whose outputs it
+// does not read (its inputs, X and the bank, were final before that kernel started), so its
+// CTAs may run beside it on free SMs. Every CTA waits for that kernel before it exits: the
+// bank grid completes only after the GEMV, so the verdict kernel's wait covers both.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -68,12 +73,18 @@ __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__
   const BankBatchJob& jb = plan.jobs[j];
   const int tile = static_cast<int>(blockIdx.x) - jb.tile_begin;
   const int seg = static_cast<int>(blockIdx.z);
-  if (seg >= jb.segs) return;  // uniform
+  if (seg >= jb.segs) {  // uniform
+    wait_for_producers();
+    return;
+  }
   const bool bound = tile >= jb.c_tiles;  // a rows: |x|, rounded up
   const int64_t nrows = bound ? jb.nb : static_cast<int64_t>(jb.checks) * jb.nb;
   const int64_t row0 = static_cast<int64_t>(bound ? tile - jb.c_tiles : tile) * kRows;
   const int b0 = static_cast<int>(blockIdx.y) * kCols;
-  if (b0 >= jb.batch) return;
+  if (b0 >= jb.batch) {
+    wait_for_producers();
+    return;
+  }
   const int64_t j0 = static_cast<int64_t>(seg) * jb.seg_len;
   const int64_t j1 = min(jb.n, j0 + jb.seg_len);
   const int t = static_cast<int>(threadIdx.x);
@@ -134,7 +145,10 @@ __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__
     }
   }
   __syncthreads();
-  if (grp > 0) return;
+  if (grp > 0) {
+    wait_for_producers();
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int64_t row = row0 + 4 * ty + i;
@@ -155,6 +169,7 @@ __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__
       }
     }
   }
+  wait_for_producers();
 }
 
 }  // namespace
@@ -162,8 +177,16 @@ __global__ void __launch_bounds__(256) bank_batch_kernel(const __grid_constant__
 cudaError_t launch_bank_batch(const BankBatchPlan& plan, int col_groups, int max_segs, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(plan.total_tiles), static_cast<unsigned>(col_groups),
                   static_cast<unsigned>(max_segs));
-  bank_batch_kernel<<<grid, 256, 0, stream>>>(plan);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, bank_batch_kernel, plan);
 }
 
 }  // namespace pck

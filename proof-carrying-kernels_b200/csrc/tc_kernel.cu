@@ -93,6 +93,9 @@ __device__ __forceinline__ int job_of(const TcPlan& plan, int tile) {
 // The persistent form (splits == 1 and many tiles): a CTA per SM walks the tiles with two
 // tensor-memory accumulators, so the epilogue of one tile overlaps the main loop of the next.
 __global__ void __launch_bounds__(kTcThreads, 1) tc_persistent_kernel(const __grid_constant__ TcPlan plan) {
+  // The bank kernel that follows (launched as a programmatic dependent) reads nothing this
+  // kernel writes, so it may start on the SMs this grid leaves free.
+  allow_dependents();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -221,6 +224,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_persistent_kernel(const __gr
 
 // The split form: one tile per cluster of `splits` CTAs, each a range of the tile's K blocks.
 __global__ void __launch_bounds__(kTcThreads, 1) tc_split_kernel(const __grid_constant__ TcPlan plan) {
+  allow_dependents();  // as in tc_persistent_kernel
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
