@@ -182,9 +182,16 @@ def build_layer(args, rank: int, world: int, device: torch.device):
     return groups, verdict, plain, xs, ex, ex_plain
 
 
-# Consecutive layer steps captured in one CUDA graph (a decode graph holds every layer of the
-# model, so only one step in this many pays the graph launch boundary).
-GRAPH_STEPS = 8
+# Consecutive layer steps captured in one CUDA graph at most: a decode graph holds every
+# layer of the model (Llama-3-8B has 32), so only one step in that many pays the graph
+# launch boundary.
+GRAPH_STEPS = 32
+
+
+def graph_steps(steps: int) -> int:
+    """Steps per captured graph: the largest divisor of ``steps`` up to GRAPH_STEPS, so the
+    timed region replays whole graphs and holds exactly ``steps`` steps."""
+    return max(d for d in range(1, min(steps, GRAPH_STEPS) + 1) if steps % d == 0)
 
 
 def cuda_graph(fn, steps: int = 1) -> tuple[torch.cuda.CUDAGraph, int]:
@@ -431,7 +438,7 @@ def main() -> None:
         return checked_step
 
     # the other verdict form, for comparison (captured before the launches are re-planned)
-    per_graph = GRAPH_STEPS if args.steps % GRAPH_STEPS == 0 else 1
+    per_graph = graph_steps(args.steps)
     graph_other = cuda_graph(step_of([*groups, verdict]), per_graph) if args.verdicts == "carried" else None
     if args.verdicts == "carried":  # each launch decides the previous one's checks
         for i, g in enumerate(groups):

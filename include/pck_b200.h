@@ -31,11 +31,21 @@ extern "C" {
 
 #define PCK_WEIGHTS_BF16 0
 #define PCK_WEIGHTS_E4M3 1
+/*
+ * Flag OR-ed into a job's weight_format: the weights were written before the kernel that
+ * precedes this call on its stream began (e.g. loaded at start-up, followed by a
+ * synchronize). The streaming kernel then requests its first weight pieces while that
+ * kernel is still running (programmatic dependent launch); without the flag it waits for
+ * the preceding kernel to complete before reading any weight, as it always does for the
+ * checksum bank (c, a) and the activations. A caller that sets the flag while the
+ * preceding kernel writes W can get stale weights and false alarms.
+ */
+#define PCK_WEIGHTS_SETTLED 0x100
 
 /* Message of the last failing call on this thread ("" if none). */
 const char* pck_last_error(void);
 
-/* ABI version of this library (increases when a declaration here changes): 3. */
+/* ABI version of this library (increases when a declaration here changes): 4. */
 int pck_abi_version(void);
 
 /*
@@ -133,7 +143,8 @@ int pck_blocked_check(const pck_check_desc* descs, int count, void* stream);
 
 /*
  * One GEMV, optionally checked in the same pass over memory.
- * weight_format: PCK_WEIGHTS_BF16 (vec 8) or PCK_WEIGHTS_E4M3 (vec 16).
+ * weight_format: PCK_WEIGHTS_BF16 (vec 8) or PCK_WEIGHTS_E4M3 (vec 16), optionally OR-ed
+ * with PCK_WEIGHTS_SETTLED.
  * If `check` is not NULL, its x and y must equal this job's X and Y; the streaming kernel
  * reduces the job's bank rows against x together with W (fused production mode), and the
  * verdict of each row block is then computed from the y values as stored in memory.
@@ -210,7 +221,9 @@ int pck_check_verdicts(const pck_check_desc* descs, int count, void* stream);
  * contents: calls whose work overlaps on the GPU (different streams or host threads) race
  * and must be ordered by the caller. The first call on each device (with that device
  * current) looks up the array's address with cudaGetSymbolAddress; make that first call
- * before any stream capture. No counterpart in the reference.
+ * before any stream capture. A later call that finds another context current on the device
+ * (after cudaDeviceReset, or under a driver-API context) looks the address up again.
+ * No counterpart in the reference.
  */
 #define PCK_STATIC_SCRATCH_BYTES (4 << 20)
 int pck_gemv_checked_static(const pck_gemv_job* jobs, int count, void* stream);

@@ -80,6 +80,7 @@ struct Spec {
   int threads;
   int wfmt;
   bool has_w;
+  bool settled;  // PCK_WEIGHTS_SETTLED: weights may be read before the producer wait
   const pck_check_desc* check;
   int w_exp_min;
   int w_exp_max;
@@ -274,7 +275,11 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
     plan.sum_bytes = static_cast<int32_t>(row_piece);
     bool checked = !prior.empty();
     for (const Spec* sp : live) checked = checked || sp->check != nullptr;
-    plan.pre_slots = checked ? pck::kPreSlotsChecked : pck::kPreSlotsPlain;
+    // Weight pieces before the producer wait only when every job's weights are settled (the
+    // bank CTAs never read before it: the bank may come from the kernel just before).
+    bool settled = true;
+    for (const Spec* sp : live) settled = settled && (!sp->has_w || sp->settled);
+    plan.pre_slots = !settled ? 0 : checked ? pck::kPreSlotsChecked : pck::kPreSlotsPlain;
   }
 
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs
@@ -480,7 +485,7 @@ extern "C" {
 
 const char* pck_last_error(void) { return g_error.c_str(); }
 
-int pck_abi_version(void) { return 3; }
+int pck_abi_version(void) { return 4; }
 
 int pck_device_status(unsigned int* status, int clear) {
   if (!status) return fail(PCK_ERR_ARGUMENT, "status must not be NULL");
@@ -517,7 +522,7 @@ int pck_gemv_batched(int weight_format, const void* W, const void* X, float* Y, 
     return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %lld", pck::kMaxBatch, static_cast<long long>(batch));
   }
   if (m == 0) return ok();
-  std::vector<Spec> specs{{W, X, Y, m, n, static_cast<int>(batch), threads, weight_format, true, nullptr, 0, 0}};
+  std::vector<Spec> specs{{W, X, Y, m, n, static_cast<int>(batch), threads, weight_format, true, false, nullptr, 0, 0}};
   return run_stream(specs, static_cast<cudaStream_t>(stream));
 }
 
@@ -539,7 +544,7 @@ int pck_blocked_check(const pck_check_desc* descs, int count, void* stream) {
   for (int i = 0; i < count; ++i) {
     if (int rc = validate_check(descs + i)) return rc;
     specs.push_back(Spec{nullptr, nullptr, nullptr, 0, descs[i].n, descs[i].batch, 256,
-                         PCK_WEIGHTS_BF16, false, descs + i, 0, 0});
+                         PCK_WEIGHTS_BF16, false, false, descs + i, 0, 0});
   }
   if (int rc = run_stream(specs, static_cast<cudaStream_t>(stream))) return rc;
   const pck_check_desc* checks[PCK_MAX_JOBS];
@@ -562,7 +567,8 @@ int pck_gemv_pipelined(const pck_gemv_job* jobs, int count, const pck_check_desc
   std::vector<Spec> specs;
   for (int i = 0; i < count; ++i) {
     const pck_gemv_job& jb = jobs[i];
-    if (jb.weight_format != PCK_WEIGHTS_BF16 && jb.weight_format != PCK_WEIGHTS_E4M3) {
+    const int wfmt = jb.weight_format & ~PCK_WEIGHTS_SETTLED;
+    if (wfmt != PCK_WEIGHTS_BF16 && wfmt != PCK_WEIGHTS_E4M3) {
       return fail(PCK_ERR_ARGUMENT, "unknown weight format %d", jb.weight_format);
     }
     if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, jb.threads, 32)) return rc;
@@ -577,8 +583,8 @@ int pck_gemv_pipelined(const pck_gemv_job* jobs, int count, const pck_check_desc
         return fail(PCK_ERR_ARGUMENT, "a fused check must cover the job's own x, y and shape");
       }
     }
-    specs.push_back(Spec{jb.W, jb.X, jb.Y, jb.m, jb.n, jb.batch, jb.threads, jb.weight_format,
-                         true, jb.check, jb.w_exp_min, jb.w_exp_max});
+    specs.push_back(Spec{jb.W, jb.X, jb.Y, jb.m, jb.n, jb.batch, jb.threads, wfmt, true,
+                         (jb.weight_format & PCK_WEIGHTS_SETTLED) != 0, jb.check, jb.w_exp_min, jb.w_exp_max});
   }
   std::vector<const pck_check_desc*> before;
   for (int i = 0; i < nprior; ++i) {
@@ -747,7 +753,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   int tiles = 0, nj = 0;
   for (int i = 0; i < count; ++i) {
     const pck_gemv_job& jb = jobs[i];
-    if (jb.weight_format != PCK_WEIGHTS_BF16) {
+    if ((jb.weight_format & ~PCK_WEIGHTS_SETTLED) != PCK_WEIGHTS_BF16) {
       return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV takes bfloat16 weights only");
     }
     if (jb.batch != batch) return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the batch");

@@ -17,10 +17,12 @@
 // order them.
 //
 // The address of the array on a device is looked up by the first call made while that
-// device is current, and cached; that first call should come before any stream capture.
+// device is current, and cached together with the device's current context; that first call
+// should come before any stream capture. A call that finds another context current on the
+// device (after cudaDeviceReset, or under a context of the driver API) looks it up again.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
-#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -43,8 +45,28 @@ constexpr int64_t kRegionAlign = 256;
 constexpr int64_t kLimit = PCK_STATIC_SCRATCH_BYTES;
 constexpr int64_t kSaturated = INT64_MAX / 4;
 
+// Per device: the context the address was looked up in, and the address.
+struct Cached {
+  CUcontext ctx;
+  unsigned char* base;
+};
 std::mutex g_setup;
-std::atomic<unsigned char*> g_base[kMaxDevices];
+Cached g_cache[kMaxDevices];
+
+// cuCtxGetCurrent from the driver, through the runtime (no link against libcuda).
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+CtxGetCurrent ctx_get_current() {
+  static CtxGetCurrent fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      return reinterpret_cast<CtxGetCurrent>(p);
+    }
+    return static_cast<CtxGetCurrent>(nullptr);
+  }();
+  return fn;
+}
 
 __attribute__((format(printf, 2, 3))) int reject(int code, const char* fmt, ...) {
   char msg[256];
@@ -55,7 +77,7 @@ __attribute__((format(printf, 2, 3))) int reject(int code, const char* fmt, ...)
   return pck::report_error(code, msg);
 }
 
-// Address of the array on the current device (looked up once per device).
+// Address of the array on the current device, looked up once per device and context.
 int scratch_base(unsigned char** base) {
   int dev = -1;
   cudaError_t err = cudaGetDevice(&dev);
@@ -63,22 +85,26 @@ int scratch_base(unsigned char** base) {
   if (dev < 0 || dev >= kMaxDevices) {
     return reject(PCK_ERR_UNSUPPORTED, "device %d is beyond the %d devices served", dev, kMaxDevices);
   }
-  unsigned char* p = g_base[dev].load(std::memory_order_acquire);
-  if (!p) {
-    std::lock_guard<std::mutex> lock(g_setup);
-    p = g_base[dev].load(std::memory_order_relaxed);
-    if (!p) {
-      void* addr = nullptr;
-      err = cudaGetSymbolAddress(&addr, g_static_scratch);
-      if (err != cudaSuccess || !addr) {
-        return reject(PCK_ERR_CUDA, "static scratch set-up failed: %s",
-                      err != cudaSuccess ? cudaGetErrorString(err) : "no address");
-      }
-      p = static_cast<unsigned char*>(addr);
-      g_base[dev].store(p, std::memory_order_release);
+  const CtxGetCurrent current = ctx_get_current();
+  if (!current) return reject(PCK_ERR_CUDA, "static scratch set-up failed: cuCtxGetCurrent is unavailable");
+  CUcontext ctx = nullptr;  // NULL until the runtime has made a context current on this thread
+  if (current(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  std::lock_guard<std::mutex> lock(g_setup);
+  Cached& entry = g_cache[dev];
+  if (!ctx || !entry.base || entry.ctx != ctx) {
+    void* addr = nullptr;
+    err = cudaGetSymbolAddress(&addr, g_static_scratch);  // makes the primary context current if none is
+    if (err != cudaSuccess || !addr) {
+      return reject(PCK_ERR_CUDA, "static scratch set-up failed: %s",
+                    err != cudaSuccess ? cudaGetErrorString(err) : "no address");
     }
+    if (current(&ctx) != CUDA_SUCCESS || !ctx) {
+      return reject(PCK_ERR_CUDA, "static scratch set-up failed: no current context");
+    }
+    entry.ctx = ctx;
+    entry.base = static_cast<unsigned char*>(addr);
   }
-  *base = p;
+  *base = entry.base;
   return PCK_OK;
 }
 

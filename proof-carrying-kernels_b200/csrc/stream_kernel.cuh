@@ -1281,8 +1281,8 @@ __device__ __forceinline__ void prior_verdicts(const Plan& plan, int warp, int l
   }
 }
 
-// A warp's stream: primes its ring with weight pieces (weights are never written by a
-// kernel of this library, so this may overlap the previous kernel), then calls
+// A warp's stream: primes its ring with up to pre_slots weight pieces (settled weights only,
+// which the previous kernel does not write, so this may overlap it), then calls
 // `before_inputs` (which waits for the producers and brings in the activations; it returns
 // -1 if that failed, else the arithmetic mode: 0 product then sum, 1 one FMA per exact
 // product, 2 E4M3 weights against binary16 activations), then reduces its units.
@@ -1310,9 +1310,9 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
       walk_next(issue, jb, u0, count, row_piece, seg_piece);
     }
   };
-  // pre_slots slots before the producers are waited for (weights are never written by a
-  // kernel of this library); the rest after the activations, whose loads would otherwise
-  // queue behind the whole ring's worth of weight requests.
+  // pre_slots slots before the producers are waited for (only settled weights, which the
+  // preceding kernel does not write); the rest after the activations, whose loads would
+  // otherwise queue behind the whole ring's worth of weight requests.
   prime(min(slots, pre_slots));
   const int fma_mode = before_inputs();
   prime(slots);
@@ -1394,12 +1394,15 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
       return jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]) ? 1 : 0;
     };
     if (jb.has_check && !jb.has_w) {  // a bank CTA (uniform for the CTA)
-      bank_warp(jb, u0, count, slots, plan.pre_slots, slot_bytes, ring, full, xs_addr, warp, lane, inputs);
+      // No bank piece before the producer wait: c and a may come from the kernel just before
+      // (pck_bank_build), whose writes are visible only after griddepcontrol.wait.
+      bank_warp(jb, u0, count, slots, 0, slot_bytes, ring, full, xs_addr, warp, lane, inputs);
     } else if (!jb.has_check && jb.rows == 1) {  // a row CTA
       row_warp<WFMT, NV, BG>(jb, u0, count, slots, plan.pre_slots, slot_bytes, row_piece, ring, full, xs_addr, warp,
                              lane, inputs);
     } else {
-      staged_warp<WFMT, NV, BG>(jb, u0, count, slots, plan.pre_slots, slot_bytes, row_piece, ring, full, xs_addr,
+      staged_warp<WFMT, NV, BG>(jb, u0, count, slots, jb.has_check ? 0 : plan.pre_slots, slot_bytes, row_piece,
+                                ring, full, xs_addr,
                                 warp, lane, inputs);
     }
   } else {

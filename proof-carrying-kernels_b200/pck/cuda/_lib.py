@@ -15,6 +15,7 @@ LIBRARY = Path(__file__).resolve().parent.parent / "_lib" / "libpck_b200.so"
 PCK_OK = 0
 PCK_WEIGHTS_BF16 = 0
 PCK_WEIGHTS_E4M3 = 1
+PCK_WEIGHTS_SETTLED = 0x100  # weights written before the preceding kernel began
 MAX_JOBS = 16  # PCK_MAX_JOBS
 MAX_BATCH = 16
 STATIC_SCRATCH_BYTES = 4 << 20  # PCK_STATIC_SCRATCH_BYTES

@@ -10,6 +10,7 @@ launch with its checks fused.
 from __future__ import annotations
 
 import ctypes
+import math
 from collections.abc import Sequence
 
 import torch
@@ -90,6 +91,12 @@ class GemvLaunch:
                 out = (p.view(out[0].shape), out[1], out[2])
             self.results.append(CheckResult(*out))
             job.check = ctypes.pointer(self._descs[g])
+        # The weights are final from here on (a launch object is made at weight load), so the
+        # streaming kernel may request its first weight pieces before the preceding kernel on
+        # the stream has finished.
+        torch.cuda.synchronize(self.device)
+        for job in self._jobs:
+            job.weight_format |= _lib.PCK_WEIGHTS_SETTLED
         self.prior: list[GemvLaunch] = []
         self._prior = None
         self.set_prior(prior)
@@ -179,7 +186,12 @@ class TcLaunch:
     ``height=tc_height(n)``): Y_i (B, m_i) = X_i (B, n_i) W_i^T. Reusable launch after launch
     (e.g. captured in a CUDA graph); outputs in ``ys``, check results in ``results``."""
 
-    def __init__(self, items: Sequence[tuple[torch.Tensor, torch.Tensor, GpuBlockedChecker | None]]) -> None:
+    def __init__(self, items: Sequence[tuple[torch.Tensor, torch.Tensor, GpuBlockedChecker | None]],
+                 ys: Sequence[torch.Tensor] | None = None,
+                 passed: Sequence[torch.Tensor | None] | None = None) -> None:  # fmt: skip
+        """``ys`` / ``passed`` may give preallocated outputs (e.g. views into the packed
+        buffer of a row-sharded exchange): y (B, m) float32 and the verdict bits as a
+        contiguous bool tensor of B * checks * num_blocks elements."""
         if not 1 <= len(items) <= 8:
             raise ValueError(f"a tensor-core launch holds 1 to 8 GEMVs, got {len(items)}")
         self.device = items[0][0].device
@@ -196,7 +208,10 @@ class TcLaunch:
                 raise RuntimeError("W and X must be bfloat16, X (B, n) with one B for the launch")
             if not (W.is_contiguous() and X.is_contiguous()) or X.size(1) != W.size(1):
                 raise RuntimeError("expected contiguous W (m, n) and X (B, n)")
-            y = torch.empty((batch, W.size(0)), dtype=torch.float32, device=self.device)
+            shape = (batch, W.size(0))
+            y = ys[g] if ys is not None else torch.empty(shape, dtype=torch.float32, device=self.device)
+            if tuple(y.shape) != shape or y.dtype != torch.float32 or not y.is_contiguous():
+                raise RuntimeError(f"y must be a contiguous float32 tensor of shape {shape}")
             self.ys.append(y)
             job = self._jobs[g]
             job.W, job.X, job.Y = W.data_ptr(), X.data_ptr(), y.data_ptr()
@@ -208,7 +223,10 @@ class TcLaunch:
                 continue
             pcx, ps = ch.scratch(batch)
             shape = (batch, ch.checks, ch.num_blocks)
-            out = (torch.empty(shape, dtype=torch.bool, device=self.device),
+            p = passed[g] if passed is not None else None
+            if p is not None and (p.numel() != math.prod(shape) or p.dtype != torch.bool or not p.is_contiguous()):
+                raise RuntimeError("passed must be a contiguous bool tensor of the check's size")
+            out = (p.view(shape) if p is not None else torch.empty(shape, dtype=torch.bool, device=self.device),
                    torch.empty(shape, dtype=torch.float64, device=self.device),
                    torch.empty(shape, dtype=torch.float64, device=self.device))  # fmt: skip
             d = self._descs[g]
@@ -225,3 +243,14 @@ class TcLaunch:
         with on_device(self.device):
             rc = self.lib.pck_gemv_tc(self._jobs, self.count, stream_handle(self.device))
         _lib.check(rc, "tensor-core gemv kernel")
+
+    @property
+    def algorithmic_bytes(self) -> int:
+        """Bytes the launch must move at least: W, X and Y and, for checked items, the bank
+        (c, a, r) and the verdict outputs (passed, rho, tau)."""
+        total = 0
+        for (W, X, ch), y, res in zip(self.items, self.ys, self.results, strict=True):
+            total += W.numel() * W.element_size() + X.numel() * 2 + y.numel() * 4
+            if ch is not None:
+                total += ch.c.numel() * 4 + ch.a.numel() * 2 + ch.r.numel() + res.passed.numel() * (1 + 8 + 8)
+        return total

@@ -94,9 +94,13 @@ class PackedOutputs:
             raise RuntimeError("a section of an Exchange is gathered by the Exchange")
         dist.all_gather_into_tensor(self.gathered, self.local, group=group)
 
-    def assemble(self, j: int) -> torch.Tensor:
-        """Projection j's full output, (m,) or (batch, m), from the gathered buffer."""
-        return torch.cat([self._chunk(self._ranks[r], j, r) for r in range(self.world)], dim=-1)
+    def assemble(self, j: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Projection j's full output, (m,) or (batch, m), from the gathered buffer (one
+        concatenation kernel; into ``out`` when given, e.g. a fixed buffer of a captured step)."""
+        chunks = [self._chunk(self._ranks[r], j, r) for r in range(self.world)]
+        if out is None:
+            return torch.cat(chunks, dim=-1)
+        return torch.cat(chunks, dim=-1, out=out)
 
 
 class Exchange:

@@ -27,6 +27,7 @@ import atexit
 import json
 import os
 import time
+from collections import deque
 from pathlib import Path
 from typing import Any
 
@@ -35,77 +36,86 @@ import torch
 from pck.member import check_members
 
 
-class CheckStats:
-    """Running totals as device tensors; written from pinned host copies, an interval late."""
+class SamplingTally:
+    """Per-process totals of the sampling check, kept on the device and reported without
+    ever stalling the decode loop.
 
-    FIELDS = ("rows", "rejected", "injected", "caught", "false_alarms")
+    Each step files every row into one of four bins, ``2 * injected + rejected`` (honest and
+    accepted, false alarm, missed injection, caught injection), added in place to a device
+    histogram, and folds the step's largest top-p excess into a running maximum. Every
+    ``every`` steps both are copied into a pinned host buffer behind an event; the queue of
+    such copies is drained (oldest first) whenever their events have completed, so a line is
+    written once its copy has arrived and none is dropped. `close` waits for what is still in
+    flight and adds a line with the current totals. The JSON-lines schema (rows, rejected,
+    injected, caught, false_alarms, steps, max_excess, seconds, pid, rank) is the reference
+    plugin's log format."""
 
     def __init__(self, path: Path, every: int) -> None:
-        self.path, self.every = path, every
-        self.steps = 0
-        self.written = 0
-        self.totals: torch.Tensor | None = None
-        self.max_excess: torch.Tensor | None = None
-        self.pending: tuple[torch.Tensor, Any, int, float] | None = None
-        self.start = time.time()
+        self.path = path
+        self.every = max(1, every)
+        self.step = 0
+        self.last_reported = 0
+        self.bins: torch.Tensor | None = None  # int64 (4,)
+        self.peak: torch.Tensor | None = None  # float64 (1,)
+        self.inflight: deque[tuple[torch.Tensor, torch.cuda.Event | None, int, float]] = deque()
+        self.t0 = time.monotonic()
         self.rank = os.environ.get("RANK", os.environ.get("LOCAL_RANK"))
 
     def add(self, ok: torch.Tensor, injected: torch.Tensor, excess: torch.Tensor) -> None:
-        rejected = ~ok
-        counts = torch.stack([torch.ones_like(ok).sum(), rejected.sum(), injected.sum(),
-                              (rejected & injected).sum(), (rejected & ~injected).sum()])  # fmt: skip
-        step_excess = excess.max()
-        if self.totals is None:
-            self.totals, self.max_excess = counts, step_excess
+        if self.bins is None:
+            self.bins = torch.zeros(4, dtype=torch.int64, device=ok.device)
+            self.peak = torch.full((1,), -1.0, dtype=torch.float64, device=ok.device)
+        code = injected.to(torch.int64) * 2 + (~ok).to(torch.int64)
+        self.bins.index_add_(0, code, torch.ones_like(code))
+        torch.maximum(self.peak, excess.max().reshape(1), out=self.peak)
+        self.step += 1
+        if self.step % self.every == 0:
+            self._enqueue()
+        self._drain(block=False)
+
+    def _enqueue(self) -> None:
+        merged = torch.cat((self.bins.double(), self.peak))
+        if merged.is_cuda:
+            host = torch.empty(5, dtype=torch.float64, pin_memory=True)
+            host.copy_(merged, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record()
         else:
-            self.totals = self.totals + counts
-            self.max_excess = torch.maximum(self.max_excess, step_excess)
-        self.steps += 1
-        if self.steps % self.every == 0:
-            self._write_ready(wait=False)
-            self.pending = self._snapshot()
+            host, done = merged.clone(), None
+        self.inflight.append((host, done, self.step, time.monotonic() - self.t0))
 
-    def _snapshot(self) -> tuple[torch.Tensor, Any, int, float]:
-        vals = torch.cat([self.totals.to(torch.float64), self.max_excess.reshape(1).double()])
-        if not vals.is_cuda:
-            return vals.clone(), None, self.steps, time.time()
-        host = torch.empty(vals.shape, dtype=vals.dtype, pin_memory=True)
-        host.copy_(vals, non_blocking=True)
-        event = torch.cuda.Event()
-        event.record()
-        return host, event, self.steps, time.time()
+    def _drain(self, block: bool) -> None:
+        while self.inflight:
+            host, done, step, elapsed = self.inflight[0]
+            if done is not None and not done.query():
+                if not block:
+                    return
+                done.synchronize()
+            self.inflight.popleft()
+            honest_ok, false_alarm, missed, caught = (int(v) for v in host[:4].tolist())
+            line = {"rows": honest_ok + false_alarm + missed + caught, "rejected": false_alarm + caught,
+                    "injected": missed + caught, "caught": caught, "false_alarms": false_alarm,
+                    "steps": step, "max_excess": float(host[4]), "seconds": round(elapsed, 1),
+                    "pid": os.getpid(), "rank": self.rank}  # fmt: skip
+            with self.path.open("a") as log:
+                log.write(json.dumps(line) + "\n")
+            self.last_reported = step
 
-    def _write_ready(self, wait: bool) -> None:
-        if self.pending is None:
-            return
-        host, event, steps, now = self.pending
-        if event is not None and not event.query():
-            if not wait:
-                return  # still in flight: the next snapshot replaces it
-            event.synchronize()
-        values = host.tolist()
-        row: dict[str, Any] = dict(zip(self.FIELDS, (int(v) for v in values[:-1]), strict=True))
-        row |= {"steps": steps, "max_excess": values[-1], "seconds": round(now - self.start, 1),
-                "pid": os.getpid(), "rank": self.rank}  # fmt: skip
-        with self.path.open("a") as f:
-            f.write(json.dumps(row) + "\n")
-        self.pending, self.written = None, steps
-
-    def flush(self) -> None:
-        """Write the pending copy, then the current totals (synchronizes; for the end)."""
-        self._write_ready(wait=True)
-        if self.totals is not None and self.written != self.steps:
-            self.pending = self._snapshot()
-            self._write_ready(wait=True)
+    def close(self) -> None:
+        """Write every queued copy and then the current totals (synchronizes; for exit)."""
+        self._drain(block=True)
+        if self.bins is not None and self.last_reported != self.step:
+            self._enqueue()
+            self._drain(block=True)
 
 
 def install(sampler_cls: Any, states_cls: Any, log: Path, every: int = 16, tol: float = 1e-4,
-            fault_rate: float = 0.0) -> CheckStats:  # fmt: skip
+            fault_rate: float = 0.0) -> SamplingTally:  # fmt: skip
     """Wrap ``states_cls.apply_top_k_top_p`` and ``sampler_cls.sample`` (vLLM's V2 sampler
     classes, or stand-ins with the same methods and attributes in tests)."""
     original_mask = states_cls.apply_top_k_top_p
     original_sample = sampler_cls.sample
-    stats = CheckStats(log, every)
+    stats = SamplingTally(log, every)
 
     def keep_unmasked(self: Any, logits: torch.Tensor, expanded_idx_mapping: torch.Tensor, idx_mapping_np: Any):
         host_k = self.top_k.np[idx_mapping_np]
@@ -154,7 +164,7 @@ def install(sampler_cls: Any, states_cls: Any, log: Path, every: int = 16, tol: 
 
     states_cls.apply_top_k_top_p = keep_unmasked
     sampler_cls.sample = checked
-    atexit.register(stats.flush)
+    atexit.register(stats.close)
     return stats
 
 

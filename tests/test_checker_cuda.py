@@ -286,3 +286,51 @@ def test_an_overflowing_threshold_fails_closed() -> None:
     res = checker.check(xt, torch.full((m,), 1e30, device="cuda"))
     assert not torch.isfinite(res.tau).any()
     assert not res.passed.any()
+
+
+@pytest.mark.parametrize("settled", [False, True])
+def test_bank_built_just_before_a_checked_launch(settled: bool) -> None:
+    """pck_bank_build directly followed, on the same stream and with no synchronization, by a
+    checked launch that reads the new bank: the launch waits for the bank kernel before it
+    reads c and a (the bank CTAs never prefetch), so the verdicts equal those of the same
+    launch run after a synchronize. Settled weights (PCK_WEIGHTS_SETTLED) change nothing
+    here: only W, written long before, is read early."""
+    import ctypes
+
+    from pck.cuda import _lib
+    from pck.cuda._ext import extension, stream_handle
+    from pck.fp import sum_up_factor
+
+    W, x, Wt, xt = problem(1024, 4096, seed=5)
+    ch = make(Wt, block=128, checks=2, seed=9, height=tree_height(4096, THREADS, 8))
+    lib = _lib.library()
+    ext = extension()
+    stream = stream_handle(Wt.device)
+
+    def launch(c, a):
+        y = torch.empty(1024, dtype=torch.float32, device="cuda")
+        desc = _lib.CheckDesc()
+        _, _, r, pcx, ps, ctr, coef, geps, floor = ch.check_args(xt)
+        out = ext.describe(c, a, r, xt, y, pcx, ps, ctr, coef, geps, floor, Wt.device, desc)
+        job = (_lib.GemvJob * 1)()
+        job[0].W, job[0].X, job[0].Y = Wt.data_ptr(), xt.data_ptr(), y.data_ptr()
+        job[0].m, job[0].n, job[0].batch, job[0].threads = 1024, 4096, 1, THREADS
+        job[0].weight_format = _lib.PCK_WEIGHTS_BF16 | (_lib.PCK_WEIGHTS_SETTLED if settled else 0)
+        job[0].check = ctypes.pointer(desc)
+        _lib.check(lib.pck_gemv_checked(job, 1, stream))
+        return y, out
+
+    torch.cuda.synchronize()
+    for trial in range(3):
+        c = torch.full_like(ch.c, float("nan"))  # a stale bank would fail every block
+        a = torch.full_like(ch.a, float("nan"))
+        torch.cuda.synchronize()
+        _lib.check(lib.pck_bank_build(Wt.data_ptr(), ch.r.data_ptr(), c.data_ptr(), a.data_ptr(), 1024, 4096,
+                                      128, 2, float(sum_up_factor(128)), stream))  # fmt: skip
+        y, (passed, rho, tau) = launch(c, a)
+        torch.cuda.synchronize()
+        assert bool(passed.all()), f"trial {trial}: a block failed against a bank built just before"
+        y0, (passed0, rho0, tau0) = launch(ch.c, ch.a)
+        torch.cuda.synchronize()
+        assert torch.equal(y, y0) and torch.equal(passed, passed0)
+        assert torch.equal(rho, rho0) and torch.equal(tau, tau0)

@@ -46,7 +46,7 @@ def test_library_exports_every_declared_symbol(lib) -> None:
 
 
 def test_abi_version(lib) -> None:
-    assert lib.pck_abi_version() == 3
+    assert lib.pck_abi_version() == 4
 
 
 def _err(lib) -> str:

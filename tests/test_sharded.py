@@ -82,6 +82,13 @@ def _rank_main(rank: int, world: int, port: int, batch: int, out: dict) -> None:
         for j, m in enumerate(ms):
             assert torch.equal(yv.assemble(j), torch.arange(m, dtype=torch.float32).expand(batch, -1).squeeze(0))
             assert torch.equal(vv.assemble(j), (torch.arange(m // block) % 3 == 0).expand(2, -1))
+            # into fixed buffers (the LM head's captured step)
+            fixed = torch.full((batch, m) if batch > 1 else (m,), -1.0)
+            yv.assemble(j, out=fixed)
+            assert torch.equal(fixed, torch.arange(m, dtype=torch.float32).expand(batch, -1).squeeze(0))
+            bits = torch.zeros((2, m // block), dtype=torch.bool)
+            vv.assemble(j, out=bits)
+            assert torch.equal(bits, (torch.arange(m // block) % 3 == 0).expand(2, -1))
         out[rank] = True
     finally:
         dist.destroy_process_group()

@@ -5,6 +5,7 @@ false alarm on legitimately sampled tokens and catches every injected non-member
 from __future__ import annotations
 
 import json
+import os
 from pathlib import Path
 
 import numpy as np
@@ -96,8 +97,32 @@ def test_stand_in_sampler_no_false_alarm_and_faults_caught(tmp_path: Path) -> No
     for step in range(24):
         logits = torch.randn(rows, vocab, device="cuda") * 3.0
         sampler.sample(logits, idx, np.arange(rows), None, None, None)
-    stats.flush()
+    stats.close()
     last = json.loads(log.read_text().strip().splitlines()[-1])
     assert last["steps"] == 24 and last["rows"] == 24 * rows
     assert last["false_alarms"] == 0
     assert last["injected"] > 0 and last["caught"] == last["injected"]
+
+
+def test_tally_lines_on_the_host(tmp_path: Path) -> None:
+    """The tally's bins and log lines, driven with host tensors (no GPU): every interval
+    writes one line of running totals, and close() adds the unreported tail."""
+    from pck.vllm_plugin import SamplingTally
+
+    log = tmp_path / "tally.jsonl"
+    tally = SamplingTally(log, every=2)
+    steps = [
+        (torch.tensor([True, False, True, False]), torch.tensor([False, False, True, True]), torch.tensor([-1.0, 0.2])),
+        (torch.tensor([True, True, True, True]), torch.tensor([False, False, False, False]), torch.tensor([0.5, -1.0])),
+        (torch.tensor([False, True, True, True]), torch.tensor([True, False, False, False]), torch.tensor([0.1])),
+    ]  # fmt: skip
+    for ok, injected, excess in steps:
+        tally.add(ok, injected, excess.double())
+    tally.close()
+    lines = [json.loads(x) for x in log.read_text().splitlines()]
+    assert [ln["steps"] for ln in lines] == [2, 3]
+    first, last = lines
+    assert (first["rows"], first["rejected"], first["injected"], first["caught"], first["false_alarms"]) == (8, 2, 2, 1, 1)
+    assert (last["rows"], last["rejected"], last["injected"], last["caught"], last["false_alarms"]) == (12, 3, 3, 2, 1)
+    assert first["max_excess"] == 0.5 and last["max_excess"] == 0.5
+    assert all(ln["pid"] == os.getpid() for ln in lines)

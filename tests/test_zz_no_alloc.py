@@ -141,3 +141,26 @@ def test_rejects_checks_beyond_the_static_limit() -> None:
     rc = lib.library().pck_gemv_checked_static(job, 1, None)
     assert rc == 1
     assert "static limit" in lib.library().pck_last_error().decode()
+
+
+def test_rejects_jobs_that_fit_alone_but_not_together() -> None:
+    """Two checks of 2.125 MiB of scratch each fit the array alone but not together: the call
+    is refused with the summed size, before any device work (so no GPU is needed)."""
+    lib = _lib()
+    count = 2
+    descs = (lib.CheckDesc * count)()
+    jobs = (lib.GemvJob * count)()
+    for g in range(count):
+        d = descs[g]
+        d.c = d.a = d.r = d.x = d.y = d.passed = d.rho = d.tau = 16 * (g + 1)
+        d.n, d.block, d.num_blocks, d.checks, d.segments, d.batch = 4096, 128, 256, 16, 64, 1
+        d.coef = d.geps = d.tau_floor = 1.0
+        jobs[g].W = jobs[g].X = jobs[g].Y = 16 * (g + 1)
+        jobs[g].m, jobs[g].n, jobs[g].batch, jobs[g].threads = 256 * 128, 4096, 1, 256
+        jobs[g].check = ctypes.pointer(d)
+    one = 8 * 16 * 256 * 64 + 8 * 256 * 64  # c . x partials, then a . |x| partials
+    assert one <= lib.STATIC_SCRATCH_BYTES < count * one
+    rc = lib.library().pck_gemv_checked_static(jobs, count, None)
+    assert rc == 1  # PCK_ERR_ARGUMENT
+    msg = lib.library().pck_last_error().decode()
+    assert f"need {count * one} bytes" in msg and "static limit" in msg
