@@ -48,6 +48,7 @@ VERDICTS = {
 SCOPE = {"carried": "4 stream_kernel launches, each deciding the previous launch's checks",
          "launch": "4 stream_kernel launches + 1 verdict_kernel launch"}  # fmt: skip
 L2_BYTES = 126 * 2**20
+LLAMA3_GROUP_NAMES = [["q", "k", "v"], ["o"], ["gate", "up"], ["down"]]
 
 
 def measured_peaks() -> dict:
@@ -135,8 +136,10 @@ def outlier_x(n: int, batch: int, gen: torch.Generator) -> torch.Tensor:
     return x.bfloat16()
 
 
-def build_layer(args, rank: int, world: int, device: torch.device):
-    """Sharded weights, inputs, checkers and the launch objects of one decode layer."""
+def build_layer(args, rank: int, world: int, device: torch.device, keep_full: bool = False):
+    """Sharded weights, inputs, checkers and the launch objects of one decode layer. With
+    ``keep_full``, also the unsharded weights of every projection (for the check that the
+    gathered outputs equal the single-GPU ones)."""
     from pck.cuda import GpuBlockedChecker
     from pck.cuda.plan import LLAMA3_8B_GROUPS, GemvLaunch, VerdictLaunch
     from pck.cuda.sharded import Exchange, shard_rows
@@ -150,7 +153,7 @@ def build_layer(args, rank: int, world: int, device: torch.device):
     ex_plain = Exchange([(ms, args.block, args.batch, torch.float32)], world, rank, device)
     ys, vs = ex.parts
     gen = torch.Generator().manual_seed(0)
-    groups, plain, xs, j = [], [], [], 0
+    groups, plain, xs, full, j = [], [], [], [], 0
     for group in LLAMA3_8B_GROUPS:
         n = group[0][2]
         x = outlier_x(n, args.batch, gen).to(device)
@@ -160,13 +163,17 @@ def build_layer(args, rank: int, world: int, device: torch.device):
         for _name, m, nn in group:
             shard = shard_rows(m, args.block, world, rank)
             dgen = torch.Generator(device=device).manual_seed(1000 + j)
-            W = (torch.randn(m, nn, generator=dgen, device=device) * 0.02).bfloat16()
-            W = W[shard.row0 : shard.row1].contiguous()
+            W_all = (torch.randn(m, nn, generator=dgen, device=device) * 0.02).bfloat16()
+            W = W_all[shard.row0 : shard.row1].contiguous()
             vec = 8
             if args.weights == "e4m3":  # config 3: per-row E4M3 quantisation, checked against Q
                 from pck.cuda import quantize_fp8
 
                 W, vec = quantize_fp8(W)[0], 16
+                if keep_full:
+                    W_all = quantize_fp8(W_all)[0]
+            full.append(W_all if keep_full else None)
+            del W_all
             checker = GpuBlockedChecker(W.to(torch.bfloat16), args.block, tree_height(nn, args.threads, vec),
                                         checks=args.checks, generator=torch.Generator().manual_seed(2000 + j))  # fmt: skip
             items.append((W, x, checker))
@@ -179,7 +186,7 @@ def build_layer(args, rank: int, world: int, device: torch.device):
         plain.append(GemvLaunch(items_plain, args.threads, ys=y_plain))
     verdict = VerdictLaunch(groups)
     torch.cuda.synchronize()
-    return groups, verdict, plain, xs, ex, ex_plain
+    return groups, verdict, plain, xs, ex, ex_plain, full
 
 
 # Consecutive layer steps captured in one CUDA graph at most: a decode graph holds every
@@ -238,32 +245,34 @@ def timed(graph: tuple[torch.cuda.CUDAGraph, int], steps: int, warmup: int, worl
     return ms / 1e3 / steps
 
 
-def e2e_step_time(groups, xs, ex, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
-    """The public launch API with host buffers: every step copies the layer's activations
-    from pinned host memory, launches, gathers and copies outputs and verdicts back."""
+def e2e_step_time(launches, xs, ex, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
+    """The public API with host buffers (`pck.cuda.plan.CapturedStep`): every step copies the
+    layer's activations from pinned host memory, runs the layer's launches (and the gather),
+    and copies every output and verdict bit back to pinned host memory; one graph launch per
+    step. Device time per step, max over ranks."""
+    from pck.cuda.plan import CapturedStep
+
     hx = [x.cpu().pin_memory() for x in xs]
     hout = torch.empty(ex.gathered.shape, dtype=ex.gathered.dtype, pin_memory=True)
 
-    def step() -> None:
-        for x, h in zip(xs, hx, strict=True):
-            x.copy_(h, non_blocking=True)
-        for g in groups:
+    def body() -> None:
+        for g in launches:
             g.launch()
         if world > 1:
             ex.gather()
-        else:
-            ex.gathered.copy_(ex.local)
-        hout.copy_(ex.gathered, non_blocking=True)
 
+    result = ex.gathered if world > 1 else ex.local
+    hres = hout if world > 1 else torch.empty(ex.local.shape, dtype=ex.local.dtype, pin_memory=True)
+    step = CapturedStep(body, list(zip(hx, xs, strict=True)), [(result, hres)])
     for _ in range(warmup):
-        step()
+        step.run()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(steps):
-        step()
+        step.run()
     end.record()
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
@@ -271,9 +280,187 @@ def e2e_step_time(groups, xs, ex, steps: int, warmup: int, world: int) -> tuple[
         t = torch.tensor([ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    h2d = sum(h.numel() * h.element_size() for h in hx)
-    d2h = hout.numel() * hout.element_size()
+    h2d, d2h = step.h2d_bytes, step.d2h_bytes
+    del step
     return ms / 1e3 / steps, h2d, d2h
+
+
+def launch_times(fns, steps: int, world: int) -> list[float]:
+    """Device time of each launch of a step, in ms: the step issued eagerly ``steps`` times
+    with a CUDA event between consecutive launches (on the launching stream), averaged. The
+    events keep each launch from overlapping its neighbour, so the sum is a little above the
+    graph's time per step."""
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(len(fns) + 1)]
+    totals = [0.0] * len(fns)
+    for _ in range(3):
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    for _ in range(steps):
+        events[0].record()
+        for i, f in enumerate(fns):
+            f()
+            events[i + 1].record()
+        torch.cuda.synchronize()
+        for i in range(len(fns)):
+            totals[i] += events[i].elapsed_time(events[i + 1])
+    out = [t / steps for t in totals]
+    if world > 1:
+        t = torch.tensor(out, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        out = t.tolist()
+    return [round(v, 5) for v in out]
+
+
+def all_ranks(flag: bool, world: int) -> bool:
+    """True iff ``flag`` holds on every rank."""
+    if world == 1:
+        return flag
+    t = torch.tensor([1 if flag else 0], device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def gathered_layer_matches(groups, xs, ex, full, world: int, rank: int) -> bool | None:
+    """Multi-GPU correctness of the timed path, after a step has run: every rank's copy of
+    the gathered verdict bits passes every block, and on rank 0 every projection's gathered
+    output equals, bit for bit, the output of the unsharded matrix (the single-GPU result).
+    The same answer on every rank. None at one GPU."""
+    from pck.cuda import gemv_coalesced, gemv_fp8
+
+    if world == 1:
+        return None
+    ys, vs = ex.parts
+    ok = all(bool(vs.assemble(j).all()) for j in range(len(vs.ms)))
+    if rank == 0:
+        j = 0
+        for g, x in zip(groups, xs, strict=True):
+            for _ in g.items:
+                W = full[j]
+                y = gemv_fp8(W, x) if W.dtype == torch.float8_e4m3fn else gemv_coalesced(W, x)
+                ok = ok and torch.equal(ys.assemble(j).view(torch.int32), y.view(torch.int32))
+                j += 1
+    return all_ranks(ok, world)
+
+
+LM_VOCAB, LM_N, LM_BATCH = 128256, 4096, 64
+
+
+def lm_head_reading(rank: int, world: int, device, steps: int, warmup: int) -> dict:
+    """Config 5: the Llama-3 LM head W (128256, 4096) bfloat16 at decode batch 64, row-sharded
+    by whole 128-row blocks over the ranks, each rank's slice checked in the same call as its
+    tensor-core GEMV; one all-gather of logits and verdict bits; top-k 50 / top-p 0.9 sampling
+    at temperature 1 (untrusted torch) with 1% of the tokens replaced by the row's lowest
+    logit; the fused membership check of every token. Activations are scaled so that the
+    logits are ~N(0, 3^2). Device times of CUDA graphs, max over ranks."""
+    from pck.cuda import gemv_tc
+    from pck.cuda.lm_head import CheckedLMHead, TopKTopPSampler, membership
+    from pck.cuda.sharded import shard_rows
+
+    sh = shard_rows(LM_VOCAB, 128, world, rank)
+    gen = torch.Generator(device=device).manual_seed(5000)
+    W_all = (torch.randn(LM_VOCAB, LM_N, generator=gen, device=device) * 0.02).bfloat16()
+    X = (torch.randn(LM_BATCH, LM_N, generator=gen, device=device) * (3.0 / (0.02 * LM_N**0.5))).bfloat16()
+    W = W_all[sh.row0 : sh.row1].contiguous()
+    if not (world > 1 and rank == 0):
+        del W_all
+        W_all = None
+    head = CheckedLMHead(W, X, LM_VOCAB, world=world, rank=rank, generator=torch.Generator().manual_seed(5001))
+    torch.manual_seed(5002)  # the sampler's draws: the same on every rank
+    sampler = TopKTopPSampler(LM_BATCH, LM_VOCAB, k=50, p=0.9, temperature=1.0, device=device, fault_rate=0.01)
+    counts = torch.zeros(4, dtype=torch.int64, device=device)  # steps all passed, planted, caught, false alarms
+
+    def sample_and_check() -> None:
+        sampler(head.logits)
+        ok = membership(head.logits, sampler)["ok"]
+        inj = sampler.injected
+        counts.add_(torch.stack([head.passed.all().to(torch.int64), inj.sum(), (inj & ~ok).sum(), (~inj & ~ok).sum()]))
+
+    def full_step() -> None:
+        head.forward()
+        sample_and_check()
+
+    per = graph_steps(steps)
+    g_gemv = cuda_graph(head.gemv.launch, per)
+    g_forward = cuda_graph(head.forward, per)
+    sampler(head.logits)
+    g_member = cuda_graph(lambda: membership(head.logits, sampler), per)
+    g_full = cuda_graph(full_step, per)
+    counts.zero_()
+    torch.cuda.synchronize()
+    t_gemv = timed(g_gemv, steps, warmup, world)
+    t_forward = timed(g_forward, steps, warmup, world)
+    t_member = timed(g_member, steps, warmup, world)
+    counts.zero_()
+    t_full = timed(g_full, steps, warmup, world)
+    torch.cuda.synchronize()
+    replays = (-(-warmup // per) + steps // per) * per  # steps the counters saw
+    passed_steps, planted, caught, false_alarms = (int(v) for v in counts.tolist())
+    matches = None
+    if world > 1:  # rank 0: the gathered logits against the unsharded GEMV, bit for bit
+        ok = True
+        if rank == 0:
+            ok = torch.equal(gemv_tc(W_all, X).view(torch.int32), head.logits.view(torch.int32))
+        matches = all_ranks(ok, world)
+    local_bytes = head.gemv_bytes
+    total = torch.tensor([float(local_bytes)], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(total)
+    gemv_gbs = float(total.item()) / t_gemv / 1e9
+    peak = float(measured_peaks()["hbm_gbs"])
+    del g_gemv, g_forward, g_member, g_full
+    return {
+        "workload": "Llama-3 LM head 128256x4096 bf16, batch 64, row-sharded checked tcgen05 GEMV + all-gather "
+                    "+ top-k 50 / top-p 0.9 sampling + fused membership check (1% planted non-members)",
+        "parallelism": f"row-shard x{world}" if world > 1 else "single",
+        "ms_per_step": round(t_full * 1e3, 4), "tokens_per_s": round(LM_BATCH / t_full),
+        "gemv_ms": round(t_gemv * 1e3, 4), "gemv_and_gather_ms": round(t_forward * 1e3, 4),
+        "gather_ms": round((t_forward - t_gemv) * 1e3, 4) if world > 1 else 0.0,
+        "membership_ms": round(t_member * 1e3, 4),
+        "gemv_GB_per_s": round(gemv_gbs, 1),
+        "roofline": {"bound": "hbm", "achieved": round(gemv_gbs / world, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gemv_gbs / world / peak, 4),
+                     "scope": "per GPU: the checked GEMV launch (W slice, X, logits, bank, verdicts)"},
+        "all_blocks_passed": passed_steps == replays, "planted": planted, "caught": caught,
+        "false_alarms": false_alarms, "sampled_tokens_checked": replays * LM_BATCH,
+        "gathered_logits_equal_single_gpu": matches,
+    }  # fmt: skip
+
+
+def e4m3_reading(args, device, steps: int, warmup: int) -> dict:
+    """Config 3 at batch 1 on one GPU: the same decode layer with per-row E4M3 weights,
+    checked against Q with the fused checker, verdicts carried by the next launch."""
+    import copy
+
+    a = copy.copy(args)
+    a.weights, a.batch = "e4m3", 1
+    groups, _verdict, plain, _xs, ex, _ex_plain, _ = build_layer(a, 0, 1, device)
+    for i, g in enumerate(groups):
+        g.set_prior([groups[i - 1]])
+    per = graph_steps(steps)
+    g_checked = cuda_graph(lambda: [g.launch() for g in groups], per)
+    g_plain = cuda_graph(lambda: [g.launch() for g in plain], per)
+    g_checked[0].replay()
+    torch.cuda.synchronize()
+    passed = bool(ex.parts[1].local.all())
+    t_checked = timed(g_checked, steps, warmup, 1)
+    t_plain = timed(g_plain, steps, warmup, 1)
+    per_launch = launch_times([g.launch for g in groups], max(10, steps), 1)
+    step_bytes = sum(g.algorithmic_bytes for g in groups)
+    value = step_bytes / t_checked / 1e9
+    peak = float(measured_peaks()["hbm_gbs"])
+    del g_checked, g_plain
+    return {
+        "workload": "llama3-8b decode layer, E4M3 weights (per-row absmax scales) x bf16 activations, batch 1, "
+                    "fused blocked check against Q",
+        "value": round(value, 2), "unit": UNIT, "ms_per_step": round(t_checked * 1e3, 5),
+        "unchecked_ms_per_step": round(t_plain * 1e3, 5),
+        "checker_overhead_pct": round((t_checked / t_plain - 1) * 100, 2),
+        "launch_ms": per_launch, "all_blocks_passed": passed,
+        "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(value / peak, 4), "traffic": profile_traffic("e4m3"),
+                     "scope": "one step = 4 stream_kernel launches (E4M3), each deciding the previous launch's checks"},
+    }  # fmt: skip
 
 
 def batch128_reading(args, groups, device, steps: int, warmup: int) -> dict:
@@ -404,6 +591,8 @@ def main() -> None:
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-batch128", action="store_true", help="skip the batch-128 tensor-core reading")
+    parser.add_argument("--no-e4m3", action="store_true", help="skip the E4M3 (config 3, batch 1) reading")
+    parser.add_argument("--no-lm-head", action="store_true", help="skip the LM-head (config 5) reading")
     parser.add_argument("--verdicts", choices=sorted(VERDICTS), default="carried",
                         help="carried: each launch decides the previous launch's checks; launch: a verdict launch per step")
     args = parser.parse_args()
@@ -424,7 +613,7 @@ def main() -> None:
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)  # fmt: skip
 
-    groups, verdict, plain, xs, ex, ex_plain = build_layer(args, rank, world, device)
+    groups, verdict, plain, xs, ex, ex_plain, full = build_layer(args, rank, world, device, keep_full=world > 1)
     vs = ex.parts[1]
     step_bytes_local = sum(g.algorithmic_bytes for g in groups)
 
@@ -456,10 +645,13 @@ def main() -> None:
 
     graph_checked = cuda_graph(checked_step, per_graph)
     graph_plain = cuda_graph(plain_step, per_graph)
-    # correctness of the timed path: every block of the honest layer passes
+    # correctness of the timed path: every block of the honest layer passes on every rank,
+    # and (N > 1) the gathered outputs equal the unsharded ones bit for bit
     graph_checked[0].replay()
     torch.cuda.synchronize()
-    all_passed = bool(vs.local.all()) if world == 1 else None
+    all_passed = all_ranks(bool(vs.local.all()), world)
+    gathered_ok = gathered_layer_matches(groups, xs, ex, full, world, rank)
+    del full
 
     gpu_index = local
     visible = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -473,10 +665,16 @@ def main() -> None:
         t_plain = timed(graph_plain, args.steps, args.warmup, world)
         t_other = timed(graph_other, args.steps, args.warmup, world) if graph_other is not None else None
     clock = clocks.summary()
-    batch128 = None
+    side_steps = max(20, args.steps // 10)
+    per_launch = launch_times([g.launch for g in launches] + ([ex.gather] if world > 1 else []), side_steps, world)
+    batch128 = e4m3 = lm_head = None
     if world == 1 and args.weights == "bf16" and args.batch == 1 and not args.no_batch128:
-        batch128 = batch128_reading(args, groups, device, max(20, args.steps // 10), args.warmup)
-    t_e2e, h2d, d2h = e2e_step_time(launches, xs, ex, max(20, args.steps // 10), args.warmup, world)
+        batch128 = batch128_reading(args, groups, device, side_steps, args.warmup)
+    if world == 1 and args.weights == "bf16" and args.batch == 1 and not args.no_e4m3:
+        e4m3 = e4m3_reading(args, device, side_steps, args.warmup)
+    if not args.no_lm_head:
+        lm_head = lm_head_reading(rank, world, device, side_steps, args.warmup)
+    t_e2e, h2d, d2h = e2e_step_time(launches, xs, ex, side_steps, args.warmup, world)
 
     total_bytes = torch.tensor([float(step_bytes_local)], device=device)
     if world > 1:
@@ -517,6 +715,13 @@ def main() -> None:
             "unchecked_ms_per_step": round(t_plain * 1e3, 5),
             "verdict_launch_ms_per_step": round(t_other * 1e3, 5) if t_other is not None else None,
             "all_blocks_passed": all_passed,
+            "gathered_outputs_equal_single_gpu": gathered_ok,
+            "launch_ms": {"launches": [f"stream_kernel:{'+'.join(grp)}" for grp in LLAMA3_GROUP_NAMES]
+                                      + (["nccl all_gather"] if world > 1 else []) + ([] if args.verdicts == "carried"
+                                                                                     else ["verdict_kernel"]),
+                          "ms": per_launch,
+                          "how": "eager, a CUDA event between consecutive launches, mean over "
+                                 f"{side_steps} steps, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(value / world / peak, 4),
                          "traffic": traffic,
@@ -529,6 +734,8 @@ def main() -> None:
             "clocks": clock,
             "cpu_baseline": cpu,
             "batch128": batch128,
+            "e4m3": e4m3,
+            "lm_head": lm_head,
         }  # fmt: skip
         print(json.dumps(line), flush=True)
     del graph_checked, graph_plain, graph_other

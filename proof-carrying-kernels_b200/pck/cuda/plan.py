@@ -254,3 +254,51 @@ class TcLaunch:
             if ch is not None:
                 total += ch.c.numel() * 4 + ch.a.numel() * 2 + ch.r.numel() + res.passed.numel() * (1 + 8 + 8)
         return total
+
+
+class CapturedStep:
+    """One decode step replayed from a CUDA graph, host buffers included: the copies of the
+    step's inputs from pinned host memory, the step's launches (``body``, any sequence of the
+    launch objects above plus collectives) and the copies of its results back to pinned host
+    memory, captured once and replayed by `run` with a single graph launch. Refill the host
+    input buffers between runs; `run` does not synchronize (read the host outputs after a
+    `torch.cuda.synchronize()` or an event)."""
+
+    def __init__(self, body, inputs: Sequence[tuple[torch.Tensor, torch.Tensor]],
+                 outputs: Sequence[tuple[torch.Tensor, torch.Tensor]]) -> None:  # fmt: skip
+        for host, dev in inputs:
+            if not host.is_pinned() or host.shape != dev.shape or host.dtype != dev.dtype:
+                raise ValueError("every input needs a pinned host buffer of the device tensor's shape and dtype")
+        for dev, host in outputs:
+            if not host.is_pinned() or host.shape != dev.shape or host.dtype != dev.dtype:
+                raise ValueError("every output needs a pinned host buffer of the device tensor's shape and dtype")
+        self.inputs, self.outputs = list(inputs), list(outputs)
+
+        def step() -> None:
+            for host, dev in self.inputs:
+                dev.copy_(host, non_blocking=True)
+            body()
+            for dev, host in self.outputs:
+                host.copy_(dev, non_blocking=True)
+
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()  # once eagerly (lazy initialisation stays out of the graph)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            step()
+        torch.cuda.synchronize()
+
+    @property
+    def h2d_bytes(self) -> int:
+        return sum(h.numel() * h.element_size() for h, _ in self.inputs)
+
+    @property
+    def d2h_bytes(self) -> int:
+        return sum(h.numel() * h.element_size() for _, h in self.outputs)
+
+    def run(self) -> None:
+        self.graph.replay()
