@@ -153,11 +153,17 @@ def build_layer(args, rank: int, world: int, device: torch.device, keep_full: bo
     ex_plain = Exchange([(ms, args.block, args.batch, torch.float32)], world, rank, device)
     ys, vs = ex.parts
     gen = torch.Generator().manual_seed(0)
+    # the layer's activations in one device buffer (each group's x a 16-byte aligned view), so
+    # a step's inputs arrive with one host-to-device copy
+    host_x = [outlier_x(group[0][2], args.batch, gen) for group in LLAMA3_8B_GROUPS]
+    x_all = torch.cat([h.reshape(-1) for h in host_x]).to(device)
+    views, off = [], 0
+    for h in host_x:
+        views.append(x_all[off : off + h.numel()].view(h.shape if args.batch > 1 else h.shape[1:]))
+        off += h.numel()
     groups, plain, xs, full, j = [], [], [], [], 0
-    for group in LLAMA3_8B_GROUPS:
-        n = group[0][2]
-        x = outlier_x(n, args.batch, gen).to(device)
-        x = x[0].contiguous() if args.batch == 1 else x.contiguous()
+    for gi, group in enumerate(LLAMA3_8B_GROUPS):
+        x = views[gi]
         xs.append(x)
         items, items_plain, y_views, p_views, y_plain = [], [], [], [], []
         for _name, m, nn in group:
@@ -185,7 +191,12 @@ def build_layer(args, rank: int, world: int, device: torch.device, keep_full: bo
         groups.append(GemvLaunch(items, args.threads, ys=y_views, passed=p_views, verdicts=False))
         plain.append(GemvLaunch(items_plain, args.threads, ys=y_plain))
     verdict = VerdictLaunch(groups)
+    if not getattr(args, "no_prefetch", False):  # unchecked launches prefetch the next one's first pieces too
+        for i, g in enumerate(plain):
+            g.verdicts = False
+            g.set_next(plain[(i + 1) % len(plain)])
     torch.cuda.synchronize()
+    build_layer.x_all = x_all  # the buffer behind xs (one copy per step in the end-to-end reading)
     return groups, verdict, plain, xs, ex, ex_plain, full
 
 
@@ -245,14 +256,14 @@ def timed(graph: tuple[torch.cuda.CUDAGraph, int], steps: int, warmup: int, worl
     return ms / 1e3 / steps
 
 
-def e2e_step_time(launches, xs, ex, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
+def e2e_step_time(launches, x_all, ex, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
     """The public API with host buffers (`pck.cuda.plan.CapturedStep`): every step copies the
     layer's activations from pinned host memory, runs the layer's launches (and the gather),
     and copies every output and verdict bit back to pinned host memory; one graph launch per
     step. Device time per step, max over ranks."""
     from pck.cuda.plan import CapturedStep
 
-    hx = [x.cpu().pin_memory() for x in xs]
+    hx = [x_all.cpu().pin_memory()]  # x_all: the buffer the layer's activations are views of
     hout = torch.empty(ex.gathered.shape, dtype=ex.gathered.dtype, pin_memory=True)
 
     def body() -> None:
@@ -263,7 +274,7 @@ def e2e_step_time(launches, xs, ex, steps: int, warmup: int, world: int) -> tupl
 
     result = ex.gathered if world > 1 else ex.local
     hres = hout if world > 1 else torch.empty(ex.local.shape, dtype=ex.local.dtype, pin_memory=True)
-    step = CapturedStep(body, list(zip(hx, xs, strict=True)), [(result, hres)])
+    step = CapturedStep(body, [(hx[0], x_all)], [(result, hres)])
     for _ in range(warmup):
         step.run()
     torch.cuda.synchronize()
@@ -437,6 +448,8 @@ def e4m3_reading(args, device, steps: int, warmup: int) -> dict:
     groups, _verdict, plain, _xs, ex, _ex_plain, _ = build_layer(a, 0, 1, device)
     for i, g in enumerate(groups):
         g.set_prior([groups[i - 1]])
+        if not args.no_prefetch:
+            g.set_next(groups[(i + 1) % len(groups)])
     per = graph_steps(steps)
     g_checked = cuda_graph(lambda: [g.launch() for g in groups], per)
     g_plain = cuda_graph(lambda: [g.launch() for g in plain], per)
@@ -593,6 +606,8 @@ def main() -> None:
     parser.add_argument("--no-batch128", action="store_true", help="skip the batch-128 tensor-core reading")
     parser.add_argument("--no-e4m3", action="store_true", help="skip the E4M3 (config 3, batch 1) reading")
     parser.add_argument("--no-lm-head", action="store_true", help="skip the LM-head (config 5) reading")
+    parser.add_argument("--no-prefetch", action="store_true",
+                        help="launches do not prefetch the next launch's first weight pieces into L2")
     parser.add_argument("--verdicts", choices=sorted(VERDICTS), default="carried",
                         help="carried: each launch decides the previous launch's checks; launch: a verdict launch per step")
     args = parser.parse_args()
@@ -614,6 +629,7 @@ def main() -> None:
                                              device_id=device)  # fmt: skip
 
     groups, verdict, plain, xs, ex, ex_plain, full = build_layer(args, rank, world, device, keep_full=world > 1)
+    x_all = build_layer.x_all
     vs = ex.parts[1]
     step_bytes_local = sum(g.algorithmic_bytes for g in groups)
 
@@ -632,6 +648,8 @@ def main() -> None:
     if args.verdicts == "carried":  # each launch decides the previous one's checks
         for i, g in enumerate(groups):
             g.set_prior([groups[i - 1]])
+            if not args.no_prefetch:  # and prefetches the next one's first weight pieces
+                g.set_next(groups[(i + 1) % len(groups)])
         launches = list(groups)
     else:
         launches = [*groups, verdict]
@@ -674,7 +692,7 @@ def main() -> None:
         e4m3 = e4m3_reading(args, device, side_steps, args.warmup)
     if not args.no_lm_head:
         lm_head = lm_head_reading(rank, world, device, side_steps, args.warmup)
-    t_e2e, h2d, d2h = e2e_step_time(launches, xs, ex, side_steps, args.warmup, world)
+    t_e2e, h2d, d2h = e2e_step_time(launches, x_all, ex, side_steps, args.warmup, world)
 
     total_bytes = torch.tensor([float(step_bytes_local)], device=device)
     if world > 1:
@@ -710,6 +728,8 @@ def main() -> None:
                 "verdicts": VERDICTS[args.verdicts], "parallelism": f"row-shard x{world}" if world > 1 else "single",
                 "l2": "inputs larger than L2 (436 MB of weights per step, 126 MB L2)",
                 "graph": f"CUDA graph of {per_graph} consecutive steps, replayed",
+                "prefetch": "none" if args.no_prefetch else
+                            "each launch's CTAs prefetch the next launch's first weight pieces into L2 as they finish",
             },
             "checker_overhead_pct": round((t_checked / t_plain - 1) * 100, 2),
             "unchecked_ms_per_step": round(t_plain * 1e3, 5),

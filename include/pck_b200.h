@@ -45,8 +45,16 @@ extern "C" {
 /* Message of the last failing call on this thread ("" if none). */
 const char* pck_last_error(void);
 
-/* ABI version of this library (increases when a declaration here changes): 4. */
+/* ABI version of this library (increases when a declaration here changes): 6. */
 int pck_abi_version(void);
+
+/*
+ * SHA-256 (hex) over the sources this library was compiled from (csrc/, include/ and the
+ * compiler flags), as computed by the build; pck.manifest compares it with the sources on
+ * disk and their pinned hashes. No counterpart in the reference, whose checker is compiled
+ * at import time from the pinned sources themselves (src/pck/cuda/_ext.py:20-29).
+ */
+const char* pck_source_digest(void);
 
 /*
  * Device status word shared by every kernel of the library: bit 0 = a bounded wait gave up
@@ -197,6 +205,17 @@ int pck_gemv_partials(const pck_gemv_job* jobs, int count, void* stream);
  */
 int pck_gemv_pipelined(const pck_gemv_job* jobs, int count, const pck_check_desc* prior, int nprior,
                        void* stream);
+
+/*
+ * pck_gemv_pipelined for a launch that is followed on the stream by a known one (`next`, the
+ * jobs of that launch, e.g. the next projection group of a decode layer, which will decide
+ * this call's checks): as each CTA of this launch finishes its work, it prefetches into L2
+ * the first weight pieces that the same-numbered CTA of the next launch will read, so that
+ * launch starts from L2 while this one's last CTAs still stream. The results are those of
+ * pck_gemv_pipelined; nnext = 0 is pck_gemv_pipelined. No reference counterpart.
+ */
+int pck_gemv_pipelined_next(const pck_gemv_job* jobs, int count, const pck_check_desc* prior, int nprior,
+                            const pck_gemv_job* next, int nnext, void* stream);
 
 /*
  * The block verdicts of up to PCK_MAX_JOBS checks whose partial sums an earlier

@@ -121,10 +121,22 @@ int64_t fill_verdicts(const pck_check_desc* const* descs, int count, const int32
 int run_verdicts(const pck_check_desc* const* descs, int count, cudaStream_t stream,
                  const int32_t* fixed_segs);
 
-// Plans and launches the streaming kernel for `specs` (validated by the caller); `prior`
-// (validated, at most kMaxVerdictJobs) are checks of earlier launches that this one decides.
-int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
-               const std::vector<const pck_check_desc*>& prior = {}) {
+// Launch shape of a planned streaming launch.
+struct StreamShape {
+  bool empty = false;  // no job has work (only prior verdicts, if any)
+  int wfmt = 0;
+  int nv = 8;
+  int bg = 1;
+  bool tma = false;
+  unsigned grid = 0;
+  size_t smem = 0;
+};
+
+// Plans the streaming kernel for `specs` (validated by the caller) into `plan` (zeroed by the
+// caller); `prior` (validated, at most kMaxVerdictJobs) are checks of earlier launches that
+// this one decides.
+int plan_stream(const std::vector<Spec>& specs, const std::vector<const pck_check_desc*>& prior,
+                pck::Plan& plan, StreamShape& shape) {
   if (specs.empty() || specs.size() > static_cast<size_t>(pck::kMaxJobs)) {
     return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %zu", pck::kMaxJobs, specs.size());
   }
@@ -168,14 +180,14 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
     }
   }
   if (live.empty()) {  // nothing to stream: the prior verdicts alone
-    return prior.empty() ? ok() : run_verdicts(prior.data(), static_cast<int>(prior.size()), stream, nullptr);
+    shape.empty = true;
+    return PCK_OK;
   }
 
   // Pass 2: units and bytes of every job (one row per row unit). A checked GEMV becomes two
   // jobs of the launch: its rows, and its bank rows (reduced against the same x). Their
   // partial sums meet in the verdict kernel, so the bank work need not follow the rows of
   // its block; as a job of its own it is spread over CTAs weighted by its cost.
-  pck::Plan plan{};
   int64_t x_bytes = 0;
   std::vector<double> bytes;  // cost-weighted, for the CTA split
   int64_t max_row_bytes = 0;
@@ -369,10 +381,63 @@ int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
   plan.prior_tasks = prior_tasks;
 
   if (!tma) bg = 1;
-  const unsigned grid = static_cast<unsigned>(begin + verdict_ctas);
-  const cudaError_t err = wfmt == pck::kWeightsBf16
-                              ? pck::launch_stream_bf16(plan, nv, bg, tma, grid, smem, stream)
-                              : pck::launch_stream_e4m3(plan, nv, bg, tma, grid, smem, stream);
+  shape.wfmt = wfmt;
+  shape.nv = nv;
+  shape.bg = bg;
+  shape.tma = tma;
+  shape.grid = static_cast<unsigned>(begin + verdict_ctas);
+  shape.smem = smem;
+  return PCK_OK;
+}
+
+// The first weight pieces of the launch planned in `next` (its GEMV CTAs' first row per warp,
+// up to two pieces each), as a table in `plan` that the CTAs of `plan`'s launch prefetch into
+// L2 as they finish.
+void fill_prefetch(pck::Plan& plan, const pck::Plan& next, const StreamShape& ns) {
+  plan.next_ctas = 0;
+  if (ns.empty || !ns.tma) return;
+  int nj = 0;
+  int8_t map[pck::kMaxPlanJobs];
+  for (int j = 0; j < next.njobs; ++j) {
+    map[j] = -1;
+    const pck::JobPlan& jb = next.jobs[j];
+    if (!jb.has_w || jb.has_check || jb.rows != 1 || nj >= pck::kMaxPrefetchJobs) continue;
+    pck::PrefetchJob& pj = plan.next_jobs[nj];
+    pj.W = static_cast<const uint8_t*>(jb.W);
+    pj.row_bytes = jb.row_bytes;
+    pj.bytes = static_cast<int32_t>(std::min<int64_t>(jb.row_bytes, 2LL * next.sum_bytes) / 16 * 16);
+    map[j] = static_cast<int8_t>(nj++);
+  }
+  const int ctas = std::min<int>(next.verdict_cta_begin, pck::kMaxCtas);
+  for (int c = 0; c < ctas; ++c) {
+    const int j = next.cta_job[c];
+    plan.next_job[c] = static_cast<uint8_t>(map[j] < 0 ? 255 : map[j]);
+    plan.next_units[c] = next.cta_units[c];
+  }
+  plan.next_ctas = ctas;
+}
+
+// Plans and launches the streaming kernel for `specs`; with `next` (the jobs of the launch
+// that follows on the stream, deciding `next_prior`), the CTAs also prefetch that launch's
+// first weight pieces into L2 as they finish.
+int run_stream(const std::vector<Spec>& specs, cudaStream_t stream,
+               const std::vector<const pck_check_desc*>& prior = {}, const std::vector<Spec>* next = nullptr,
+               const std::vector<const pck_check_desc*>& next_prior = {}) {
+  pck::Plan plan{};
+  StreamShape shape;
+  if (int rc = plan_stream(specs, prior, plan, shape)) return rc;
+  if (shape.empty) {
+    return prior.empty() ? ok() : run_verdicts(prior.data(), static_cast<int>(prior.size()), stream, nullptr);
+  }
+  if (next && !next->empty() && shape.tma) {
+    pck::Plan np{};
+    StreamShape ns;
+    if (plan_stream(*next, next_prior, np, ns) == PCK_OK) fill_prefetch(plan, np, ns);
+    g_error.clear();  // a next launch that does not plan only loses its prefetch
+  }
+  const cudaError_t err = shape.wfmt == pck::kWeightsBf16
+                              ? pck::launch_stream_bf16(plan, shape.nv, shape.bg, shape.tma, shape.grid, shape.smem, stream)
+                              : pck::launch_stream_e4m3(plan, shape.nv, shape.bg, shape.tma, shape.grid, shape.smem, stream);
   if (err != cudaSuccess) return cuda_fail("streaming kernel", err);
   return ok();
 }
@@ -456,6 +521,20 @@ bool encode_bf16_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t co
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A 2-D E4M3 tensor map over rows x cols bytes (row-major), box 64 columns x 128 rows, no
+// swizzle (the kernel widens the tile to bfloat16 itself), zero fill outside.
+bool encode_e4m3_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(pck::kTcTileK), static_cast<cuuint32_t>(pck::kTcTileM)};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // A byte range of device memory (NULL or empty: nothing).
 struct Range {
   const void* p;
@@ -481,11 +560,84 @@ int check_gemv_args(const void* W, const void* x, const float* y, int64_t m, int
 
 }  // namespace
 
+namespace {
+
+// The specs of a validated job array (shared by the pipelined entry points).
+int job_specs(const pck_gemv_job* jobs, int count, std::vector<Spec>& specs) {
+  if (count < 1 || count > PCK_MAX_JOBS || !jobs) {
+    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", PCK_MAX_JOBS, count);
+  }
+  for (int i = 0; i < count; ++i) {
+    const pck_gemv_job& jb = jobs[i];
+    const int wfmt = jb.weight_format & ~PCK_WEIGHTS_SETTLED;
+    if (wfmt != PCK_WEIGHTS_BF16 && wfmt != PCK_WEIGHTS_E4M3) {
+      return fail(PCK_ERR_ARGUMENT, "unknown weight format %d", jb.weight_format);
+    }
+    if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, jb.threads, 32)) return rc;
+    if (jb.batch < 1 || jb.batch > pck::kMaxBatch) {
+      return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %d", pck::kMaxBatch, jb.batch);
+    }
+    if (jb.check) {
+      const pck_check_desc* d = jb.check;
+      if (int rc = validate_check(d)) return rc;
+      if (d->x != jb.X || d->y != jb.Y || d->n != jb.n || d->batch != jb.batch ||
+          static_cast<int64_t>(d->num_blocks) * d->block != jb.m) {
+        return fail(PCK_ERR_ARGUMENT, "a fused check must cover the job's own x, y and shape");
+      }
+    }
+    specs.push_back(Spec{jb.W, jb.X, jb.Y, jb.m, jb.n, jb.batch, jb.threads, wfmt, true,
+                         (jb.weight_format & PCK_WEIGHTS_SETTLED) != 0, jb.check, jb.w_exp_min, jb.w_exp_max});
+  }
+  return PCK_OK;
+}
+
+// The prior checks of a pipelined call, validated against what the call's jobs write.
+int prior_checks(const pck_gemv_job* jobs, int count, const pck_check_desc* prior, int nprior,
+                 std::vector<const pck_check_desc*>& before) {
+  if (nprior < 0 || nprior > PCK_MAX_JOBS || (nprior > 0 && !prior)) {
+    return fail(PCK_ERR_ARGUMENT, "prior checks must number [0, %d], got %d", PCK_MAX_JOBS, nprior);
+  }
+  for (int i = 0; i < nprior; ++i) {
+    const pck_check_desc* d = prior + i;
+    if (int rc = validate_check(d)) return rc;
+    // The prior checks' inputs must be final and their outputs untouched by this launch.
+    const int64_t nb = d->num_blocks, rows = nb * d->block;
+    const Range reads_writes[] = {
+        {d->y, 4 * d->batch * rows},
+        {d->partial_cx, 8 * d->batch * d->checks * nb * d->segments},
+        {d->partial_s, 8 * d->batch * nb * d->segments},
+        {d->passed, d->batch * d->checks * nb},
+        {d->rho, 8 * d->batch * d->checks * nb},
+        {d->tau, 8 * d->batch * d->checks * nb},
+    };
+    for (int j = 0; j < count; ++j) {
+      const pck_gemv_job& jb = jobs[j];
+      const pck_check_desc* c = jb.check;
+      const Range writes[] = {
+          {jb.Y, 4 * jb.batch * jb.m},
+          {c ? c->partial_cx : nullptr, c ? 8LL * c->batch * c->checks * c->num_blocks * c->segments : 0},
+          {c ? c->partial_s : nullptr, c ? 8LL * c->batch * c->num_blocks * c->segments : 0},
+      };
+      for (const Range& a : reads_writes) {
+        for (const Range& b : writes) {
+          if (overlaps(a, b)) {
+            return fail(PCK_ERR_ARGUMENT, "prior check %d shares memory with what job %d writes", i, j);
+          }
+        }
+      }
+    }
+    before.push_back(d);
+  }
+  return PCK_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* pck_last_error(void) { return g_error.c_str(); }
 
-int pck_abi_version(void) { return 4; }
+int pck_abi_version(void) { return 6; }
 
 int pck_device_status(unsigned int* status, int clear) {
   if (!status) return fail(PCK_ERR_ARGUMENT, "status must not be NULL");
@@ -558,67 +710,27 @@ int pck_gemv_partials(const pck_gemv_job* jobs, int count, void* stream) {
 
 int pck_gemv_pipelined(const pck_gemv_job* jobs, int count, const pck_check_desc* prior, int nprior,
                        void* stream) {
-  if (count < 1 || count > PCK_MAX_JOBS || !jobs) {
-    return fail(PCK_ERR_ARGUMENT, "batch size must be in [1, %d], got %d", PCK_MAX_JOBS, count);
-  }
-  if (nprior < 0 || nprior > PCK_MAX_JOBS || (nprior > 0 && !prior)) {
-    return fail(PCK_ERR_ARGUMENT, "prior checks must number [0, %d], got %d", PCK_MAX_JOBS, nprior);
-  }
+  return pck_gemv_pipelined_next(jobs, count, prior, nprior, nullptr, 0, stream);
+}
+
+int pck_gemv_pipelined_next(const pck_gemv_job* jobs, int count, const pck_check_desc* prior, int nprior,
+                            const pck_gemv_job* next, int nnext, void* stream) {
   std::vector<Spec> specs;
-  for (int i = 0; i < count; ++i) {
-    const pck_gemv_job& jb = jobs[i];
-    const int wfmt = jb.weight_format & ~PCK_WEIGHTS_SETTLED;
-    if (wfmt != PCK_WEIGHTS_BF16 && wfmt != PCK_WEIGHTS_E4M3) {
-      return fail(PCK_ERR_ARGUMENT, "unknown weight format %d", jb.weight_format);
-    }
-    if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, jb.threads, 32)) return rc;
-    if (jb.batch < 1 || jb.batch > pck::kMaxBatch) {
-      return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %d", pck::kMaxBatch, jb.batch);
-    }
-    if (jb.check) {
-      const pck_check_desc* d = jb.check;
-      if (int rc = validate_check(d)) return rc;
-      if (d->x != jb.X || d->y != jb.Y || d->n != jb.n || d->batch != jb.batch ||
-          static_cast<int64_t>(d->num_blocks) * d->block != jb.m) {
-        return fail(PCK_ERR_ARGUMENT, "a fused check must cover the job's own x, y and shape");
-      }
-    }
-    specs.push_back(Spec{jb.W, jb.X, jb.Y, jb.m, jb.n, jb.batch, jb.threads, wfmt, true,
-                         (jb.weight_format & PCK_WEIGHTS_SETTLED) != 0, jb.check, jb.w_exp_min, jb.w_exp_max});
-  }
+  if (int rc = job_specs(jobs, count, specs)) return rc;
   std::vector<const pck_check_desc*> before;
-  for (int i = 0; i < nprior; ++i) {
-    const pck_check_desc* d = prior + i;
-    if (int rc = validate_check(d)) return rc;
-    // The prior checks' inputs must be final and their outputs untouched by this launch.
-    const int64_t nb = d->num_blocks, rows = nb * d->block;
-    const Range reads_writes[] = {
-        {d->y, 4 * d->batch * rows},
-        {d->partial_cx, 8 * d->batch * d->checks * nb * d->segments},
-        {d->partial_s, 8 * d->batch * nb * d->segments},
-        {d->passed, d->batch * d->checks * nb},
-        {d->rho, 8 * d->batch * d->checks * nb},
-        {d->tau, 8 * d->batch * d->checks * nb},
-    };
-    for (int j = 0; j < count; ++j) {
-      const pck_gemv_job& jb = jobs[j];
-      const pck_check_desc* c = jb.check;
-      const Range writes[] = {
-          {jb.Y, 4 * jb.batch * jb.m},
-          {c ? c->partial_cx : nullptr, c ? 8LL * c->batch * c->checks * c->num_blocks * c->segments : 0},
-          {c ? c->partial_s : nullptr, c ? 8LL * c->batch * c->num_blocks * c->segments : 0},
-      };
-      for (const Range& a : reads_writes) {
-        for (const Range& b : writes) {
-          if (overlaps(a, b)) {
-            return fail(PCK_ERR_ARGUMENT, "prior check %d shares memory with what job %d writes", i, j);
-          }
-        }
-      }
-    }
-    before.push_back(d);
+  if (int rc = prior_checks(jobs, count, prior, nprior, before)) return rc;
+  if (nnext < 0 || nnext > PCK_MAX_JOBS || (nnext > 0 && !next)) {
+    return fail(PCK_ERR_ARGUMENT, "next jobs must number [0, %d], got %d", PCK_MAX_JOBS, nnext);
   }
-  return run_stream(specs, static_cast<cudaStream_t>(stream), before);
+  std::vector<Spec> next_specs;
+  std::vector<const pck_check_desc*> next_prior;  // the next launch decides this call's checks
+  if (nnext > 0) {
+    if (int rc = job_specs(next, nnext, next_specs)) return rc;
+    for (int i = 0; i < count; ++i) {
+      if (jobs[i].check && jobs[i].m > 0) next_prior.push_back(jobs[i].check);
+    }
+  }
+  return run_stream(specs, static_cast<cudaStream_t>(stream), before, nnext > 0 ? &next_specs : nullptr, next_prior);
 }
 
 int pck_check_verdicts(const pck_check_desc* descs, int count, void* stream) {
@@ -750,25 +862,32 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   if (batch < 1 || batch > pck::kTcMaxBatch) {
     return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %d", pck::kTcMaxBatch, batch);
   }
+  const int wfmt = jobs[0].weight_format & ~PCK_WEIGHTS_SETTLED;
+  if (wfmt != PCK_WEIGHTS_BF16 && wfmt != PCK_WEIGHTS_E4M3) {
+    return fail(PCK_ERR_ARGUMENT, "unknown weight format %d", jobs[0].weight_format);
+  }
+  const bool e4m3 = wfmt == PCK_WEIGHTS_E4M3;
+  const int n_pad = (batch + 15) / 16 * 16;
   int tiles = 0, nj = 0;
+  const pck_check_desc* descs[pck::kTcMaxJobs] = {};
   for (int i = 0; i < count; ++i) {
     const pck_gemv_job& jb = jobs[i];
-    if ((jb.weight_format & ~PCK_WEIGHTS_SETTLED) != PCK_WEIGHTS_BF16) {
-      return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV takes bfloat16 weights only");
+    if ((jb.weight_format & ~PCK_WEIGHTS_SETTLED) != wfmt) {
+      return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the weight format");
     }
     if (jb.batch != batch) return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the batch");
     if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, 256, 1)) return rc;
     if (jb.m == 0) continue;
-    if (jb.n % 8 != 0 || !aligned16(jb.W) || !aligned16(jb.X)) {
-      return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV needs n a multiple of 8 and 16-byte aligned W and X");
+    if (jb.n % (e4m3 ? 16 : 8) != 0 || !aligned16(jb.W) || !aligned16(jb.X)) {
+      return fail(PCK_ERR_UNSUPPORTED, "the tensor-core GEMV needs n a multiple of 8 (16 for E4M3) and 16-byte "
+                                       "aligned W and X");
     }
     if (jb.m > (1LL << 31) - pck::kTcTileM || jb.n > (1LL << 31)) return fail(PCK_ERR_UNSUPPORTED, "matrix too large");
     pck::TcJob& tj = plan.jobs[nj];
-    const int n_pad = (batch + 15) / 16 * 16;
-    if (!encode_bf16_map(&tj.w_map, jb.W, jb.m, jb.n, pck::kTcTileM) ||
-        !encode_bf16_map(&tj.x_map, jb.X, batch, jb.n, n_pad)) {
-      return fail(PCK_ERR_CUDA, "tensor map encoding failed");
-    }
+    const bool maps = (e4m3 ? encode_e4m3_map(&tj.w_map, jb.W, jb.m, jb.n)
+                            : encode_bf16_map(&tj.w_map, jb.W, jb.m, jb.n, pck::kTcTileM)) &&
+                      encode_bf16_map(&tj.x_map, jb.X, batch, jb.n, n_pad);
+    if (!maps) return fail(PCK_ERR_CUDA, "tensor map encoding failed");
     tj.Y = jb.Y;
     tj.m = jb.m;
     tj.n = jb.n;
@@ -788,6 +907,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
       if (!(d->coef > 0) || !(d->geps > 0) || !(d->tau_floor > 0)) {
         return fail(PCK_ERR_ARGUMENT, "coef, geps and floor must be positive");
       }
+      descs[nj] = d;
     }
     tj.tile_begin = tiles;
     tj.tiles = static_cast<int32_t>((jb.m + pck::kTcTileM - 1) / pck::kTcTileM);
@@ -798,40 +918,97 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   plan.njobs = nj;
   plan.total_tiles = tiles;
   plan.batch = batch;
-  plan.n_pad = (batch + 15) / 16 * 16;
-  const size_t stage = pck::tc_stage_bytes(plan.n_pad);
-  plan.stages = static_cast<int32_t>(std::min<size_t>(8, (232448 - 1024 - 256) / stage));
-  // Few tiles with a small batch or a long K: split the K range of every tile over a cluster
-  // of CTAs while the launch still fits in one wave (one CTA per SM), keeping at least 4 K
-  // blocks (256 columns) per split. Otherwise the persistent kernel, whose two accumulators
-  // overlap one tile's epilogue with the next tile's loads.
+  plan.n_pad = n_pad;
+  plan.weights = e4m3 ? pck::kTcWeightsE4m3 : pck::kTcWeightsBf16;
+
+  // The form: with at least as many tiles as SMs, the persistent kernel (units of two tiles
+  // sharing each staged X tile); with fewer, each tile's K range split over a cluster of CTAs
+  // (up to 8, at least 4 K blocks each) so that the launch still fills the GPU.
+  const int sms = sm_count();
   int64_t kmin = INT64_MAX;
   for (int j = 0; j < nj; ++j) kmin = std::min<int64_t>(kmin, (plan.jobs[j].n + pck::kTcTileK - 1) / pck::kTcTileK);
-  int splits = 1;
-  if (tiles * 2 <= sm_count() && (batch <= 32 || kmin >= 128)) {
-    while (splits < pck::kTcMaxSplits && static_cast<int64_t>(tiles) * splits * 2 <= sm_count() &&
-           kmin / (2 * splits) >= 4) {
-      splits *= 2;
+  int splits = 1;  // a power of two: clusters of 3, 5, ... CTAs ran far slower
+  if (tiles < sms) {
+    while (splits * 2 <= pck::kTcMaxSplits && tiles * splits * 2 <= sms && kmin / (splits * 2) >= 4) splits *= 2;
+  }
+  plan.unit_tiles = splits == 1 ? pck::kTcMaxUnitTiles : 1;
+  plan.strided = 0;
+  plan.total_units = 0;
+  for (int j = 0; j < nj; ++j) {
+    plan.jobs[j].unit_begin = plan.total_units;
+    plan.jobs[j].units = (plan.jobs[j].tiles + plan.unit_tiles - 1) / plan.unit_tiles;
+    plan.total_units += plan.jobs[j].units;
+  }
+
+  // Checks whose bank rows the kernel reduces itself: 128-row blocks (one per tile), at most
+  // kTcMaxChecks sign draws, 16-byte aligned bank rows, room for one partial sum per tile (per
+  // K range in the split form), and batches up to kTcFuseMaxBatch: the binary64 work per stage
+  // grows with the batch while a stage's weight bytes do not, and past 64 columns the bank
+  // warps fall behind the weight stream (measured: the separate bank launch is then faster).
+  // Others take the wide-batch bank kernel.
+  const int segs_fused = splits;
+  int max_checks = 0;
+  for (int j = 0; j < nj; ++j) {
+    const pck_check_desc* d = descs[j];
+    pck::TcJob& tj = plan.jobs[j];
+    if (d && batch <= pck::kTcFuseMaxBatch && d->block == pck::kTcTileM && d->checks <= pck::kTcMaxChecks &&
+        d->segments >= segs_fused &&
+        aligned16(d->c) && aligned16(d->a)) {
+      tj.fused = 1;
+      tj.c = d->c;
+      tj.a = static_cast<const uint16_t*>(d->a);
+      tj.partial_cx = d->partial_cx;
+      tj.partial_s = d->partial_s;
+      tj.checks = d->checks;
+      tj.nb = d->num_blocks;
+      tj.seg_alloc = d->segments;
+      max_checks = std::max(max_checks, d->checks);
     }
   }
-  plan.acc_stride = (plan.n_pad + 31) / 32 * 32;  // every epilogue read takes 32 columns
+  plan.any_fused = max_checks > 0;
+  plan.max_checks = max_checks;
+
+  plan.w_bytes = plan.unit_tiles * pck::kTcTileM * 128;
+  plan.x_bytes = n_pad * 128;
+  plan.tile_bank_bytes = plan.any_fused ? max_checks * 256 + 128 : 0;
+  plan.bank_bytes = (plan.unit_tiles * plan.tile_bank_bytes + 1023) / 1024 * 1024;
+  plan.raw_bytes = e4m3 ? plan.unit_tiles * pck::kTcTileM * 64 : 0;
+  plan.stage_bytes = (plan.w_bytes + plan.x_bytes + plan.bank_bytes + plan.raw_bytes + 1023) / 1024 * 1024;
+  // Beyond the stages: 1024 bytes of alignment slack, the bank warps' binary64 staging and
+  // group sums, and the barriers.
+  const size_t extra = 1024 + pck::kTcBankSmemBytes + 8 * (3 * 8 + 5) + 16;
+  constexpr size_t kSmemCap = 232448;
+  plan.stages = static_cast<int32_t>(std::min<size_t>(8, (kSmemCap - extra) / plan.stage_bytes));
+  if (plan.stages < 2) return fail(PCK_ERR_UNSUPPORTED, "a batch of %d leaves no room for two stages", batch);
+  if (splits > 1 && static_cast<size_t>(plan.stages) * plan.stage_bytes < static_cast<size_t>(pck::kTcTileM) * (n_pad + 1) * 4) {
+    return fail(PCK_ERR_UNSUPPORTED, "no room for the partial accumulator of a batch of %d", batch);
+  }
+  plan.acc_stride = (n_pad + 31) / 32 * 32;  // every epilogue read takes 32 columns
+  plan.acc_bufs = (splits == 1 && 2 * plan.unit_tiles * plan.acc_stride <= 512) ? 2 : 1;
   int cols = 32;
-  while (cols < (splits == 1 ? 2 * plan.acc_stride : plan.n_pad)) cols *= 2;
+  while (cols < plan.acc_bufs * plan.unit_tiles * plan.acc_stride) cols *= 2;
   plan.tmem_cols = cols;
-  const size_t smem = 1024 + static_cast<size_t>(plan.stages) * stage + 256;
-  cudaError_t err = pck::launch_tc(plan, splits, smem, static_cast<cudaStream_t>(stream));
+  const size_t smem = extra + static_cast<size_t>(plan.stages) * plan.stage_bytes;
+  const int grid = splits == 1 ? std::min(plan.strided ? plan.total_units : tiles, sms) : tiles * splits;
+  cudaError_t err = pck::launch_tc(plan, splits, grid, smem, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("tensor-core gemv kernel", err);
-  // The checks: the wide-batch bank kernel (bank rows x batch columns in binary64), then the
-  // block verdicts.
+
+  // The checks: the wide-batch bank kernel for the checks the GEMV kernel did not reduce
+  // (bank rows x batch columns in binary64), then the block verdicts of all of them.
   const pck_check_desc* checks[pck::kTcMaxJobs];
   int32_t segs[pck::kTcMaxJobs];
-  int nc = 0;
+  int nc = 0, nbank = 0;
   pck::BankBatchPlan bank{};
   int max_segs = 1;
-  for (int i = 0; i < count; ++i) {
-    const pck_check_desc* d = jobs[i].check;
-    if (!d || jobs[i].m == 0) continue;
-    pck::BankBatchJob& bj = bank.jobs[nc];
+  for (int j = 0; j < nj; ++j) {
+    const pck_check_desc* d = descs[j];
+    if (!d) continue;
+    if (plan.jobs[j].fused) {
+      segs[nc] = segs_fused;
+      checks[nc++] = d;
+      continue;
+    }
+    pck::BankBatchJob& bj = bank.jobs[nbank++];
     bj.c = d->c;
     bj.a = static_cast<const uint16_t*>(d->a);
     bj.X = static_cast<const uint16_t*>(d->x);
@@ -852,9 +1029,11 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
     checks[nc++] = d;
   }
   if (nc == 0) return ok();
-  bank.njobs = nc;
-  err = pck::launch_bank_batch(bank, (batch + 31) / 32, max_segs, static_cast<cudaStream_t>(stream));
-  if (err != cudaSuccess) return cuda_fail("bank kernel", err);
+  if (nbank > 0) {
+    bank.njobs = nbank;
+    err = pck::launch_bank_batch(bank, (batch + 31) / 32, max_segs, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail("bank kernel", err);
+  }
   return run_verdicts(checks, nc, static_cast<cudaStream_t>(stream), segs);
 }
 

@@ -92,6 +92,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// mbar_wait for waits that usually last long (a whole tile of work): each try suspends the
+// thread in hardware for up to `hint_ns` or until the phase completes, instead of spinning,
+// so waiting warps leave the issue slots to the warps that compute. Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns = 20000) {
+  const unsigned long long start = global_ns();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    if (done) return true;
+    if (global_ns() - start > kWaitLimitNs) {
+      report(kDevTimeout);
+      return false;
+    }
+  }
+}
+
 // L2 policy for data read exactly once (weights, bank rows).
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;

@@ -1336,6 +1336,23 @@ __device__ __forceinline__ void staged_warp(const JobPlan& jb, int64_t u0, int64
   }
 }
 
+// Once this warp has finished its units: the first pieces of row (next_units[c].x + warp) of
+// the next launch's CTA c (same index), into L2, so the next launch starts from L2 while this
+// one's last CTAs still stream (the launch boundary keeps HBM busy).
+__device__ __forceinline__ void prefetch_next(const Plan& plan, int warp, int lane) {
+  const int c = static_cast<int>(blockIdx.x);
+  if (lane != 0 || c >= plan.next_ctas) return;
+  const int j = plan.next_job[c];
+  if (j == 255) return;
+  const int2 r = plan.next_units[c];
+  const int64_t row = static_cast<int64_t>(r.x) + warp;
+  if (row >= r.y) return;
+  const PrefetchJob& pj = plan.next_jobs[j];
+  if (pj.bytes <= 0) return;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pj.W + row * pj.row_bytes), "r"(pj.bytes)
+               : "memory");
+}
+
 template <int WFMT, int NV, int BG, bool kTma>
 __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_constant__ Plan plan) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1343,6 +1360,7 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
     allow_dependents();
     wait_for_producers();
     prior_verdicts(plan, static_cast<int>(threadIdx.x) / kWarp, static_cast<int>(threadIdx.x) % kWarp);
+    prefetch_next(plan, static_cast<int>(threadIdx.x) / kWarp, static_cast<int>(threadIdx.x) % kWarp);
     return;
   }
   // The CTA's job and unit range come precomputed (one parameter read, no divisions).
@@ -1350,9 +1368,12 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
   const JobPlan& jb = plan.jobs[plan.cta_job[blockIdx.x]];
   const int64_t u0 = range.x;
   const int64_t count = range.y - range.x;
-  if (count <= 0) return;  // uniform for the whole CTA
   const int warp = static_cast<int>(threadIdx.x) / kWarp;
   const int lane = static_cast<int>(threadIdx.x) % kWarp;
+  if (count <= 0) {  // uniform for the whole CTA
+    if constexpr (kTma) prefetch_next(plan, warp, lane);
+    return;
+  }
 
   if constexpr (kTma) {
     const int slots = plan.stages;  // per warp
@@ -1405,6 +1426,7 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
                                 ring, full, xs_addr,
                                 warp, lane, inputs);
     }
+    prefetch_next(plan, warp, lane);
   } else {
     // Plain path: every warp takes whole units and reads global memory directly, one
     // element at a time (product, then sum: the same values as the staged path's).

@@ -113,6 +113,15 @@ __host__ __device__ __forceinline__ int64_t first_unit_at(const JobPlan& jb, int
   return base + ru + static_cast<int64_t>(jb.checks) * jb.segs + ceil_div64(rem, 2 * jb.seg_len);
 }
 
+// A GEMV job of the launch that follows, whose first weight pieces this launch prefetches.
+constexpr int kMaxPrefetchJobs = 16;
+struct PrefetchJob {
+  const uint8_t* W;
+  int64_t row_bytes;
+  int32_t bytes;  // prefetched from the start of each row (up to two row pieces)
+  int32_t pad;
+};
+
 struct Plan {
   JobPlan jobs[kMaxPlanJobs];
   int32_t njobs;
@@ -128,6 +137,13 @@ struct Plan {
   VerdictPlan prior;          // checks of an earlier launch decided by this one
   int2 cta_units[kMaxCtas];   // CTA c reduces units [x, y) of job cta_job[c]
   uint8_t cta_job[kMaxCtas];
+  // The next launch's first pieces: CTA c of this launch, as its warps finish, prefetches into
+  // L2 the first pieces of rows next_units[c].x + w (w = the warp) of next_jobs[next_job[c]],
+  // the rows the next launch's CTA c starts with (255: nothing).
+  int32_t next_ctas;
+  PrefetchJob next_jobs[kMaxPrefetchJobs];
+  int2 next_units[kMaxCtas];
+  uint8_t next_job[kMaxCtas];
 };
 
 // Host-side launch of one instantiation family (stream_bf16.cu, stream_e4m3.cu). nv is

@@ -1,25 +1,37 @@
-// Tensor-core batched GEMV for decode batches: Y (batch, m) = X (batch, n) W^T with bfloat16 W
-// and X and binary32 accumulation in tensor memory (tcgen05), for the batched decode path.
+// Tensor-core batched GEMV for decode batches: Y (batch, m) = X (batch, n) W^T with bfloat16 X,
+// bfloat16 or E4M3 W (E4M3 widened exactly to bfloat16 in shared memory) and binary32
+// accumulation in tensor memory (tcgen05), with the binary64 checksum-bank sums of each job's
+// blocked check reduced in the same pass over the staged X tiles.
 //
 // The summation order is the tensor core's, not the reference's coalesced tree, so the result
 // is not bit-exact to it; its checker uses the declared height of this accumulation (see
 // pck.cuda.gemv.tc_height): each tcgen05.mma adds 16 exact products to the accumulator, at most
 // n/16 of them in sequence per output.
 //
-// A 128-row tile of W is one thread-block cluster of `splits` CTAs (splits <= 8, chosen by
-// the host so that small matrices still fill the GPU); CTA r of the cluster accumulates the
-// r-th range of the tile's K blocks:
-//   warp 0      one thread issues the TMA loads of a 128 x 64 tile of W and the n_pad x 64 tile
-//               of X per stage (128-byte swizzle, the canonical K-major layout of the MMA);
-//   warp 1      allocates the tensor memory, and one thread issues four 128 x n_pad x 16 MMAs
-//               per stage, committing each stage back to the producer and the last to the
-//               epilogue;
-//   warps 2..5  copy the accumulator out of tensor memory (warp w reads lanes 32 (w % 4) ...)
-//               into shared memory. After a cluster barrier, CTA r adds rows r*128/splits ...
-//               of all the cluster's partial accumulators, in rank order (distributed shared
-//               memory), and stores them as columns of Y.
-// Every mbarrier wait is bounded; a wait that gives up records the status bit and the roles
-// stop issuing work.
+// Work is a sequence of 128-row tiles of W (one checker block each when the check is fused).
+// Two forms share the kernel body:
+//   persistent  a CTA per SM takes a contiguous range of the launch's tiles and walks it in
+//               units of up to two tiles of one job, which share every staged X tile (two
+//               MMAs per K step, two accumulators): X crosses L2 once per 256 rows of W;
+//   split       a tile per cluster of `splits` CTAs; CTA r accumulates the r-th range of the
+//               tile's K blocks, the partial accumulators are added in rank order through
+//               distributed shared memory (for launches with fewer tiles than SMs).
+// Roles (14 warps):
+//   warp 0      one thread issues, per stage, the TMA loads of the unit's W tiles (128 rows x
+//               64 columns each; bfloat16 with 128-byte swizzle, or raw E4M3 bytes) and of the
+//               n_pad x 64 X tile, and the bulk copies of the fused checks' bank rows;
+//   warp 1      allocates tensor memory; one thread issues four 128 x n_pad x 16 MMAs per tile
+//               and stage and commits each stage back to the producer, each unit to the epilogue;
+//   warps 2..5  copy the accumulators out of tensor memory (warp w reads lanes 32 (w % 4) ...)
+//               into Y (persistent) or into shared memory for the cluster sum (split);
+//   warps 6..13 the bank warps: widen E4M3 tiles to bfloat16 for the MMA, and for fused checks
+//               reduce the stage's bank rows against the stage's X tile in binary64 — c . x
+//               rounded to nearest, a . |x| rounded up, exact products (binary32 x bfloat16
+//               and bfloat16 x bfloat16 fit in 53 bits) — into the checks' partial sums: one
+//               segment per tile (persistent) or per K range (split).
+// A stage is released to the producer once the MMAs have read it (tcgen05.commit) and every
+// bank warp is done with it. Every mbarrier wait is bounded; a wait that gives up records the
+// status bit and the roles stop issuing work.
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -33,6 +45,10 @@ namespace cg = cooperative_groups;
 
 namespace pck {
 namespace {
+
+constexpr uint32_t kTileBf16Bytes = kTcTileM * 128u;  // one 128 x 64 bfloat16 tile
+constexpr uint32_t kTileE4m3Bytes = kTcTileM * 64u;   // one 128 x 64 E4M3 tile
+constexpr int kBankThreads = 32 * kTcBankWarps;
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             uint64_t policy) {
@@ -72,6 +88,9 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// Shared-memory writes of this thread become visible to the tensor core (the async proxy).
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -84,42 +103,434 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void lds_f64x2(uint32_t addr, double& a, double& b) {
+  asm volatile("ld.shared.v2.f64 {%0, %1}, [%2];" : "=d"(a), "=d"(b) : "r"(addr));
+}
+
+__device__ __forceinline__ void lds_f64x2_one(uint32_t addr, double& a) {
+  asm volatile("ld.shared.f64 %0, [%1];" : "=d"(a) : "r"(addr));
+}
+
+__device__ __forceinline__ void sts_f64(uint32_t addr, double v) {
+  asm volatile("st.shared.f64 [%0], %1;" ::"r"(addr), "d"(v) : "memory");
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Two E4M3 values (low byte first) to two bfloat16 in one word, exactly: E4M3 -> binary16 is
+// exact, binary16 -> binary32 is exact, and a value of at most 4 significant bits in the
+// E4M3 range rounds to itself in bfloat16.
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t pair) {
+  uint32_t h2, out;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(pair)));
+  asm("{\n\t.reg .b16 l, h;\n\t.reg .f32 fl, fh;\n\tmov.b32 {l, h}, %1;\n\tcvt.f32.f16 fl, l;\n\t"
+      "cvt.f32.f16 fh, h;\n\tcvt.rn.bf16x2.f32 %0, fh, fl;\n\t}"
+      : "=r"(out)
+      : "r"(h2));
+  return out;
+}
+
 __device__ __forceinline__ int job_of(const TcPlan& plan, int tile) {
   int j = 0;
   while (j + 1 < plan.njobs && tile >= plan.jobs[j + 1].tile_begin) ++j;
   return j;
 }
 
-// The persistent form (splits == 1 and many tiles): a CTA per SM walks the tiles with two
-// tensor-memory accumulators, so the epilogue of one tile overlaps the main loop of the next.
-__global__ void __launch_bounds__(kTcThreads, 1) tc_persistent_kernel(const __grid_constant__ TcPlan plan) {
-  // The bank kernel that follows (launched as a programmatic dependent) reads nothing this
-  // kernel writes, so it may start on the SMs this grid leaves free.
+// One item of a CTA's work: `ntiles` consecutive 128-row tiles of one job (from job-local
+// tile `tile`), over the K blocks [kb0, kb1); its bank sums go to segment `seg`.
+struct Work {
+  int job;
+  int tile;
+  int ntiles;
+  int kb0;
+  int kb1;
+  int seg;
+};
+
+// The work sequence of a CTA; every role walks the same one.
+struct WorkWalk {
+  int cur;
+  int end;
+  bool split;
+};
+
+__device__ __forceinline__ WorkWalk work_start(const TcPlan& plan, bool split) {
+  WorkWalk w;
+  w.split = split;
+  if (split) {
+    w.cur = 0;
+    w.end = 1;
+  } else if (plan.strided) {
+    w.cur = static_cast<int>(blockIdx.x);  // a unit index, stepping by the grid
+    w.end = plan.total_units;
+  } else {
+    const int64_t total = plan.total_tiles, g = gridDim.x, c = blockIdx.x;
+    w.cur = static_cast<int>(c * total / g);
+    w.end = static_cast<int>((c + 1) * total / g);
+  }
+  return w;
+}
+
+__device__ __forceinline__ bool work_next(const TcPlan& plan, WorkWalk& w, Work& out) {
+  if (w.cur >= w.end) return false;
+  if (w.split) {
+    cg::cluster_group cluster = cg::this_cluster();
+    const int splits = static_cast<int>(cluster.num_blocks());
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int tile = static_cast<int>(blockIdx.x) / splits;
+    out.job = job_of(plan, tile);
+    const TcJob& jb = plan.jobs[out.job];
+    out.tile = tile - jb.tile_begin;
+    out.ntiles = 1;
+    const int kblocks = static_cast<int>((jb.n + kTcTileK - 1) / kTcTileK);
+    const int kper = (kblocks + splits - 1) / splits;
+    out.kb0 = min(kblocks, rank * kper);
+    out.kb1 = min(kblocks, out.kb0 + kper);
+    out.seg = rank;
+    w.cur = 1;
+    return true;
+  }
+  if (plan.strided) {
+    int j = 0;
+    while (j + 1 < plan.njobs && w.cur >= plan.jobs[j + 1].unit_begin) ++j;
+    const TcJob& jb = plan.jobs[j];
+    out.job = j;
+    out.tile = (w.cur - jb.unit_begin) * plan.unit_tiles;
+    out.ntiles = min(plan.unit_tiles, jb.tiles - out.tile);
+    out.kb0 = 0;
+    out.kb1 = static_cast<int>((jb.n + kTcTileK - 1) / kTcTileK);
+    out.seg = 0;
+    w.cur += static_cast<int>(gridDim.x);
+    return true;
+  }
+  out.job = job_of(plan, w.cur);
+  const TcJob& jb = plan.jobs[out.job];
+  out.tile = w.cur - jb.tile_begin;
+  out.ntiles = (plan.unit_tiles > 1 && w.cur + 1 < w.end && out.tile + 1 < jb.tiles) ? 2 : 1;
+  out.kb0 = 0;
+  out.kb1 = static_cast<int>((jb.n + kTcTileK - 1) / kTcTileK);
+  out.seg = 0;
+  w.cur += out.ntiles;
+  return true;
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// Bank warps
+
+// Which batch columns and which 16-byte chunks of a stage's X rows a bank thread reduces. The
+// 256 bank threads form `nsplit` groups of `group` threads, group g taking chunks
+// [8g / nsplit, 8(g + 1) / nsplit) of every column. Up to 32 columns: one column per thread
+// (group 32, 8 groups); more: two columns c and c + group per thread (group = the batch
+// rounded up to 64, 128 or 256, halved), so each widened bank value serves two columns. A
+// group is whole warps, so the chunks of a warp are uniform. The group sums are added in
+// group order at the end of a work item.
+struct BankLanes {
+  int col[2];  // batch columns, -1 for none
+  int ch0;
+  int ch1;
+  int split;
+  int nsplit;
+  int group;
+};
+
+__device__ __forceinline__ BankLanes bank_lanes(int batch, int bt) {
+  BankLanes L;
+  if (batch <= 32) {
+    L.group = 32;
+    L.col[0] = bt % 32 < batch ? bt % 32 : -1;
+    L.col[1] = -1;
+  } else {
+    L.group = (batch <= 64 ? 64 : batch <= 128 ? 128 : 256) / 2;
+    const int c = bt % L.group;
+    L.col[0] = c < batch ? c : -1;
+    L.col[1] = c + L.group < batch ? c + L.group : -1;
+  }
+  L.nsplit = kBankThreads / L.group;
+  L.split = bt / L.group;
+  const int per = 8 / L.nsplit;
+  L.ch0 = L.split * per;
+  L.ch1 = L.ch0 + per;
+  return L;
+}
+
+// The stage's raw E4M3 tiles widened to bfloat16 in the 128-byte-swizzled K-major layout the
+// MMA reads (16-byte chunk c of row r at chunk c ^ (r % 8) of the row), then made visible to
+// the tensor core.
+__device__ __forceinline__ void widen_stage(const TcPlan& plan, int ntiles, uint8_t* stage, int bt) {
+  const uint32_t raw = smem_addr(stage + plan.w_bytes + plan.x_bytes + plan.bank_bytes);
+  const uint32_t wbase = smem_addr(stage);
+  const int items = ntiles * kTcTileM * 8;  // 8 bytes of one row each
+  for (int i = bt; i < items; i += kBankThreads) {
+    const int t = i >> 10, r = (i >> 3) & (kTcTileM - 1), ch = i & 7;
+    const uint2 q = lds64(raw + static_cast<uint32_t>(t) * kTileE4m3Bytes + static_cast<uint32_t>(r * 64 + ch * 8));
+    uint4 o;
+    o.x = e4m3x2_to_bf16x2(q.x & 0xFFFFu);
+    o.y = e4m3x2_to_bf16x2(q.x >> 16);
+    o.z = e4m3x2_to_bf16x2(q.y & 0xFFFFu);
+    o.w = e4m3x2_to_bf16x2(q.y >> 16);
+    sts128(wbase + static_cast<uint32_t>(t) * kTileBf16Bytes + static_cast<uint32_t>(r * 128 + ((ch ^ (r & 7)) << 4)), o);
+  }
+  fence_proxy_async();
+}
+
+// Running sums of a bank thread over a work item, per column: c . x per (tile, check) rounded
+// to nearest, a . |x| per tile rounded up, each as kPartials interleaved partial sums (column j
+// to partial j % kPartials), added in order at the end. Binary64 FMAs take about 100 cycles
+// on this GPU, so a warp needs many independent chains; the binary64 bound holds for any split
+// of a sum.
+constexpr int kPartials = 2;
+struct BankSums {
+  double cx[2][kTcMaxUnitTiles][kTcMaxChecks][kPartials];
+  double sx[2][kTcMaxUnitTiles][kPartials];
+};
+
+__device__ __forceinline__ void bank_zero(BankSums& a) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+#pragma unroll
+    for (int t = 0; t < kTcMaxUnitTiles; ++t) {
+#pragma unroll
+      for (int p = 0; p < kPartials; ++p) {
+        a.sx[c][t][p] = 0.0;
+#pragma unroll
+        for (int k = 0; k < kTcMaxChecks; ++k) a.cx[c][t][k][p] = 0.0;
+      }
+    }
+  }
+}
+
+// One stage of the fused check for one bank warp. The warp widens to binary64 the bank values
+// its chunks need (rows c[k] and a of each tile of the unit, zeros past the end of the row)
+// into its own staging buffer at shared address `wstg` ([tile][row][32 columns j]), then each
+// thread, chunk by chunk: its columns' 8 activations widened, and per tile and bank row 4
+// two-value shared loads serving 8 FMAs per column. Only the warp synchronizes; every access
+// names the shared space.
+__device__ __forceinline__ void bank_stage(const TcPlan& plan, const TcJob& jb, int ntiles, int kb,
+                                           const uint8_t* stage, uint32_t wstg, const BankLanes& L, int lane,
+                                           BankSums& acc) {
+  const int K = jb.checks;
+  const int jmax = static_cast<int>(min(static_cast<int64_t>(kTcTileK), jb.n - static_cast<int64_t>(kb) * kTcTileK));
+  const uint32_t bank = smem_addr(stage + plan.w_bytes + plan.x_bytes);
+  const int j0 = L.ch0 * 8, jn = (L.ch1 - L.ch0) * 8;  // at most 32 columns j
+  __syncwarp();  // the previous stage's reads of the buffer are done
+  if (lane < jn) {  // lane jj widens column j0 + jj of every bank row of the unit
+    const int j = j0 + lane;
+#pragma unroll
+    for (int t = 0; t < kTcMaxUnitTiles; ++t) {
+      if (t >= ntiles) break;
+      const uint32_t tb = bank + static_cast<uint32_t>(t * plan.tile_bank_bytes);
+      const uint32_t dst = wstg + static_cast<uint32_t>((t * (kTcMaxChecks + 1) * 32 + lane) * 8);
+#pragma unroll
+      for (int r = 0; r <= kTcMaxChecks; ++r) {
+        if (r > K) break;
+        double v = 0.0;
+        if (j < jmax) {
+          if (r < K) {
+            v = static_cast<double>(__uint_as_float(lds32(tb + static_cast<uint32_t>(r * 256 + j * 4))));
+          } else {
+            const uint32_t w = lds32(tb + static_cast<uint32_t>(K * 256 + (j & ~1) * 2));
+            v = static_cast<double>((j & 1) ? bf16_hi(w) : bf16_lo(w));
+          }
+        }
+        sts_f64(dst + static_cast<uint32_t>(r * 32 * 8), v);
+      }
+    }
+  }
+  __syncwarp();
+  if (L.col[0] < 0) return;
+  const uint32_t xs = smem_addr(stage + plan.w_bytes);
+  const bool two = L.col[1] >= 0;
+  for (int ch = L.ch0; ch < L.ch1 && ch * 8 < jmax; ++ch) {  // jmax is a multiple of 8
+    double xv[2][8], ax[2][8];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int b = (c == 0 || two) ? L.col[c] : L.col[0];
+      const uint4 q = lds128(xs + static_cast<uint32_t>(b * 128 + ((ch ^ (b & 7)) << 4)));
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        xv[c][h] = static_cast<double>((h & 1) ? bf16_hi(w[h >> 1]) : bf16_lo(w[h >> 1]));
+        ax[c][h] = fabs(xv[c][h]);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kTcMaxUnitTiles; ++t) {
+      if (t >= ntiles) break;
+      const uint32_t row0 = wstg + static_cast<uint32_t>((t * (kTcMaxChecks + 1) * 32 + (ch - L.ch0) * 8) * 8);
+#pragma unroll
+      for (int k = 0; k <= kTcMaxChecks; ++k) {
+        if (k > K) break;
+        double v[8];
+#pragma unroll
+        for (int h = 0; h < 8; h += 2) lds_f64x2(row0 + static_cast<uint32_t>((k * 32 + h) * 8), v[h], v[h + 1]);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          if (c == 1 && !two) break;
+          if (k < K) {
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+              acc.cx[c][t][k][h % kPartials] = __fma_rn(v[h], xv[c][h], acc.cx[c][t][k][h % kPartials]);
+            }
+          } else {
+#pragma unroll
+            for (int h = 0; h < 8; ++h) acc.sx[c][t][h % kPartials] = __fma_ru(v[h], ax[c][h], acc.sx[c][t][h % kPartials]);
+          }
+        }
+      }
+    }
+  }
+}
+
+// The end of a work item: each thread's partial sums added in order, then the chunk groups'
+// sums added in group order through `comb` (the bank warps' staging area, at its shared
+// address; barrier `ready` three times: every warp is done with its staging, every sum is in
+// place, every sum is read) and stored as segment `seg` of the checks' partial sums.
+// `phase` counts the barrier's completions. False if a barrier wait gave up.
+__device__ __forceinline__ bool bank_finish(const TcJob& jb, const Work& wk, uint32_t comb, uint64_t* ready,
+                                            uint32_t& phase, const BankLanes& L, int bt, const BankSums& acc) {
+  const int K = jb.checks;
+  double cx[2][kTcMaxUnitTiles][kTcMaxChecks], sx[2][kTcMaxUnitTiles];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+#pragma unroll
+    for (int t = 0; t < kTcMaxUnitTiles; ++t) {
+      sx[c][t] = acc.sx[c][t][0];
+#pragma unroll
+      for (int p = 1; p < kPartials; ++p) sx[c][t] = __dadd_ru(sx[c][t], acc.sx[c][t][p]);
+#pragma unroll
+      for (int k = 0; k < kTcMaxChecks; ++k) {
+        cx[c][t][k] = acc.cx[c][t][k][0];
+#pragma unroll
+        for (int p = 1; p < kPartials; ++p) cx[c][t][k] = __dadd_rn(cx[c][t][k], acc.cx[c][t][k][p]);
+      }
+    }
+  }
+  auto sync = [&]() {
+    mbar_arrive(ready);
+    const bool ok = mbar_wait(ready, phase & 1u);
+    ++phase;
+    return ok;
+  };
+  auto at = [&](int t, int r, int c, int thread) {
+    return comb + static_cast<uint32_t>((((t * (kTcMaxChecks + 1) + r) * 2 + c) * kBankThreads + thread) * 8);
+  };
+  if (L.nsplit > 1) {
+    if (!sync()) return false;  // the staging buffers are free
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+#pragma unroll
+      for (int t = 0; t < kTcMaxUnitTiles; ++t) {
+        if (t >= wk.ntiles) break;
+#pragma unroll
+        for (int k = 0; k < kTcMaxChecks; ++k) {
+          if (k < K) sts_f64(at(t, k, c, bt), cx[c][t][k]);
+        }
+        sts_f64(at(t, kTcMaxChecks, c, bt), sx[c][t]);
+      }
+    }
+    if (!sync()) return false;  // every group's sums are in place
+    if (L.split == 0) {
+      for (int g = 1; g < L.nsplit; ++g) {
+        const int src = bt + g * L.group;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int t = 0; t < kTcMaxUnitTiles; ++t) {
+            if (t >= wk.ntiles) break;
+            double other;
+#pragma unroll
+            for (int k = 0; k < kTcMaxChecks; ++k) {
+              if (k < K) {
+                lds_f64x2_one(at(t, k, c, src), other);
+                cx[c][t][k] = __dadd_rn(cx[c][t][k], other);
+              }
+            }
+            lds_f64x2_one(at(t, kTcMaxChecks, c, src), other);
+            sx[c][t] = __dadd_ru(sx[c][t], other);
+          }
+        }
+      }
+    }
+    if (!sync()) return false;  // the area is free for the next stage's staging
+    if (L.split != 0) return true;
+  }
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int b = L.col[c];
+    if (b < 0) continue;
+#pragma unroll
+    for (int t = 0; t < kTcMaxUnitTiles; ++t) {
+      if (t >= wk.ntiles) break;
+      const int64_t beta = wk.tile + t;
+#pragma unroll
+      for (int k = 0; k < kTcMaxChecks; ++k) {
+        if (k < K) jb.partial_cx[((static_cast<int64_t>(b) * K + k) * jb.nb + beta) * jb.seg_alloc + wk.seg] = cx[c][t][k];
+      }
+      jb.partial_s[(static_cast<int64_t>(b) * jb.nb + beta) * jb.seg_alloc + wk.seg] = sx[c][t];
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------------------------
+// The kernel (kSplit: the cluster form)
+
+template <bool kSplit>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant__ TcPlan plan) {
+  // A kernel launched after this one as its programmatic dependent reads nothing it writes
+  // (the bank kernel for unfused checks), so it may start on the SMs this grid leaves free.
   allow_dependents();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   const int stages = plan.stages;
-  const uint32_t a_bytes = kTcTileM * 128u;
-  const uint32_t b_bytes = static_cast<uint32_t>(plan.n_pad) * 128u;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(stages) * stage_bytes);
+  const uint32_t stage_bytes = static_cast<uint32_t>(plan.stage_bytes);
+  uint8_t* bank_area = smem + static_cast<size_t>(stages) * stage_bytes;  // kTcBankSmemBytes
+  uint64_t* full = reinterpret_cast<uint64_t*>(bank_area + kTcBankSmemBytes);
   uint64_t* empty = full + stages;
-  uint64_t* tfull = empty + stages;   // [2]
+  uint64_t* wready = empty + stages;  // E4M3: the stage's W widened
+  uint64_t* tfull = wready + stages;  // [2]
   uint64_t* tempty = tfull + 2;       // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* comb_ready = tempty + 2;  // the bank threads' barrier at the end of a work item
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(comb_ready + 1);
+  const bool e4m3 = plan.weights == kTcWeightsE4m3;
+  const bool bank_role = plan.any_fused != 0 || e4m3;
   const int warp = static_cast<int>(threadIdx.x) / kWarp;
   const int lane = static_cast<int>(threadIdx.x) % kWarp;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, 1);
+      mbar_init(empty + s, 1 + (bank_role ? kTcBankWarps : 0));
+      mbar_init(wready + s, kTcBankWarps);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull + a, 1);
       mbar_init(tempty + a, 4);
     }
+    mbar_init(comb_ready, kBankThreads);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -129,222 +540,222 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_persistent_kernel(const __gr
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kSplit) {
+    cg::this_cluster().sync();  // every CTA's barriers are initialised before any peer access
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t tile_w_bytes = e4m3 ? kTileE4m3Bytes : kTileBf16Bytes;
+  [[maybe_unused]] Work last{};  // the split form's one item, for its epilogue
+  [[maybe_unused]] uint32_t last_it = 0;
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
       const uint64_t stream_policy = policy_evict_first();
       const uint64_t keep_policy = policy_evict_last();
+      WorkWalk walk = work_start(plan, kSplit);
+      Work wk;
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < plan.total_tiles; tile += gridDim.x) {
-        const TcJob& jb = plan.jobs[job_of(plan, tile)];
-        const int row0 = (tile - jb.tile_begin) * kTcTileM;
-        const int kblocks = static_cast<int>((jb.n + kTcTileK - 1) / kTcTileK);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+      while (ok && work_next(plan, walk, wk)) {
+        const TcJob& jb = plan.jobs[wk.job];
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++it) {
           const int s = static_cast<int>(it % stages);
-          if (!mbar_wait(empty + s, ((it / stages) & 1u) ^ 1u)) {
+          if (!mbar_wait_sleep(empty + s, ((it / stages) & 1u) ^ 1u)) {
             ok = false;
             break;
           }
-          uint8_t* a_dst = smem + static_cast<size_t>(s) * stage_bytes;
-          mbar_arrive_expect_tx(full + s, stage_bytes);
-          tma_load_2d(a_dst, &jb.w_map, full + s, kb * kTcTileK, row0, stream_policy);
-          tma_load_2d(a_dst + a_bytes, &jb.x_map, full + s, kb * kTcTileK, 0, keep_policy);
+          uint8_t* st = smem + static_cast<size_t>(s) * stage_bytes;
+          const int64_t col = static_cast<int64_t>(kb) * kTcTileK;
+          const uint32_t jmax = static_cast<uint32_t>(min(static_cast<int64_t>(kTcTileK), jb.n - col));
+          uint32_t bytes = static_cast<uint32_t>(wk.ntiles) * tile_w_bytes + static_cast<uint32_t>(plan.x_bytes);
+          if (jb.fused) bytes += static_cast<uint32_t>(wk.ntiles) * (static_cast<uint32_t>(jb.checks) * jmax * 4u + jmax * 2u);
+          mbar_arrive_expect_tx(full + s, bytes);
+          uint8_t* wdst = e4m3 ? st + plan.w_bytes + plan.x_bytes + plan.bank_bytes : st;
+          for (int t = 0; t < wk.ntiles; ++t) {
+            tma_load_2d(wdst + static_cast<size_t>(t) * tile_w_bytes, &jb.w_map, full + s, kb * kTcTileK,
+                        (wk.tile + t) * kTcTileM, stream_policy);
+          }
+          tma_load_2d(st + plan.w_bytes, &jb.x_map, full + s, kb * kTcTileK, 0, keep_policy);
+          if (jb.fused) {
+            for (int t = 0; t < wk.ntiles; ++t) {
+              const int64_t beta = wk.tile + t;
+              uint8_t* tb = st + plan.w_bytes + plan.x_bytes + t * plan.tile_bank_bytes;
+              for (int k = 0; k < jb.checks; ++k) {
+                bulk_load(tb + k * 256, jb.c + (static_cast<int64_t>(k) * jb.nb + beta) * jb.n + col, jmax * 4u,
+                          full + s, stream_policy);
+              }
+              bulk_load(tb + jb.checks * 256, jb.a + beta * jb.n + col, jmax * 2u, full + s, stream_policy);
+            }
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
       const uint32_t idesc = instr_desc(plan.n_pad);
+      WorkWalk walk = work_start(plan, kSplit);
+      Work wk;
       uint32_t it = 0, local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < plan.total_tiles; tile += gridDim.x, ++local) {
-        const TcJob& jb = plan.jobs[job_of(plan, tile)];
-        const int kblocks = static_cast<int>((jb.n + kTcTileK - 1) / kTcTileK);
-        const uint32_t acc = local & 1u;
-        if (!mbar_wait(tempty + acc, ((local >> 1) & 1u) ^ 1u)) break;
+      while (ok && work_next(plan, walk, wk)) {
+        const uint32_t ab = kSplit ? 0u : local % static_cast<uint32_t>(plan.acc_bufs);
+        const uint32_t use = kSplit ? 0u : local / static_cast<uint32_t>(plan.acc_bufs);
+        if (!mbar_wait_sleep(tempty + ab, (use & 1u) ^ 1u)) break;
         tc_fence_after();
-        const uint32_t d = tmem + acc * static_cast<uint32_t>(plan.acc_stride);
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++it) {
           const int s = static_cast<int>(it % stages);
-          if (!mbar_wait(full + s, (it / stages) & 1u)) {
+          const uint32_t parity = (it / stages) & 1u;
+          if (!mbar_wait_sleep(full + s, parity) || (e4m3 && !mbar_wait_sleep(wready + s, parity))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_addr(smem + static_cast<size_t>(s) * stage_bytes);
-          const uint64_t adesc = sw128_desc(a_addr);
-          const uint64_t bdesc = sw128_desc(a_addr + a_bytes);
+          const uint32_t st = smem_addr(smem + static_cast<size_t>(s) * stage_bytes);
+          const uint64_t bdesc = sw128_desc(st + static_cast<uint32_t>(plan.w_bytes));
+          for (int t = 0; t < wk.ntiles; ++t) {
+            const uint32_t d = tmem + (ab * static_cast<uint32_t>(plan.unit_tiles) + static_cast<uint32_t>(t)) *
+                                          static_cast<uint32_t>(plan.acc_stride);
+            const uint64_t adesc = sw128_desc(st + static_cast<uint32_t>(t) * kTileBf16Bytes);
 #pragma unroll
-          for (int k = 0; k < kTcTileK / 16; ++k) {  // 16 bfloat16 = 32 bytes = 2 descriptor units
-            umma_bf16(d, adesc + 2u * k, bdesc + 2u * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kTcTileK / 16; ++k) {  // 16 bfloat16 = 32 bytes = 2 descriptor units
+              umma_bf16(d, adesc + 2u * k, bdesc + 2u * k, idesc, (kb > wk.kb0 || k > 0) ? 1u : 0u);
+            }
           }
-          umma_commit(empty + s);  // the stage is free once these MMAs have read it
+          umma_commit(empty + s);  // the stage is free once these MMAs (and the bank warps) are done
         }
-        if (ok) umma_commit(tfull + acc);
+        if (ok && wk.kb1 > wk.kb0) umma_commit(tfull + ab);
+        ++local;
       }
     }
-  } else {  // epilogue warps 2..5
+  } else if (warp < 6) {  // epilogue warps 2..5
     const int quarter = warp % 4;
-    uint32_t local = 0;
-    for (int tile = blockIdx.x; tile < plan.total_tiles; tile += gridDim.x, ++local) {
-      const TcJob& jb = plan.jobs[job_of(plan, tile)];
-      const uint32_t acc = local & 1u;
-      if (!mbar_wait(tfull + acc, (local >> 1) & 1u)) break;
-      tc_fence_after();
-      const int64_t row = static_cast<int64_t>(tile - jb.tile_begin) * kTcTileM + quarter * 32 + lane;
-      const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + acc * static_cast<uint32_t>(plan.acc_stride);
-      for (int c0 = 0; c0 < plan.n_pad; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(base + static_cast<uint32_t>(c0), v);
-        if (row < jb.m) {
+    if constexpr (!kSplit) {
+      WorkWalk walk = work_start(plan, false);
+      Work wk;
+      uint32_t local = 0;
+      while (work_next(plan, walk, wk)) {
+        const TcJob& jb = plan.jobs[wk.job];
+        const uint32_t ab = local % static_cast<uint32_t>(plan.acc_bufs);
+        const uint32_t use = local / static_cast<uint32_t>(plan.acc_bufs);
+        if (!mbar_wait_sleep(tfull + ab, use & 1u)) break;
+        tc_fence_after();
+        for (int t = 0; t < wk.ntiles; ++t) {
+          const int64_t row = static_cast<int64_t>(wk.tile + t) * kTcTileM + quarter * 32 + lane;
+          const uint32_t base = tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                (ab * static_cast<uint32_t>(plan.unit_tiles) + static_cast<uint32_t>(t)) *
+                                    static_cast<uint32_t>(plan.acc_stride);
+          for (int c0 = 0; c0 < plan.n_pad; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(base + static_cast<uint32_t>(c0), v);
+            if (row < jb.m) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (c0 + i < plan.batch) jb.Y[static_cast<int64_t>(c0 + i) * jb.m + row] = __uint_as_float(v[i]);
+              for (int i = 0; i < 32; ++i) {
+                if (c0 + i < plan.batch) jb.Y[static_cast<int64_t>(c0 + i) * jb.m + row] = __uint_as_float(v[i]);
+              }
+            }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty + ab);
+        ++local;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty + acc);
+    } else {
+      WorkWalk walk = work_start(plan, true);
+      work_next(plan, walk, last);
+      last_it = static_cast<uint32_t>(last.kb1 - last.kb0);
     }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(static_cast<uint32_t>(plan.tmem_cols))
-                 : "memory");
-  }
-}
-
-// The split form: one tile per cluster of `splits` CTAs, each a range of the tile's K blocks.
-__global__ void __launch_bounds__(kTcThreads, 1) tc_split_kernel(const __grid_constant__ TcPlan plan) {
-  allow_dependents();  // as in tc_persistent_kernel
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_addr(smem_raw);
-  uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  cg::cluster_group cluster = cg::this_cluster();
-  const int splits = static_cast<int>(cluster.num_blocks());
-  const int rank = static_cast<int>(cluster.block_rank());
-  const int stages = plan.stages;
-  const uint32_t a_bytes = kTcTileM * 128u;
-  const uint32_t b_bytes = static_cast<uint32_t>(plan.n_pad) * 128u;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(stages) * stage_bytes);
-  uint64_t* empty = full + stages;
-  uint64_t* tfull = empty + stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
-  // After the main loop the stages hold the partial accumulator: 128 rows of n_pad + 1 words
-  // (the extra word keeps the rows of a warp in different banks).
-  float* part = reinterpret_cast<float*>(smem);
-  const int pstride = plan.n_pad + 1;
-  const int warp = static_cast<int>(threadIdx.x) / kWarp;
-  const int lane = static_cast<int>(threadIdx.x) % kWarp;
-
-  const int tile = static_cast<int>(blockIdx.x) / splits;
-  const TcJob& jb = plan.jobs[job_of(plan, tile)];
-  const int row0 = (tile - jb.tile_begin) * kTcTileM;
-  const int kblocks = static_cast<int>((jb.n + kTcTileK - 1) / kTcTileK);
-  const int kper = (kblocks + splits - 1) / splits;
-  const int kb0 = min(kblocks, rank * kper);
-  const int kb1 = min(kblocks, kb0 + kper);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < stages; ++s) {
-      mbar_init(full + s, 1);
-      mbar_init(empty + s, 1);
-    }
-    mbar_init(tfull, 1);
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                 "r"(static_cast<uint32_t>(plan.tmem_cols))
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {  // TMA producer
-      const uint64_t stream_policy = policy_evict_first();
-      const uint64_t keep_policy = policy_evict_last();
-      uint32_t it = 0;
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
-        const int s = static_cast<int>(it % stages);
-        if (!mbar_wait(empty + s, ((it / stages) & 1u) ^ 1u)) break;
-        uint8_t* a_dst = smem + static_cast<size_t>(s) * stage_bytes;
-        mbar_arrive_expect_tx(full + s, stage_bytes);
-        tma_load_2d(a_dst, &jb.w_map, full + s, kb * kTcTileK, row0, stream_policy);
-        tma_load_2d(a_dst + a_bytes, &jb.x_map, full + s, kb * kTcTileK, 0, keep_policy);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {  // MMA issuer
-      const uint32_t idesc = instr_desc(plan.n_pad);
-      uint32_t it = 0;
-      bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+  } else if (bank_role) {  // bank warps 6..13
+    const int bt = static_cast<int>(threadIdx.x) - 6 * kWarp;
+    const BankLanes L = bank_lanes(plan.batch, bt);
+    const uint32_t wstg = smem_addr(bank_area) + static_cast<uint32_t>((warp - 6) * kTcBankWarpStage * 8);
+    WorkWalk walk = work_start(plan, kSplit);
+    Work wk;
+    uint32_t it = 0, phase = 0;
+    bool ok = true;
+    BankSums acc;
+    while (ok && work_next(plan, walk, wk)) {
+      const TcJob& jb = plan.jobs[wk.job];
+      bank_zero(acc);
+      for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++it) {
         const int s = static_cast<int>(it % stages);
         if (!mbar_wait(full + s, (it / stages) & 1u)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t a_addr = smem_addr(smem + static_cast<size_t>(s) * stage_bytes);
-        const uint64_t adesc = sw128_desc(a_addr);
-        const uint64_t bdesc = sw128_desc(a_addr + a_bytes);
-#pragma unroll
-        for (int k = 0; k < kTcTileK / 16; ++k) {  // 16 bfloat16 = 32 bytes = 2 descriptor units
-          umma_bf16(tmem, adesc + 2u * k, bdesc + 2u * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        uint8_t* st = smem + static_cast<size_t>(s) * stage_bytes;
+        if (e4m3) {
+          widen_stage(plan, wk.ntiles, st, bt);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(wready + s);
         }
-        umma_commit(empty + s);  // the stage is free once these MMAs have read it
+        if (jb.fused) bank_stage(plan, jb, wk.ntiles, kb, st, wstg, L, lane, acc);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + s);
       }
-      if (ok && kb1 > kb0) umma_commit(tfull);
-    }
-  } else {  // epilogue warps 2..5: the partial accumulator into shared memory
-    const int quarter = warp % 4;
-    const int lrow = quarter * 32 + lane;
-    const bool have = __all_sync(kFullMask, kb1 > kb0 && mbar_wait(tfull, 0));  // uniform per warp
-    tc_fence_after();
-    for (int c0 = 0; c0 < plan.n_pad; c0 += 32) {
-      uint32_t v[32];
-      if (have) tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(c0), v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (c0 + i < plan.n_pad) part[lrow * pstride + c0 + i] = have ? __uint_as_float(v[i]) : 0.0f;
-      }
+      if (ok && jb.fused && wk.kb1 > wk.kb0) ok = bank_finish(jb, wk, smem_addr(bank_area), comb_ready, phase, L, bt, acc);
     }
   }
-  __syncwarp();  // the roles' lane 0 rejoins its warp before the cluster barrier
-  tc_fence_before();
-  cluster.sync();  // every CTA's partial is in its shared memory
 
-  if (warp >= 2) {  // rows [rank * R, (rank + 1) * R) of the tile, summed over the cluster
-    const int R = kTcTileM / splits;
-    const int t = static_cast<int>(threadIdx.x) - 2 * kWarp;  // 0..127
-    for (int idx = t; idx < R * plan.batch; idx += 4 * kWarp) {
-      const int r = rank * R + idx % R;
-      const int col = idx / R;
-      float sum = 0.0f;
-      for (int c = 0; c < splits; ++c) {
-        const float* peer = cluster.map_shared_rank(part, c);
-        const float v = peer[r * pstride + col];
-        sum = c == 0 ? v : __fadd_rn(sum, v);
+  if constexpr (kSplit) {
+    // The partial accumulator into shared memory (over the stages, once every stage is done
+    // with: the last stage's release covers the MMAs and the bank warps), the cluster sum in
+    // rank order, rows [rank * R, (rank + 1) * R) of the tile per CTA.
+    float* part = reinterpret_cast<float*>(smem);
+    const int pstride = plan.n_pad + 1;  // keeps the rows of a warp in different banks
+    if (warp >= 2 && warp < 6) {
+      const int quarter = warp % 4;
+      const int lrow = quarter * 32 + lane;
+      bool have = last_it > 0;
+      if (have) {
+        const uint32_t i = last_it - 1;
+        have = mbar_wait_sleep(tfull, 0) && mbar_wait_sleep(empty + i % stages, (i / stages) & 1u);
       }
-      const int64_t row = static_cast<int64_t>(row0) + r;
-      if (row < jb.m) jb.Y[static_cast<int64_t>(col) * jb.m + row] = sum;
+      have = __all_sync(kFullMask, have);
+      tc_fence_after();
+      for (int c0 = 0; c0 < plan.n_pad; c0 += 32) {
+        uint32_t v[32];
+        if (have) tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(c0), v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (c0 + i < plan.n_pad) part[lrow * pstride + c0 + i] = have ? __uint_as_float(v[i]) : 0.0f;
+        }
+      }
     }
+    __syncwarp();  // the roles' lane 0 rejoins its warp before the cluster barrier
+    tc_fence_before();
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every CTA's partial is in its shared memory
+    if (warp >= 2 && warp < 6) {
+      const int splits = static_cast<int>(cluster.num_blocks());
+      const int rank = static_cast<int>(cluster.block_rank());
+      const TcJob& jb = plan.jobs[last.job];
+      const int R = kTcTileM / splits;
+      const int r0 = rank * R;
+      const int rows = rank == splits - 1 ? kTcTileM - r0 : R;
+      const int t = static_cast<int>(threadIdx.x) - 2 * kWarp;  // 0..127
+      for (int idx = t; idx < rows * plan.batch; idx += 4 * kWarp) {
+        const int r = r0 + idx % rows;
+        const int colb = idx / rows;
+        float sum = 0.0f;
+        for (int c = 0; c < splits; ++c) {
+          const float* peer = cluster.map_shared_rank(part, c);
+          const float v = peer[r * pstride + colb];
+          sum = c == 0 ? v : __fadd_rn(sum, v);
+        }
+        const int64_t row = static_cast<int64_t>(last.tile) * kTcTileM + r;
+        if (row < jb.m) jb.Y[static_cast<int64_t>(colb) * jb.m + row] = sum;
+      }
+    }
+    cluster.sync();  // no CTA leaves while a peer may still read its partial
+  } else {
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
   }
-  cluster.sync();  // no CTA leaves while a peer may still read its partial
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -357,24 +768,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_split_kernel(const __grid_co
 
 PCK_STATUS_READER(tc_status)
 
-size_t tc_stage_bytes(int n_pad) { return static_cast<size_t>(kTcTileM) * 128 + static_cast<size_t>(n_pad) * 128; }
-
-cudaError_t launch_tc(const TcPlan& plan, int splits, size_t smem, cudaStream_t stream) {
+cudaError_t launch_tc(const TcPlan& plan, int splits, int grid, size_t smem, cudaStream_t stream) {
   static int configured[64] = {0};
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    for (auto* fn : {tc_persistent_kernel, tc_split_kernel}) {
+    for (auto* fn : {tc_kernel<false>, tc_kernel<true>}) {
       const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
       if (err != cudaSuccess) return err;
     }
     configured[dev] = 1;
   }
   if (splits <= 1) {
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const unsigned grid = static_cast<unsigned>(plan.total_tiles < sms ? plan.total_tiles : sms);
-    tc_persistent_kernel<<<grid, kTcThreads, smem, stream>>>(plan);
+    tc_kernel<false><<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(plan);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
@@ -389,7 +795,7 @@ cudaError_t launch_tc(const TcPlan& plan, int splits, size_t smem, cudaStream_t 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, tc_split_kernel, plan);
+  return cudaLaunchKernelEx(&cfg, tc_kernel<true>, plan);
 }
 
 }  // namespace pck

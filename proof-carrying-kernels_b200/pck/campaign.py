@@ -19,6 +19,14 @@ LLM-like outlier activations in turn):
 
     python -m pck.campaign [--inputs N] [--batch B] [--checks K] [--seed S]
 
+With ``--kernel tc`` the honest outputs come from the tensor-core GEMV (`gemv_tc`, decode
+batches of up to 256 columns), whose summation order is the tensor core's: its checker
+takes the declared height `tc_height(n)`, which rests on a hypothesis about the MMA's
+internal rounding (at most 8 unit roundoffs per step). The campaign then counts false alarms
+of the checks fused into the GEMV call, reports the largest |rho| / tau and the largest
+observed error as a fraction of the declared bound gamma_h sum |w||x| (binary64 reference),
+and plants bf16-rounded outputs and bit flips on the tensor-core outputs.
+
 Prints one JSON object with the counts.
 """
 
@@ -30,8 +38,8 @@ import time
 
 import torch
 
-from pck.cuda import GpuBlockedChecker, gemv_coalesced, gemv_naive
-from pck.fp import tree_height
+from pck.cuda import GpuBlockedChecker, gemv_coalesced, gemv_naive, gemv_tc, tc_height
+from pck.fp import U32, gamma, tree_height
 
 N = 4096
 THREADS = 256
@@ -165,15 +173,79 @@ def run(inputs: int, batch: int, checks: int, block: int, seed: int, device: tor
     }  # fmt: skip
 
 
+def run_tc(inputs: int, batch: int, checks: int, block: int, seed: int, device: torch.device,
+           bound_every: int = 8) -> dict:  # fmt: skip
+    """The campaign on the tensor-core GEMV: honest batches checked by the call's own fused
+    check (the production path), every ``bound_every``-th batch also measured against the
+    declared bound in binary64, and the output faults planted on its outputs."""
+    gen = torch.Generator().manual_seed(seed)
+    W = (torch.randn(N, N, generator=gen) * 0.02).bfloat16().to(device)
+    height = tc_height(N)
+    checker = GpuBlockedChecker(W, block, height, checks=checks, generator=gen)
+    W64 = W.double()
+    g = gamma(height, U32)
+    alarms = block_checks = 0
+    worst_ratio = worst_bound = 0.0
+    per_dist = {d: {"block_checks": 0, "false_alarms": 0, "max_rho_over_tau": 0.0} for d in DISTS}
+    tallies = {k: Tally() for k in ("bf16_output", "bit_flips")}
+    flips = torch.Generator().manual_seed(seed + 1)
+    start = time.perf_counter()
+    done = calls = 0
+    while done < inputs:
+        b = min(batch, inputs - done)
+        dist = DISTS[calls % len(DISTS)]
+        X = activations(dist, b, N, gen).to(device)
+        Y, res = gemv_tc(W, X, checker)
+        fa = int((~res.passed).sum())
+        ratio = float((res.rho.abs() / res.tau).max())
+        alarms += fa
+        block_checks += res.passed.numel()
+        worst_ratio = max(worst_ratio, ratio)
+        d = per_dist[dist]
+        d["block_checks"] += res.passed.numel()
+        d["false_alarms"] += fa
+        d["max_rho_over_tau"] = max(d["max_rho_over_tau"], ratio)
+        if calls % bound_every == 0:
+            X64 = X.double()
+            err = (Y.double() - X64 @ W64.T).abs()
+            mag = X64.abs() @ W64.abs().T
+            worst_bound = max(worst_bound, float((err / (g * mag).clamp(min=1e-300)).max()))
+            # planted output faults, checked by the standalone check (16 columns a call)
+            bad_r = _bf16(Y)
+            bad_f = flip_bits(Y, 1e-4, flips)
+            for b0 in range(0, b, 16):
+                b1 = min(b, b0 + 16)
+                Xs = X[b0:b1].contiguous()
+                tau = res.tau[b0:b1]
+                for name, bad in (("bf16_output", bad_r), ("bit_flips", bad_f)):
+                    v = checker.check(Xs, bad[b0:b1].contiguous()).verdict
+                    tallies[name].add(Y[b0:b1], bad[b0:b1], v, tau, block)
+        done += b
+        calls += 1
+    torch.cuda.synchronize()
+    return {
+        "config": {"kernel": "tcgen05 gemv_tc (fused check)", "W": [N, N], "inputs": inputs, "batch": batch,
+                   "checks": checks, "block": block, "seed": seed, "height": height, "distributions": list(DISTS)},
+        "honest": {"block_checks": block_checks, "false_alarms": alarms, "max_rho_over_tau": worst_ratio,
+                   "max_error_over_declared_bound": worst_bound, "bound_sampled_every": bound_every,
+                   "per_distribution": per_dist},
+        "planted": {k: t.as_dict() for k, t in tallies.items()},
+        "seconds": round(time.perf_counter() - start, 1),
+    }  # fmt: skip
+
+
 def main() -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--kernel", choices=["tree", "tc"], default="tree",
+                   help="tree: the bit-exact coalesced and naive trees; tc: the tensor-core GEMV")
     p.add_argument("--inputs", type=int, default=100_000)
     p.add_argument("--batch", type=int, default=16)
     p.add_argument("--checks", type=int, default=8)
     p.add_argument("--block", type=int, default=128)
     p.add_argument("--seed", type=int, default=0)
     a = p.parse_args()
-    print(json.dumps(run(a.inputs, a.batch, a.checks, a.block, a.seed, torch.device("cuda", 0))), flush=True)
+    fn = run_tc if a.kernel == "tc" else run
+    print(json.dumps(fn(a.inputs, a.batch, a.checks, a.block, a.seed, torch.device("cuda", 0))), flush=True)
 
 
 if __name__ == "__main__":

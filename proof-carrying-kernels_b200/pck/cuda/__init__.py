@@ -1,5 +1,6 @@
 """GPU entry points (the drop-in for the reference's `pck.cuda`, src/pck/cuda/__init__.py)."""
 
+from pck.cuda import ops
 from pck.cuda._lib import device_status
 from pck.cuda.checker import (
     DEFAULT_BLOCK,
@@ -39,6 +40,7 @@ __all__ = [
     "gemv_fp8",
     "gemv_naive",
     "gemv_tc",
+    "ops",
     "quantize_fp8",
     "round_up_bf16",
     "tc_height",

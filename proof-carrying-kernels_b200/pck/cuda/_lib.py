@@ -54,6 +54,7 @@ class GemvJob(ctypes.Structure):
 _SIGNATURES = {
     "pck_last_error": ([], ctypes.c_char_p),
     "pck_abi_version": ([], _int),
+    "pck_source_digest": ([], ctypes.c_char_p),
     "pck_device_status": ([ctypes.POINTER(ctypes.c_uint), _int], _int),
     "pck_gemv_naive": ([_p, _p, _p, _i64, _i64, _int, _p], _int),
     "pck_gemv_coalesced": ([_p, _p, _p, _i64, _i64, _int, _p], _int),
@@ -66,6 +67,8 @@ _SIGNATURES = {
     "pck_gemv_partials": ([ctypes.POINTER(GemvJob), _int, _p], _int),
     "pck_check_verdicts": ([ctypes.POINTER(CheckDesc), _int, _p], _int),
     "pck_gemv_pipelined": ([ctypes.POINTER(GemvJob), _int, ctypes.POINTER(CheckDesc), _int, _p], _int),
+    "pck_gemv_pipelined_next": ([ctypes.POINTER(GemvJob), _int, ctypes.POINTER(CheckDesc), _int,
+                                 ctypes.POINTER(GemvJob), _int, _p], _int),
     "pck_sampling_check": ([_p, _p, _p, _i64, _i64, _i64, _i64, _int, _f64, _f64, _f64, _i64, _p, _p, _p, _p,
                             _p, _p], _int),
     "pck_member_check": ([_p, _int, _i64, _i64, _i64, _p, _p, _p, _p, _f64, _p, _p, _p, _p], _int),

@@ -29,6 +29,7 @@ from dataclasses import dataclass
 
 import torch
 
+import pck.cuda.ops  # noqa: F401  (registers torch.ops.pck)
 from pck.cuda import _lib
 from pck.cuda._ext import MAX_BATCH, extension
 from pck.fp import U32, U64, ceil_div, gamma, next_up, sum_up_factor
@@ -95,10 +96,7 @@ class GpuBlockedChecker:
 
         bits = torch.randint(0, 2, (checks, self.num_blocks, block), generator=generator)
         self.r = (2 * bits - 1).to(torch.int8).to(W.device)
-        self.c = torch.empty((checks, self.num_blocks, n), dtype=torch.float32, device=W.device)
-        self.a = torch.empty((self.num_blocks, n), dtype=torch.bfloat16, device=W.device)
-        extension().bank_build(W.contiguous(), self.r, self.c, self.a, block, checks,
-                               sum_up_factor(block))  # fmt: skip
+        self.c, self.a = torch.ops.pck.bank_build(W.contiguous(), self.r, block, checks, sum_up_factor(block))
         if not bool(torch.isfinite(self.a).all()):
             raise ValueError("sum of |W| over a block overflows BF16")
 

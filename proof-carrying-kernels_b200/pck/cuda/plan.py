@@ -99,6 +99,7 @@ class GemvLaunch:
             job.weight_format |= _lib.PCK_WEIGHTS_SETTLED
         self.prior: list[GemvLaunch] = []
         self._prior = None
+        self.next: GemvLaunch | None = None
         self.set_prior(prior)
 
     def set_prior(self, launches: Sequence[GemvLaunch]) -> None:
@@ -116,6 +117,14 @@ class GemvLaunch:
         self.prior = list(launches)  # keeps the checks' tensors alive
         self._prior = (_lib.CheckDesc * len(descs))(*descs) if descs else None
 
+    def set_next(self, launch: GemvLaunch | None) -> None:
+        """Name the launch that follows this one on the stream (``verdicts=False`` launches):
+        this launch's CTAs then prefetch its first weight pieces into L2 as they finish
+        (`pck_gemv_pipelined_next`). The results do not change."""
+        if launch is not None and (self.verdicts or launch.device != self.device):
+            raise ValueError("a next launch needs verdicts=False and the same device")
+        self.next = launch
+
     def launch(self) -> None:
         """Issue the launch on the current stream (with ``verdicts=False``, the GEMVs and the
         checks' partial sums only; a VerdictLaunch, or a later launch given this one as
@@ -124,6 +133,10 @@ class GemvLaunch:
             stream = stream_handle(self.device)
             if self.verdicts:
                 rc = self.lib.pck_gemv_checked(self._jobs, self.count, stream)
+            elif self.next is not None:
+                nprior = len(self._prior) if self._prior is not None else 0
+                rc = self.lib.pck_gemv_pipelined_next(self._jobs, self.count, self._prior, nprior, self.next._jobs,
+                                                      self.next.count, stream)  # fmt: skip
             elif self._prior is not None:
                 rc = self.lib.pck_gemv_pipelined(self._jobs, self.count, self._prior, len(self._prior), stream)
             else:
@@ -181,9 +194,10 @@ LLAMA3_8B_GROUPS: list[list[tuple[str, int, int]]] = [
 
 
 class TcLaunch:
-    """One call of the tensor-core GEMV (`pck_gemv_tc`) for up to 8 bfloat16 matrices that
-    share a batch of activations, each optionally checked (a GpuBlockedChecker built with
-    ``height=tc_height(n)``): Y_i (B, m_i) = X_i (B, n_i) W_i^T. Reusable launch after launch
+    """One call of the tensor-core GEMV (`pck_gemv_tc`) for up to 8 matrices (all bfloat16 or
+    all E4M3) that share a batch of activations, each optionally checked (a GpuBlockedChecker
+    of W, widened to bfloat16 for E4M3, built with ``height=tc_height(n)``):
+    Y_i (B, m_i) = X_i (B, n_i) W_i^T. Reusable launch after launch
     (e.g. captured in a CUDA graph); outputs in ``ys``, check results in ``results``."""
 
     def __init__(self, items: Sequence[tuple[torch.Tensor, torch.Tensor, GpuBlockedChecker | None]],
@@ -203,9 +217,13 @@ class TcLaunch:
         self.ys: list[torch.Tensor] = []
         self.results: list[CheckResult | None] = []
         batch = items[0][1].size(0)
+        wtype = items[0][0].dtype
+        if wtype not in (torch.bfloat16, torch.float8_e4m3fn):
+            raise RuntimeError("W must be bfloat16 or Float8_e4m3fn")
+        fmt = _lib.PCK_WEIGHTS_E4M3 if wtype == torch.float8_e4m3fn else _lib.PCK_WEIGHTS_BF16
         for g, (W, X, ch) in enumerate(items):
-            if W.dtype != torch.bfloat16 or X.dtype != torch.bfloat16 or X.dim() != 2 or X.size(0) != batch:
-                raise RuntimeError("W and X must be bfloat16, X (B, n) with one B for the launch")
+            if W.dtype != wtype or X.dtype != torch.bfloat16 or X.dim() != 2 or X.size(0) != batch:
+                raise RuntimeError("W must share one format, X be bfloat16 (B, n) with one B for the launch")
             if not (W.is_contiguous() and X.is_contiguous()) or X.size(1) != W.size(1):
                 raise RuntimeError("expected contiguous W (m, n) and X (B, n)")
             shape = (batch, W.size(0))
@@ -216,7 +234,7 @@ class TcLaunch:
             job = self._jobs[g]
             job.W, job.X, job.Y = W.data_ptr(), X.data_ptr(), y.data_ptr()
             job.m, job.n, job.batch, job.threads = W.size(0), W.size(1), batch, 256
-            job.weight_format = _lib.PCK_WEIGHTS_BF16
+            job.weight_format = fmt
             if ch is None:
                 job.check = None
                 self.results.append(None)

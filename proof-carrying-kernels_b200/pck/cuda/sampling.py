@@ -79,7 +79,7 @@ def check_topk_gpu(logits: torch.Tensor, selected: torch.Tensor, k: int, segment
     """Check that each row of ``selected`` (B, k) is a valid top-k set of ``logits`` (B, V)."""
     segs = default_segments(logits) if segments is None else segments
     lengths = torch.full((selected.shape[0],), selected.shape[1], dtype=torch.int64, device=selected.device)
-    return _run(logits, selected, lengths, k, False, 1.0, 1.0, 0.0, segs)
+    return SamplingCheck(*torch.ops.pck.sampling_check(logits, selected, lengths, k, False, 1.0, 1.0, 0.0, segs))
 
 
 def check_topp_gpu(logits: torch.Tensor, selected: torch.Tensor, lengths: torch.Tensor, p: float,
@@ -101,7 +101,7 @@ def check_topp_gpu(logits: torch.Tensor, selected: torch.Tensor, lengths: torch.
     vocab = logits.shape[1]
     own = 16 * U32 + math.ldexp(vocab, -146) + gamma(vocab + 3 * segs + 16, U64)
     slack = math.nextafter(tol + own, math.inf)
-    return _run(logits, selected, lengths, 0, True, p, temperature, slack, segs)
+    return SamplingCheck(*torch.ops.pck.sampling_check(logits, selected, lengths, 0, True, p, temperature, slack, segs))
 
 
 def topk_sample(logits: torch.Tensor, k: int, generator: torch.Generator | None = None

@@ -43,8 +43,7 @@ def check_members(logits: torch.Tensor, tokens, top_k=None, top_p=None, greedy=N
     ``top_k`` ints (V = no top-k), ``top_p`` floats (1 = none) and ``greedy`` bools.
     ``top_k_host`` is accepted for the reference's signature; the kernel never needs it
     (nothing here synchronizes the device)."""
-    from pck.cuda import _lib
-    from pck.cuda._ext import on_device, stream_handle
+    import pck.cuda.ops  # noqa: F401  (registers torch.ops.pck)
 
     del top_k_host
     if not isinstance(logits, torch.Tensor) or not logits.is_cuda:
@@ -61,17 +60,6 @@ def check_members(logits: torch.Tensor, tokens, top_k=None, top_p=None, greedy=N
     tk = None if top_k is None else _per_row(top_k, rows, torch.int64, dev, "top_k")
     tp = None if top_p is None else _per_row(top_p, rows, torch.float64, dev, "top_p")
     gr = None if greedy is None else _per_row(greedy, rows, torch.bool, dev, "greedy")
-    ok = torch.empty(rows, dtype=torch.bool, device=dev)
-    above = torch.empty(rows, dtype=torch.int64, device=dev)
-    mass = torch.empty(rows, dtype=torch.float64, device=dev)
     slack = next_up(tol + member_eps32(vocab))
-
-    def ptr(t):
-        return None if t is None else t.data_ptr()
-
-    with on_device(dev):
-        rc = _lib.library().pck_member_check(
-            logits.data_ptr(), _DTYPES[logits.dtype], rows, vocab, logits.stride(0), tok.data_ptr(), ptr(tk),
-            ptr(tp), ptr(gr), slack, ok.data_ptr(), above.data_ptr(), mass.data_ptr(), stream_handle(dev))
-    _lib.check(rc, "membership kernel")
+    ok, above, mass = torch.ops.pck.member_check(logits, tok, tk, tp, gr, slack)
     return {"ok": ok, "above": above, "mass_above": mass}

@@ -167,3 +167,40 @@ def test_no_bounded_wait_gave_up() -> None:
     from pck.cuda import device_status
 
     assert device_status(clear=True) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")
+@pytest.mark.parametrize("fmt", ["bf16", "e4m3"])
+def test_chained_launches_with_next_prefetch_give_the_same_bits(fmt: str) -> None:
+    """Launches chained with set_next (pck_gemv_pipelined_next: the CTAs prefetch the next
+    launch's first weight pieces into L2) give the bits of the unchained calls, and the checks
+    decided by the following launch pass."""
+    from pck.cuda import GpuBlockedChecker, gemv_coalesced, gemv_fp8, quantize_fp8
+    from pck.cuda.plan import GemvLaunch
+    from pck.fp import tree_height
+
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    shapes = [(3072, 4096), (1024, 4096), (2048, 14336)]
+    launches, refs = [], []
+    for i, (m, n) in enumerate(shapes):
+        W = (torch.randn(m, n, generator=gen, device="cuda") * 0.02).bfloat16()
+        x = torch.randn(n, generator=gen, device="cuda").bfloat16()
+        vec = 8
+        if fmt == "e4m3":
+            W, vec = quantize_fp8(W)[0], 16
+        ch = GpuBlockedChecker(W.to(torch.bfloat16), 128, tree_height(n, 256, vec),
+                               generator=torch.Generator().manual_seed(i))  # fmt: skip
+        launches.append(GemvLaunch([(W, x, ch)], 256, verdicts=False))
+        refs.append(gemv_fp8(W, x) if fmt == "e4m3" else gemv_coalesced(W, x))
+    for i, g in enumerate(launches):
+        g.set_prior([launches[i - 1]])
+        g.set_next(launches[(i + 1) % len(launches)])
+    for _ in range(3):
+        for g in launches:
+            g.launch()
+    launches[0].launch()  # decides the last launch's checks
+    torch.cuda.synchronize()
+    for g, ref in zip(launches, refs, strict=True):
+        assert torch.equal(g.ys[0].view(torch.int32), ref.view(torch.int32))
+        assert bool(g.results[0].passed.all())

@@ -134,3 +134,96 @@ def test_checked_call_catches_a_bank_for_other_weights() -> None:
     delta = (X.double() @ (W2.double() - W.double()).T).abs().view(64, 4, 128).amax(dim=2)
     assert bool((delta > 2 * res.tau.amax(dim=1)).all())
     assert not res.verdict.any()
+
+
+def e4m3_problem(m: int, n: int, batch: int, seed: int):
+    from pck.cuda import quantize_fp8
+
+    W, X = problem(m, n, batch, seed)
+    Q, _ = quantize_fp8(W)
+    return Q, X
+
+
+@pytest.mark.parametrize(("m", "n", "batch"), [(128, 64, 16), (1024, 4096, 128), (384, 4096, 64), (300, 1008, 50), (19200, 4096, 64),
+                                               (512, 4096, 256), (256, 14336, 16)])  # fmt: skip
+def test_e4m3_weights_within_the_declared_bound(m: int, n: int, batch: int) -> None:
+    """E4M3 weights on the tensor cores: widened exactly to bfloat16 in shared memory, so the
+    outputs are those of the bfloat16 path on Q widened, within the same declared bound."""
+    from pck.cuda import gemv_tc
+
+    Q, X = e4m3_problem(m, n, batch, seed=m + n)
+    Y = gemv_tc(Q, X)
+    Qb = Q.to(torch.bfloat16)
+    assert bound_ratio(Qb, X, Y) <= 1.0
+    assert torch.equal(Y.view(torch.int32), gemv_tc(Qb, X).view(torch.int32))
+
+
+@pytest.mark.parametrize(("m", "n", "batch", "checks", "fmt"),
+                         [(1024, 4096, 128, 1, "bf16"), (384, 1000, 50, 3, "bf16"), (4096, 4096, 64, 4, "bf16"),
+                          (512, 4096, 256, 2, "bf16"), (37888, 4096, 64, 1, "bf16"), (1024, 4096, 128, 2, "e4m3"),
+                          (640, 14336, 32, 1, "e4m3"), (2048, 4096, 8, 1, "bf16")])  # fmt: skip
+def test_fused_bank_sums_match_the_standalone_check(m: int, n: int, batch: int, checks: int, fmt: str) -> None:
+    """The checks whose bank rows the tensor-core kernel reduces itself (persistent units of
+    two tiles and split-K clusters, every batch width) decide exactly as the standalone check
+    on the same outputs: every block passes, the bits are equal, tau agrees to binary64
+    rounding and rho far inside tau."""
+    from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
+
+    if fmt == "e4m3":
+        W, X = e4m3_problem(m, n, batch, seed=m + checks)
+        Wb = W.to(torch.bfloat16)
+    else:
+        W, X = problem(m, n, batch, seed=m + checks)
+        Wb = W
+    checker = GpuBlockedChecker(Wb, 128, tc_height(n), checks=checks, generator=torch.Generator().manual_seed(4))
+    Y, res = gemv_tc(W, X, checker)
+    assert torch.equal(Y.view(torch.int32), gemv_tc(W, X).view(torch.int32))
+    assert res.verdict.all()
+    for b0 in range(0, batch, 16):
+        b1 = min(batch, b0 + 16)
+        sep = checker.check(X[b0:b1].contiguous(), Y[b0:b1].contiguous())
+        assert torch.equal(sep.passed, res.passed[b0:b1])
+        torch.testing.assert_close(res.tau[b0:b1], sep.tau, rtol=1e-12, atol=0)
+        assert float(((res.rho[b0:b1] - sep.rho).abs() / sep.tau).max()) < 1e-6
+
+
+def test_fused_check_catches_planted_weights() -> None:
+    """A bank built for other weights: the fused reduction fails every block whose output
+    moved by more than 2 tau (the guaranteed case), at every batch width."""
+    from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
+
+    W, X = problem(1024, 4096, 128, seed=78)
+    W2 = W.clone()
+    W2[9::128] += 1.0  # one row of every block: |delta y| = |sum of x|
+    checker = GpuBlockedChecker(W2, 128, tc_height(4096), checks=1, generator=torch.Generator().manual_seed(2))
+    _, res = gemv_tc(W, X, checker)
+    delta = (X.double() @ (W2.double() - W.double()).T).abs().view(128, 8, 128).amax(dim=2)
+    guaranteed = delta > 2 * res.tau.amax(dim=1)
+    assert int(guaranteed.sum()) > 900
+    assert not bool(res.verdict[guaranteed].any())
+    from pck.cuda import device_status
+
+    assert device_status() == 0
+
+
+def test_fused_bank_sums_with_zeros_and_subnormal_activations() -> None:
+    """Activations with exact zeros (both signs), bfloat16 subnormals and large values take
+    every branch of the bank warps' widening to binary64; the fused sums still decide as the
+    standalone check does."""
+    from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
+
+    W, X = problem(2048, 4096, 64, seed=91)
+    gen = torch.Generator().manual_seed(92)
+    Xc = X.cpu().float()
+    pick = torch.rand(Xc.shape, generator=gen)
+    Xc[pick < 0.10] = 0.0
+    Xc[(pick >= 0.10) & (pick < 0.12)] = -0.0
+    Xc[(pick >= 0.12) & (pick < 0.14)] = 3e-39  # subnormal in bfloat16
+    Xc[(pick >= 0.14) & (pick < 0.15)] = -1e30
+    X = Xc.bfloat16().cuda()
+    checker = GpuBlockedChecker(W, 128, tc_height(4096), checks=2, generator=torch.Generator().manual_seed(6))
+    Y, res = gemv_tc(W, X, checker)
+    for b0 in range(0, 64, 16):
+        sep = checker.check(X[b0 : b0 + 16].contiguous(), Y[b0 : b0 + 16].contiguous())
+        assert torch.equal(sep.passed, res.passed[b0 : b0 + 16])
+        torch.testing.assert_close(res.tau[b0 : b0 + 16], sep.tau, rtol=1e-12, atol=0)

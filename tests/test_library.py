@@ -46,7 +46,7 @@ def test_library_exports_every_declared_symbol(lib) -> None:
 
 
 def test_abi_version(lib) -> None:
-    assert lib.pck_abi_version() == 4
+    assert lib.pck_abi_version() == 6
 
 
 def _err(lib) -> str:
@@ -136,3 +136,17 @@ def test_build_flags_keep_the_rounding_model() -> None:
     assert "--fmad=false" in flags and "-ftz=false" in flags and "-prec-div=true" in flags
     assert not any(f in flags for f in build.FORBIDDEN_FLAGS)
     assert "arch=compute_100a,code=sm_100a" in flags
+
+
+def test_pipelined_next_rejects_a_bad_next_count(lib) -> None:
+    """pck_gemv_pipelined_next validates its `next` jobs before any device work."""
+    import ctypes
+
+    from pck.cuda import _lib
+
+    job = (_lib.GemvJob * 1)()
+    job[0].W = job[0].X = job[0].Y = 16
+    job[0].m, job[0].n, job[0].batch, job[0].threads = 128, 64, 1, 256
+    job[0].check = ctypes.POINTER(_lib.CheckDesc)()
+    rc = lib.pck_gemv_pipelined_next(job, 1, None, 0, job, -1, None)
+    assert rc == 1 and b"next jobs" in lib.pck_last_error()
