@@ -411,7 +411,7 @@ def lm_head_reading(rank: int, world: int, device, steps: int, warmup: int) -> d
     if world > 1:  # rank 0: the gathered logits against the unsharded GEMV, bit for bit
         ok = True
         if rank == 0:
-            ok = torch.equal(gemv_tc(W_all, X).view(torch.int32), head.logits.view(torch.int32))
+            ok = torch.equal(gemv_tc(W_all, X, full_k=True).view(torch.int32), head.logits.view(torch.int32))
         matches = all_ranks(ok, world)
     local_bytes = head.gemv_bytes
     total = torch.tensor([float(local_bytes)], device=device)

@@ -41,6 +41,14 @@ extern "C" {
  * preceding kernel writes W can get stale weights and false alarms.
  */
 #define PCK_WEIGHTS_SETTLED 0x100
+/*
+ * Flag OR-ed into a job's weight_format for pck_gemv_tc: every output accumulates its whole
+ * K range in one tensor-memory chain, so its value does not depend on which other rows share
+ * the launch (the row shards of one matrix, each computed by its own call, concatenate bit
+ * for bit to the unsharded result). Without it a launch of few tiles may split K over a
+ * cluster of CTAs and add the partial sums, which is faster but rounds differently.
+ */
+#define PCK_TC_FULL_K 0x200
 
 /* Message of the last failing call on this thread ("" if none). */
 const char* pck_last_error(void);
@@ -259,17 +267,20 @@ int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m,
                    int block, int checks, double sum_up_factor, void* stream);
 
 /*
- * Batched GEMV on the tensor cores (tcgen05) for decode batches of 16 to 256: Y (batch, m) =
- * X (batch, n) W^T for up to 8 jobs sharing the batch, bfloat16 W and X (16-byte aligned,
- * n a multiple of 8), binary32 outputs accumulated in tensor memory. Not bit-exact to the
- * coalesced tree: the tensor core adds 16 exact products per MMA and n/16 MMAs in sequence,
+ * Batched GEMV on the tensor cores (tcgen05) for decode batches of 1 to 256: Y (batch, m) =
+ * X (batch, n) W^T for up to 8 jobs sharing the batch and weight format; bfloat16 X, bfloat16
+ * W (n a multiple of 8) or E4M3 W (n a multiple of 16, widened exactly to bfloat16 in shared
+ * memory), W and X 16-byte aligned; binary32 outputs accumulated in tensor memory. Not
+ * bit-exact to the coalesced tree: the tensor core adds 16 exact products per MMA and n/16
+ * MMAs in sequence (or K ranges of them, added in rank order, unless PCK_TC_FULL_K is set),
  * so a checker of these outputs takes that accumulation's declared height
  * (pck.cuda.gemv.tc_height). `threads` and the exponent range are unused. A job's `check`
- * (optional; the job's own X, Y and shape, batch up to 256) is decided in the same call: a
- * launch reduces the bank rows of all checks against X on the CUDA cores in binary64 (exact
- * products, the bound rounded up), and a verdict launch follows. The reference has no counterpart;
- * its batched decode runs batch-1 GEMVs (harness/csrc/batched_gemv.cu:25-82 is a CUDA-core
- * diagnostic).
+ * (optional; the job's own X, Y and shape, batch up to 256) is decided in the same call: for
+ * 128-row blocks, at most 2 sign draws and batches up to 64 the GEMV kernel itself reduces
+ * the bank rows against the staged X tiles in binary64 (exact products, the bound rounded
+ * up); other checks take a bank launch of their own; a verdict launch follows. The reference
+ * has no counterpart; its batched decode runs batch-1 GEMVs (harness/csrc/batched_gemv.cu:25-82
+ * is a CUDA-core diagnostic).
  */
 int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream);
 

@@ -862,19 +862,22 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   if (batch < 1 || batch > pck::kTcMaxBatch) {
     return fail(PCK_ERR_ARGUMENT, "batch must be in [1, %d], got %d", pck::kTcMaxBatch, batch);
   }
-  const int wfmt = jobs[0].weight_format & ~PCK_WEIGHTS_SETTLED;
+  constexpr int kFlags = PCK_WEIGHTS_SETTLED | PCK_TC_FULL_K;
+  const int wfmt = jobs[0].weight_format & ~kFlags;
   if (wfmt != PCK_WEIGHTS_BF16 && wfmt != PCK_WEIGHTS_E4M3) {
     return fail(PCK_ERR_ARGUMENT, "unknown weight format %d", jobs[0].weight_format);
   }
   const bool e4m3 = wfmt == PCK_WEIGHTS_E4M3;
+  bool full_k = false;
   const int n_pad = (batch + 15) / 16 * 16;
   int tiles = 0, nj = 0;
   const pck_check_desc* descs[pck::kTcMaxJobs] = {};
   for (int i = 0; i < count; ++i) {
     const pck_gemv_job& jb = jobs[i];
-    if ((jb.weight_format & ~PCK_WEIGHTS_SETTLED) != wfmt) {
+    if ((jb.weight_format & ~kFlags) != wfmt) {
       return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the weight format");
     }
+    full_k = full_k || (jb.weight_format & PCK_TC_FULL_K) != 0;
     if (jb.batch != batch) return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the batch");
     if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, 256, 1)) return rc;
     if (jb.m == 0) continue;
@@ -921,17 +924,49 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   plan.n_pad = n_pad;
   plan.weights = e4m3 ? pck::kTcWeightsE4m3 : pck::kTcWeightsBf16;
 
-  // The form: with at least as many tiles as SMs, the persistent kernel (units of two tiles
-  // sharing each staged X tile); with fewer, each tile's K range split over a cluster of CTAs
-  // (up to 8, at least 4 K blocks each) so that the launch still fills the GPU.
+  // The form. Persistent: a CTA per SM over contiguous ranges of tiles, in units of two tiles
+  // sharing each staged X tile. Split: a cluster of `splits` CTAs per unit of one or two
+  // tiles, each CTA a near-equal range of the K blocks, for launches with few tiles. The
+  // choice minimises the modelled time of the busiest CTA: its shared-memory fill (W and the
+  // X tile of every stage) at a per-SM streaming rate, bounded below by the launch's weight
+  // bytes at HBM rate (rates measured on B200: about 52 GB/s per SM, 6.5 TB/s in all).
   const int sms = sm_count();
-  int64_t kmin = INT64_MAX;
-  for (int j = 0; j < nj; ++j) kmin = std::min<int64_t>(kmin, (plan.jobs[j].n + pck::kTcTileK - 1) / pck::kTcTileK);
-  int splits = 1;  // a power of two: clusters of 3, 5, ... CTAs ran far slower
-  if (tiles < sms) {
-    while (splits * 2 <= pck::kTcMaxSplits && tiles * splits * 2 <= sms && kmin / (splits * 2) >= 4) splits *= 2;
+  int64_t kmin = INT64_MAX, kmax = 0;
+  double wtotal = 0.0;
+  for (int j = 0; j < nj; ++j) {
+    const int64_t kb = (plan.jobs[j].n + pck::kTcTileK - 1) / pck::kTcTileK;
+    kmin = std::min(kmin, kb);
+    kmax = std::max(kmax, kb);
+    wtotal += static_cast<double>(plan.jobs[j].m) * static_cast<double>(plan.jobs[j].n) * (e4m3 ? 1.0 : 2.0);
   }
-  plan.unit_tiles = splits == 1 ? pck::kTcMaxUnitTiles : 1;
+  const double tile_w = pck::kTcTileM * pck::kTcTileK * (e4m3 ? 1.0 : 2.0);  // W bytes of a tile per stage
+  const double x_stage = n_pad * 128.0;
+  constexpr double kSmRate = 52e3, kHbmRate = 6.5e6;  // bytes per microsecond
+  const double floor_us = wtotal / kHbmRate;
+  int splits = 1, unit_tiles = pck::kTcMaxUnitTiles;
+  {
+    const int64_t per = (tiles + sms - 1) / sms;  // tiles of the busiest persistent CTA
+    const double fill = static_cast<double>(kmax) * (per * tile_w + ((per + 1) / 2) * x_stage);
+    double best = std::max(fill / kSmRate, floor_us);
+    // the split form's partial sums of a unit overlay the stages: 2 tiles fit up to batch 128
+    const int max_t = full_k ? 0 : n_pad <= 128 ? 2 : 1;
+    for (int t = 1; t <= max_t; ++t) {
+      int64_t units = 0;
+      for (int j = 0; j < nj; ++j) units += (plan.jobs[j].tiles + t - 1) / t;
+      for (int sp = 2; sp <= pck::kTcMaxSplits; ++sp) {
+        if (units * sp > sms || kmin < 2LL * sp) break;
+        if (units > pck::tc_max_clusters(sp)) continue;  // would not run in one wave
+        const double f = static_cast<double>((kmax + sp - 1) / sp) * (t * tile_w + x_stage);
+        const double est = std::max(f / kSmRate, floor_us) + 0.05 * sp;  // the cluster sum grows with sp
+        if (est < best) {
+          best = est;
+          splits = sp;
+          unit_tiles = t;
+        }
+      }
+    }
+  }
+  plan.unit_tiles = unit_tiles;
   plan.strided = 0;
   plan.total_units = 0;
   for (int j = 0; j < nj; ++j) {
@@ -980,7 +1015,8 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   constexpr size_t kSmemCap = 232448;
   plan.stages = static_cast<int32_t>(std::min<size_t>(8, (kSmemCap - extra) / plan.stage_bytes));
   if (plan.stages < 2) return fail(PCK_ERR_UNSUPPORTED, "a batch of %d leaves no room for two stages", batch);
-  if (splits > 1 && static_cast<size_t>(plan.stages) * plan.stage_bytes < static_cast<size_t>(pck::kTcTileM) * (n_pad + 1) * 4) {
+  if (splits > 1 && static_cast<size_t>(plan.stages) * plan.stage_bytes <
+                        static_cast<size_t>(plan.unit_tiles) * pck::kTcTileM * n_pad * 4) {
     return fail(PCK_ERR_UNSUPPORTED, "no room for the partial accumulator of a batch of %d", batch);
   }
   plan.acc_stride = (n_pad + 31) / 32 * 32;  // every epilogue read takes 32 columns
@@ -989,7 +1025,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   while (cols < plan.acc_bufs * plan.unit_tiles * plan.acc_stride) cols *= 2;
   plan.tmem_cols = cols;
   const size_t smem = extra + static_cast<size_t>(plan.stages) * plan.stage_bytes;
-  const int grid = splits == 1 ? std::min(plan.strided ? plan.total_units : tiles, sms) : tiles * splits;
+  const int grid = splits == 1 ? std::min(plan.strided ? plan.total_units : tiles, sms) : plan.total_units * splits;
   cudaError_t err = pck::launch_tc(plan, splits, grid, smem, static_cast<cudaStream_t>(stream));
   if (err != cudaSuccess) return cuda_fail("tensor-core gemv kernel", err);
 

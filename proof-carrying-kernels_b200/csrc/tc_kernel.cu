@@ -13,9 +13,10 @@
 //   persistent  a CTA per SM takes a contiguous range of the launch's tiles and walks it in
 //               units of up to two tiles of one job, which share every staged X tile (two
 //               MMAs per K step, two accumulators): X crosses L2 once per 256 rows of W;
-//   split       a tile per cluster of `splits` CTAs; CTA r accumulates the r-th range of the
-//               tile's K blocks, the partial accumulators are added in rank order through
-//               distributed shared memory (for launches with fewer tiles than SMs).
+//   split       a unit of one or two tiles per cluster of `splits` CTAs (2 to 8); CTA r
+//               accumulates the r-th of `splits` near-equal ranges of the K blocks, and the
+//               partial accumulators are added in rank order through distributed shared
+//               memory (for launches with few tiles).
 // Roles (14 warps):
 //   warp 0      one thread issues, per stage, the TMA loads of the unit's W tiles (128 rows x
 //               64 columns each; bfloat16 with 128-byte swizzle, or raw E4M3 bytes) and of the
@@ -101,6 +102,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// The address of the same shared-memory location in the CTA of rank `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
@@ -195,18 +212,21 @@ __device__ __forceinline__ WorkWalk work_start(const TcPlan& plan, bool split) {
 __device__ __forceinline__ bool work_next(const TcPlan& plan, WorkWalk& w, Work& out) {
   if (w.cur >= w.end) return false;
   if (w.split) {
+    // cluster u takes unit u (up to unit_tiles tiles of one job); its CTA of rank r takes the
+    // r-th of `splits` near-equal ranges of the K blocks
     cg::cluster_group cluster = cg::this_cluster();
     const int splits = static_cast<int>(cluster.num_blocks());
     const int rank = static_cast<int>(cluster.block_rank());
-    const int tile = static_cast<int>(blockIdx.x) / splits;
-    out.job = job_of(plan, tile);
-    const TcJob& jb = plan.jobs[out.job];
-    out.tile = tile - jb.tile_begin;
-    out.ntiles = 1;
+    const int unit = static_cast<int>(blockIdx.x) / splits;
+    int j = 0;
+    while (j + 1 < plan.njobs && unit >= plan.jobs[j + 1].unit_begin) ++j;
+    const TcJob& jb = plan.jobs[j];
+    out.job = j;
+    out.tile = (unit - jb.unit_begin) * plan.unit_tiles;
+    out.ntiles = min(plan.unit_tiles, jb.tiles - out.tile);
     const int kblocks = static_cast<int>((jb.n + kTcTileK - 1) / kTcTileK);
-    const int kper = (kblocks + splits - 1) / splits;
-    out.kb0 = min(kblocks, rank * kper);
-    out.kb1 = min(kblocks, out.kb0 + kper);
+    out.kb0 = rank * kblocks / splits;
+    out.kb1 = (rank + 1) * kblocks / splits;
     out.seg = rank;
     w.cur = 1;
     return true;
@@ -701,11 +721,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
   }
 
   if constexpr (kSplit) {
-    // The partial accumulator into shared memory (over the stages, once every stage is done
-    // with: the last stage's release covers the MMAs and the bank warps), the cluster sum in
-    // rank order, rows [rank * R, (rank + 1) * R) of the tile per CTA.
+    // The partial accumulators into shared memory (over the stages, once every stage is done
+    // with: the last stage's release covers the MMAs and the bank warps), column-major per
+    // tile, part[(t * n_pad + col) * 128 + row], so a warp's 32 rows of one column are one
+    // conflict-free line; then the cluster sum in rank order by every thread of the CTA, four
+    // rows at a time (one 16-byte load per peer), rank r taking row groups
+    // [32 r / splits, 32 (r + 1) / splits) of every column.
     float* part = reinterpret_cast<float*>(smem);
-    const int pstride = plan.n_pad + 1;  // keeps the rows of a warp in different banks
+    const int n_pad = plan.n_pad;
     if (warp >= 2 && warp < 6) {
       const int quarter = warp % 4;
       const int lrow = quarter * 32 + lane;
@@ -716,12 +739,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       }
       have = __all_sync(kFullMask, have);
       tc_fence_after();
-      for (int c0 = 0; c0 < plan.n_pad; c0 += 32) {
-        uint32_t v[32];
-        if (have) tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(c0), v);
+      for (int t = 0; t < last.ntiles; ++t) {
+        for (int c0 = 0; c0 < n_pad; c0 += 32) {
+          uint32_t v[32];
+          if (have) {
+            tmem_ld32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) +
+                          static_cast<uint32_t>(t * plan.acc_stride + c0), v);
+          }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (c0 + i < plan.n_pad) part[lrow * pstride + c0 + i] = have ? __uint_as_float(v[i]) : 0.0f;
+          for (int i = 0; i < 32; ++i) {
+            if (c0 + i < n_pad) part[(t * n_pad + c0 + i) * kTcTileM + lrow] = have ? __uint_as_float(v[i]) : 0.0f;
+          }
         }
       }
     }
@@ -729,25 +757,68 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
     tc_fence_before();
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();  // every CTA's partial is in its shared memory
-    if (warp >= 2 && warp < 6) {
+    {
+      Work unit;  // the cluster's unit, for every thread (only the epilogue warps hold `last`)
+      {
+        WorkWalk walk = work_start(plan, true);
+        work_next(plan, walk, unit);
+      }
       const int splits = static_cast<int>(cluster.num_blocks());
       const int rank = static_cast<int>(cluster.block_rank());
-      const TcJob& jb = plan.jobs[last.job];
-      const int R = kTcTileM / splits;
-      const int r0 = rank * R;
-      const int rows = rank == splits - 1 ? kTcTileM - r0 : R;
-      const int t = static_cast<int>(threadIdx.x) - 2 * kWarp;  // 0..127
-      for (int idx = t; idx < rows * plan.batch; idx += 4 * kWarp) {
-        const int r = r0 + idx % rows;
-        const int colb = idx / rows;
-        float sum = 0.0f;
-        for (int c = 0; c < splits; ++c) {
-          const float* peer = cluster.map_shared_rank(part, c);
-          const float v = peer[r * pstride + colb];
-          sum = c == 0 ? v : __fadd_rn(sum, v);
+      const TcJob& jb = plan.jobs[unit.job];
+      constexpr int kGroups = kTcTileM / 4;
+      const int g0 = rank * kGroups / splits;
+      const int ng = (rank + 1) * kGroups / splits - g0;
+      const int items = unit.ntiles * plan.batch * ng;
+      const uint32_t local = smem_addr(part);
+      uint32_t peer[kTcMaxSplits];
+#pragma unroll
+      for (int c = 0; c < kTcMaxSplits; ++c) peer[c] = c < splits ? mapa_shared(local, static_cast<uint32_t>(c)) : 0u;
+      for (int it0 = static_cast<int>(threadIdx.x); it0 < items; it0 += 2 * kTcThreads) {
+        float4 sum[2];
+        int64_t row[2];
+        int colb[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int item = it0 + h * kTcThreads;
+          row[h] = -1;
+          if (item >= items) continue;
+          const int g = g0 + item % ng;
+          const int rest = item / ng;  // t * batch + column
+          const int t = rest / plan.batch;
+          colb[h] = rest - t * plan.batch;
+          row[h] = static_cast<int64_t>(unit.tile + t) * kTcTileM + 4 * g;
+          const uint32_t off = static_cast<uint32_t>(((t * n_pad + colb[h]) * kTcTileM + 4 * g) * 4);
+          float4 v[kTcMaxSplits];
+#pragma unroll
+          for (int c = 0; c < kTcMaxSplits; ++c) {
+            if (c < splits) v[c] = ld_dsmem_f4(peer[c] + off);
+          }
+          sum[h] = v[0];
+#pragma unroll
+          for (int c = 1; c < kTcMaxSplits; ++c) {
+            if (c < splits) {
+              sum[h].x = __fadd_rn(sum[h].x, v[c].x);
+              sum[h].y = __fadd_rn(sum[h].y, v[c].y);
+              sum[h].z = __fadd_rn(sum[h].z, v[c].z);
+              sum[h].w = __fadd_rn(sum[h].w, v[c].w);
+            }
+          }
         }
-        const int64_t row = static_cast<int64_t>(last.tile) * kTcTileM + r;
-        if (row < jb.m) jb.Y[static_cast<int64_t>(colb) * jb.m + row] = sum;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (row[h] < 0) continue;
+          float* dst = jb.Y + static_cast<int64_t>(colb[h]) * jb.m + row[h];
+          if (row[h] + 3 < jb.m && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+            *reinterpret_cast<float4*>(dst) = sum[h];
+          } else {
+            const float e[4] = {sum[h].x, sum[h].y, sum[h].z, sum[h].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              if (row[h] + k < jb.m) dst[k] = e[k];
+            }
+          }
+        }
       }
     }
     cluster.sync();  // no CTA leaves while a peer may still read its partial
@@ -768,23 +839,63 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
 
 PCK_STATUS_READER(tc_status)
 
-cudaError_t launch_tc(const TcPlan& plan, int splits, int grid, size_t smem, cudaStream_t stream) {
+namespace {
+
+constexpr int kTcSmemMax = 232448;
+
+// Opts both forms into the largest dynamic shared memory, once per device.
+cudaError_t configure(int* dev_out) {
   static int configured[64] = {0};
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
     for (auto* fn : {tc_kernel<false>, tc_kernel<true>}) {
-      const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
+      const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
       if (err != cudaSuccess) return err;
     }
     configured[dev] = 1;
   }
+  *dev_out = dev;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+int tc_max_clusters(int splits) {
+  static int cache[64][kTcMaxSplits + 1] = {};
+  int dev = -1;
+  if (splits < 2 || splits > kTcMaxSplits || configure(&dev) != cudaSuccess) return 0;
+  if (cache[dev][splits] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(splits));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = kTcSmemMax;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, tc_kernel<true>, &cfg) != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = -1;  // unknown: never chosen
+    }
+    cache[dev][splits] = n;
+  }
+  return cache[dev][splits] > 0 ? cache[dev][splits] : 0;
+}
+
+cudaError_t launch_tc(const TcPlan& plan, int splits, int grid, size_t smem, cudaStream_t stream) {
+  int dev = -1;
+  if (const cudaError_t err = configure(&dev); err != cudaSuccess) return err;
   if (splits <= 1) {
     tc_kernel<false><<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(plan);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(plan.total_tiles) * static_cast<unsigned>(splits));
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));  // a cluster of `splits` CTAs per unit
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

@@ -77,9 +77,12 @@ struct alignas(64) TcPlan {
   int32_t total_units;
 };
 
-// splits == 1: the persistent kernel over `grid` CTAs; else total_tiles * splits CTAs in
-// clusters of `splits` (K ranges of one 128-row tile).
+// splits == 1: the persistent kernel over `grid` CTAs; else `grid` = total_units * splits CTAs
+// in clusters of `splits` (K ranges of one unit of unit_tiles 128-row tiles).
 cudaError_t launch_tc(const TcPlan& plan, int splits, int grid, size_t smem, cudaStream_t stream);
 cudaError_t tc_status(unsigned int* value, bool clear);
+// How many clusters of `splits` CTAs of the split form can run at once on the current device
+// (0 if unknown): a split launch of more clusters would run in waves.
+int tc_max_clusters(int splits);
 
 }  // namespace pck

@@ -16,6 +16,7 @@ PCK_OK = 0
 PCK_WEIGHTS_BF16 = 0
 PCK_WEIGHTS_E4M3 = 1
 PCK_WEIGHTS_SETTLED = 0x100  # weights written before the preceding kernel began
+PCK_TC_FULL_K = 0x200  # tensor-core GEMV: one accumulation chain over the whole K per output
 MAX_JOBS = 16  # PCK_MAX_JOBS
 MAX_BATCH = 16
 STATIC_SCRATCH_BYTES = 4 << 20  # PCK_STATIC_SCRATCH_BYTES

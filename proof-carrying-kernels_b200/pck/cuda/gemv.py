@@ -69,7 +69,7 @@ def tc_height(n: int) -> int:
     return TC_STEP_ROUNDINGS * (-(-n // 16) + 1)
 
 
-def gemv_tc(W: torch.Tensor, X: torch.Tensor, checker=None):
+def gemv_tc(W: torch.Tensor, X: torch.Tensor, checker=None, full_k: bool = False):
     """Y (B, m) = X (B, n) W^T on the tensor cores for a decode batch of 1 to 256 columns:
     bfloat16 or E4M3 W (m, n) and bfloat16 X (B, n), both contiguous and 16-byte aligned with
     n a multiple of 8 (16 for E4M3); binary32 Y. E4M3 weights are widened exactly to bfloat16
@@ -78,13 +78,17 @@ def gemv_tc(W: torch.Tensor, X: torch.Tensor, checker=None):
 
     With a ``checker`` (a GpuBlockedChecker of W, or of W widened to bfloat16 for E4M3 W,
     built with ``height=tc_height(n)``) the call also checks Y: the GEMV kernel reduces the
-    bank rows against the staged X tiles in binary64 (128-row blocks, up to 4 checks; other
-    checkers take a bank launch of their own), a verdict launch decides the blocks, and the
-    call returns (Y, CheckResult) with results of shape (B, checks, num_blocks)."""
+    bank rows against the staged X tiles in binary64 (128-row blocks, up to 2 checks, batches
+    up to 64; other checkers take a bank launch of their own), a verdict launch decides the blocks, and the
+    call returns (Y, CheckResult) with results of shape (B, checks, num_blocks).
+
+    ``full_k``: every output accumulates its whole K range in one chain, so a row's value does
+    not depend on the other rows of the call (row shards concatenate bit for bit to the
+    unsharded result); otherwise a call of few row tiles may split K over a cluster of CTAs."""
     from pck.cuda.checker import CheckResult
 
     if checker is None:
-        return torch.ops.pck.gemv_tc(W, X)
+        return torch.ops.pck.gemv_tc(W, X, full_k)
     if (checker.m, checker.n) != tuple(W.shape):
         raise ValueError("the checker was built for another shape")
     batch = X.size(0)
@@ -93,5 +97,5 @@ def gemv_tc(W: torch.Tensor, X: torch.Tensor, checker=None):
     ps = ps.view(batch, checker.num_blocks, checker.segments)
     Y, passed, rho, tau = torch.ops.pck.gemv_tc_checked(W, X, checker.c, checker.a, checker.r, pcx, ps,
                                                         float(checker.coef), float(checker.geps),
-                                                        float(checker.tau_floor))  # fmt: skip
+                                                        float(checker.tau_floor), full_k)  # fmt: skip
     return Y, CheckResult(passed, rho, tau)

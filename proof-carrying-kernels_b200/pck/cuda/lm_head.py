@@ -60,7 +60,8 @@ class CheckedLMHead:
         logits_part, verdict_part = self.exchange.parts
         self.local_logits = logits_part.local_view(0)  # (B, rows of this shard)
         self.local_passed = verdict_part.local_view(0)  # (B * checks, blocks of this shard)
-        self.gemv = TcLaunch([(W_local, X, self.checker)], ys=[self.local_logits], passed=[self.local_passed])
+        self.gemv = TcLaunch([(W_local, X, self.checker)], ys=[self.local_logits], passed=[self.local_passed],
+                             full_k=True)  # every rank's slice rounds as in the unsharded GEMV
         if world == 1:
             self.logits = self.local_logits  # (B, V)
             self.passed = self.local_passed.view(self.batch, checks, nb)

@@ -10,12 +10,12 @@ reference rejects them, rather than by a missing dispatch key).
     torch.ops.pck.gemv_naive(W, x, threads)           -> y
     torch.ops.pck.gemv_coalesced(W, x, threads)       -> y       (x (n,) or (B, n), B <= 16)
     torch.ops.pck.gemv_fp8(Q, x, threads)             -> z
-    torch.ops.pck.gemv_tc(W, X)                       -> Y       (B <= 256, bfloat16 or E4M3 W)
+    torch.ops.pck.gemv_tc(W, X, full_k=False)         -> Y       (B <= 256, bfloat16 or E4M3 W)
     torch.ops.pck.blocked_check(c, a, r, x, y, partial_cx!, partial_s!, coef, geps, tau_floor)
                                                       -> (passed, rho, tau)
     torch.ops.pck.gemv_checked(W, x, c, a, r, partial_cx!, partial_s!, coef, geps, tau_floor, threads)
                                                       -> (y, passed, rho, tau)
-    torch.ops.pck.gemv_tc_checked(W, X, c, a, r, partial_cx!, partial_s!, coef, geps, tau_floor)
+    torch.ops.pck.gemv_tc_checked(W, X, c, a, r, partial_cx!, partial_s!, coef, geps, tau_floor, full_k=False)
                                                       -> (Y, passed, rho, tau)
     torch.ops.pck.member_check(logits, tokens, top_k?, top_p?, greedy?, slack) -> (ok, above, mass_above)
     torch.ops.pck.sampling_check(logits, selected, lengths, k, top_p, p, temperature, slack, segments)
@@ -81,7 +81,7 @@ def _(Q, x, threads=256):
     return Q.new_empty((*x.shape[:-1], Q.size(0)), dtype=_FLOAT)
 
 
-def _tc_job(W: torch.Tensor, X: torch.Tensor, Y: torch.Tensor):
+def _tc_job(W: torch.Tensor, X: torch.Tensor, Y: torch.Tensor, full_k: bool = False):
     if not (W.is_cuda and X.is_cuda and W.device == X.device):
         raise RuntimeError("W and X must be CUDA tensors on one device")
     if W.dtype not in (torch.bfloat16, torch.float8_e4m3fn) or X.dtype != torch.bfloat16:
@@ -94,6 +94,8 @@ def _tc_job(W: torch.Tensor, X: torch.Tensor, Y: torch.Tensor):
     job[0].W, job[0].X, job[0].Y = W.data_ptr(), X.data_ptr(), Y.data_ptr()
     job[0].m, job[0].n, job[0].batch, job[0].threads = W.size(0), W.size(1), X.size(0), 256
     job[0].weight_format = _lib.PCK_WEIGHTS_E4M3 if W.dtype == torch.float8_e4m3fn else _lib.PCK_WEIGHTS_BF16
+    if full_k:
+        job[0].weight_format |= _lib.PCK_TC_FULL_K
     job[0].check = ctypes.POINTER(_lib.CheckDesc)()
     return job
 
@@ -107,14 +109,14 @@ def _run_tc(job, device: torch.device) -> None:
 
 
 @torch.library.custom_op("pck::gemv_tc", mutates_args=())
-def gemv_tc(W: torch.Tensor, X: torch.Tensor) -> torch.Tensor:
+def gemv_tc(W: torch.Tensor, X: torch.Tensor, full_k: bool = False) -> torch.Tensor:
     Y = torch.empty((X.size(0), W.size(0)), dtype=_FLOAT, device=W.device)
-    _run_tc(_tc_job(W, X, Y), W.device)
+    _run_tc(_tc_job(W, X, Y, full_k), W.device)
     return Y
 
 
 @gemv_tc.register_fake
-def _(W, X):
+def _(W, X, full_k=False):
     return X.new_empty((X.size(0), W.size(0)), dtype=_FLOAT)
 
 
@@ -160,9 +162,9 @@ def _(W, x, c, a, r, partial_cx, partial_s, coef, geps, tau_floor, threads=256):
 @torch.library.custom_op("pck::gemv_tc_checked", mutates_args=("partial_cx", "partial_s"))
 def gemv_tc_checked(W: torch.Tensor, X: torch.Tensor, c: torch.Tensor, a: torch.Tensor, r: torch.Tensor,
                     partial_cx: torch.Tensor, partial_s: torch.Tensor, coef: float, geps: float,
-                    tau_floor: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:  # fmt: skip
+                    tau_floor: float, full_k: bool = False) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:  # fmt: skip
     Y = torch.empty((X.size(0), W.size(0)), dtype=_FLOAT, device=W.device)
-    job = _tc_job(W, X, Y)
+    job = _tc_job(W, X, Y, full_k)
     desc = _lib.CheckDesc()
     batch = X.size(0)
     shape = (batch, c.size(0), c.size(1))
@@ -183,7 +185,7 @@ def gemv_tc_checked(W: torch.Tensor, X: torch.Tensor, c: torch.Tensor, a: torch.
 
 
 @gemv_tc_checked.register_fake
-def _(W, X, c, a, r, partial_cx, partial_s, coef, geps, tau_floor):
+def _(W, X, c, a, r, partial_cx, partial_s, coef, geps, tau_floor, full_k=False):
     shape = (X.size(0), c.size(0), c.size(1))
     return (X.new_empty((X.size(0), W.size(0)), dtype=_FLOAT), X.new_empty(shape, dtype=torch.bool),
             X.new_empty(shape, dtype=torch.float64), X.new_empty(shape, dtype=torch.float64))  # fmt: skip

@@ -202,10 +202,12 @@ class TcLaunch:
 
     def __init__(self, items: Sequence[tuple[torch.Tensor, torch.Tensor, GpuBlockedChecker | None]],
                  ys: Sequence[torch.Tensor] | None = None,
-                 passed: Sequence[torch.Tensor | None] | None = None) -> None:  # fmt: skip
+                 passed: Sequence[torch.Tensor | None] | None = None, full_k: bool = False) -> None:  # fmt: skip
         """``ys`` / ``passed`` may give preallocated outputs (e.g. views into the packed
         buffer of a row-sharded exchange): y (B, m) float32 and the verdict bits as a
-        contiguous bool tensor of B * checks * num_blocks elements."""
+        contiguous bool tensor of B * checks * num_blocks elements. ``full_k``: one
+        accumulation chain over the whole K per output (`PCK_TC_FULL_K`), so row shards
+        concatenate bit for bit to the unsharded result."""
         if not 1 <= len(items) <= 8:
             raise ValueError(f"a tensor-core launch holds 1 to 8 GEMVs, got {len(items)}")
         self.device = items[0][0].device
@@ -234,7 +236,7 @@ class TcLaunch:
             job = self._jobs[g]
             job.W, job.X, job.Y = W.data_ptr(), X.data_ptr(), y.data_ptr()
             job.m, job.n, job.batch, job.threads = W.size(0), W.size(1), batch, 256
-            job.weight_format = fmt
+            job.weight_format = fmt | (_lib.PCK_TC_FULL_K if full_k else 0)
             if ch is None:
                 job.check = None
                 self.results.append(None)

@@ -96,8 +96,9 @@ def test_sampled_tokens_membership_matches_oracle_and_catches_planted(head) -> N
 
 def test_sharded_rows_reassemble_bitwise_on_one_gpu(head) -> None:
     """The logits of the row shards of two, four and eight ranks, each computed on its own
-    (what every rank computes), concatenate to the unsharded logits bit for bit: the
-    tensor-core kernel's order does not depend on the shard (whole tiles, full K per tile)."""
+    (what every rank computes), concatenate to the unsharded logits bit for bit: with
+    full_k the tensor-core kernel's order does not depend on the shard (whole tiles, full K
+    per tile)."""
     from pck.cuda import gemv_tc
     from pck.cuda.sharded import shard_rows
 
@@ -105,7 +106,7 @@ def test_sharded_rows_reassemble_bitwise_on_one_gpu(head) -> None:
         parts = []
         for rank in range(world):
             sh = shard_rows(VOCAB, 128, world, rank)
-            parts.append(gemv_tc(head.W[sh.row0 : sh.row1].contiguous(), head.X))
+            parts.append(gemv_tc(head.W[sh.row0 : sh.row1].contiguous(), head.X, full_k=True))
         full = torch.cat(parts, dim=-1)
         torch.cuda.synchronize()
         assert torch.equal(full.view(torch.int32), head.logits.view(torch.int32)), f"world {world}"
