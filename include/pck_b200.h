@@ -145,6 +145,8 @@ typedef struct pck_check_desc {
   double coef;          /* >= gamma_h + u32, rounded up                                   */
   double geps;          /* >= the checker's own rounding constant, rounded up             */
   double tau_floor;     /* >= n 2^-148, rounded up                                        */
+  const double* c64;    /* optional: c widened to binary64, same shape (or NULL); the
+                           tensor-core GEMV's fused reduction then reads it instead of c    */
 } pck_check_desc;
 
 #define PCK_MAX_JOBS 16

@@ -983,6 +983,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   // Others take the wide-batch bank kernel.
   const int segs_fused = splits;
   int max_checks = 0;
+  bool any_c64 = false;
   for (int j = 0; j < nj; ++j) {
     const pck_check_desc* d = descs[j];
     pck::TcJob& tj = plan.jobs[j];
@@ -991,6 +992,8 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
         aligned16(d->c) && aligned16(d->a)) {
       tj.fused = 1;
       tj.c = d->c;
+      tj.c64 = d->c64 && aligned16(d->c64) ? d->c64 : nullptr;
+      any_c64 = any_c64 || tj.c64 != nullptr;
       tj.a = static_cast<const uint16_t*>(d->a);
       tj.partial_cx = d->partial_cx;
       tj.partial_s = d->partial_s;
@@ -1005,7 +1008,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
 
   plan.w_bytes = plan.unit_tiles * pck::kTcTileM * 128;
   plan.x_bytes = n_pad * 128;
-  plan.tile_bank_bytes = plan.any_fused ? max_checks * 256 + 128 : 0;
+  plan.tile_bank_bytes = plan.any_fused ? max_checks * (any_c64 ? 512 : 256) + 128 : 0;
   plan.bank_bytes = (plan.unit_tiles * plan.tile_bank_bytes + 1023) / 1024 * 1024;
   plan.raw_bytes = e4m3 ? plan.unit_tiles * pck::kTcTileM * 64 : 0;
   plan.stage_bytes = (plan.w_bytes + plan.x_bytes + plan.bank_bytes + plan.raw_bytes + 1023) / 1024 * 1024;

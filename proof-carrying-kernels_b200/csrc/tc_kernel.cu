@@ -26,10 +26,11 @@
 //   warps 2..5  copy the accumulators out of tensor memory (warp w reads lanes 32 (w % 4) ...)
 //               into Y (persistent) or into shared memory for the cluster sum (split);
 //   warps 6..13 the bank warps: widen E4M3 tiles to bfloat16 for the MMA, and for fused checks
-//               reduce the stage's bank rows against the stage's X tile in binary64 — c . x
-//               rounded to nearest, a . |x| rounded up, exact products (binary32 x bfloat16
-//               and bfloat16 x bfloat16 fit in 53 bits) — into the checks' partial sums: one
-//               segment per tile (persistent) or per K range (split).
+//               reduce the stage's bank rows against the stage's X tile — c . x in binary64
+//               rounded to nearest (binary32 x bfloat16 products are exact in binary64),
+//               a . |x| in binary32 rounded up (bfloat16 x bfloat16 products are exact in
+//               binary32) — into the checks' partial sums: one segment per tile (persistent)
+//               or per K range (split).
 // A stage is released to the producer once the MMAs have read it (tcgen05.commit) and every
 // bank warp is done with it. Every mbarrier wait is bounded; a wait that gives up records the
 // status bit and the roles stop issuing work.
@@ -185,6 +186,19 @@ struct Work {
   int seg;
 };
 
+// A role's position in the stage ring: slot and the parity of its current pass, stepped
+// without divisions (the stage count is a launch parameter).
+struct Ring {
+  int slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int stages) {
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
 // The work sequence of a CTA; every role walks the same one.
 struct WorkWalk {
   int cur;
@@ -315,15 +329,18 @@ __device__ __forceinline__ void widen_stage(const TcPlan& plan, int ntiles, uint
   fence_proxy_async();
 }
 
-// Running sums of a bank thread over a work item, per column: c . x per (tile, check) rounded
-// to nearest, a . |x| per tile rounded up, each as kPartials interleaved partial sums (column j
-// to partial j % kPartials), added in order at the end. Binary64 FMAs take about 100 cycles
-// on this GPU, so a warp needs many independent chains; the binary64 bound holds for any split
-// of a sum.
+// Running sums of a bank thread over a work item, per column: c . x per (tile, check) in
+// binary64 rounded to nearest, a . |x| per tile in binary32 rounded up, each as kPartials
+// interleaved partial sums (column j to partial j % kPartials), added in order at the end.
+// The bound sum needs no binary64: a (bfloat16) times |x| (bfloat16) is exact in binary32,
+// and a sum of non-negative terms rounded up at every step is never below the exact sum, so
+// it is an upper bound as the verdict rule requires (inflated by at most a relative
+// (1 + 2^-23)^h - 1 for a chain of h additions; an overflow gives +inf and fails the block).
+// Both bounds hold for any split of a sum.
 constexpr int kPartials = 2;
 struct BankSums {
   double cx[2][kTcMaxUnitTiles][kTcMaxChecks][kPartials];
-  double sx[2][kTcMaxUnitTiles][kPartials];
+  float sx[2][kTcMaxUnitTiles][kPartials];
 };
 
 __device__ __forceinline__ void bank_zero(BankSums& a) {
@@ -333,7 +350,7 @@ __device__ __forceinline__ void bank_zero(BankSums& a) {
     for (int t = 0; t < kTcMaxUnitTiles; ++t) {
 #pragma unroll
       for (int p = 0; p < kPartials; ++p) {
-        a.sx[c][t][p] = 0.0;
+        a.sx[c][t][p] = 0.0f;
 #pragma unroll
         for (int k = 0; k < kTcMaxChecks; ++k) a.cx[c][t][k][p] = 0.0;
       }
@@ -341,49 +358,75 @@ __device__ __forceinline__ void bank_zero(BankSums& a) {
   }
 }
 
-// One stage of the fused check for one bank warp. The warp widens to binary64 the bank values
-// its chunks need (rows c[k] and a of each tile of the unit, zeros past the end of the row)
-// into its own staging buffer at shared address `wstg` ([tile][row][32 columns j]), then each
-// thread, chunk by chunk: its columns' 8 activations widened, and per tile and bank row 4
-// two-value shared loads serving 8 FMAs per column. Only the warp synchronizes; every access
-// names the shared space.
-__device__ __forceinline__ void bank_stage(const TcPlan& plan, const TcJob& jb, int ntiles, int kb,
-                                           const uint8_t* stage, uint32_t wstg, const BankLanes& L, int lane,
-                                           BankSums& acc) {
-  const int K = jb.checks;
-  const int jmax = static_cast<int>(min(static_cast<int64_t>(kTcTileK), jb.n - static_cast<int64_t>(kb) * kTcTileK));
-  const uint32_t bank = smem_addr(stage + plan.w_bytes + plan.x_bytes);
+// What the bank warps need of a work item, read from the launch parameters once per item.
+struct BankItem {
+  int fused;
+  int checks;
+  int ntiles;
+  int c64;           // binary64 checksums staged by the producer: no widening
+  int cstride;       // bytes per checksum row of a stage's bank region
+  int tile_bytes;    // bank bytes per tile of a stage
+  int last_kb;       // the row's last K block, and its columns (a multiple of 8)
+  int last_cols;
+  uint32_t x_off;    // the X tile and the bank region within a stage
+  uint32_t bank_off;
+};
+
+__device__ __forceinline__ BankItem bank_item(const TcPlan& plan, const TcJob& jb, const Work& wk) {
+  BankItem it;
+  it.fused = jb.fused;
+  it.checks = jb.checks;
+  it.ntiles = wk.ntiles;
+  it.c64 = jb.c64 != nullptr;
+  it.cstride = it.c64 ? 512 : 256;
+  it.tile_bytes = plan.tile_bank_bytes;
+  it.last_kb = static_cast<int>((jb.n - 1) / kTcTileK);
+  it.last_cols = static_cast<int>(jb.n - static_cast<int64_t>(it.last_kb) * kTcTileK);
+  it.x_off = static_cast<uint32_t>(plan.w_bytes);
+  it.bank_off = static_cast<uint32_t>(plan.w_bytes + plan.x_bytes);
+  return it;
+}
+
+// One stage of the fused check for one bank warp (`jmax` columns of the stage are valid).
+// Without binary64 checksums in the stage, the warp widens to binary64 the checksum values its
+// chunks need (rows c[k] of each tile of the unit, zeros past the end of the row) into its own
+// staging buffer at shared address `wstg` ([tile][check][32 columns j]). Then each thread,
+// chunk by chunk: its columns' 8 activations (binary64 for c . x, binary32 |x| for the bound),
+// and per tile 4 two-value shared loads per check serving 8 binary64 FMAs per column, and one
+// 16-byte load of 8 bound values serving 8 binary32 FMAs per column. Only the warp
+// synchronizes; every access names the shared space.
+__device__ __forceinline__ void bank_stage(const BankItem& item, int jmax, const uint8_t* stage, uint32_t wstg,
+                                           const BankLanes& L, int lane, BankSums& acc) {
+  const int K = item.checks;
+  const int ntiles = item.ntiles;
+  const uint32_t bank = smem_addr(stage) + item.bank_off;
   const int j0 = L.ch0 * 8, jn = (L.ch1 - L.ch0) * 8;  // at most 32 columns j
+  const bool c64 = item.c64 != 0;
+  const int cstride = item.cstride;
   __syncwarp();  // the previous stage's reads of the buffer are done
-  if (lane < jn) {  // lane jj widens column j0 + jj of every bank row of the unit
+  if (!c64 && lane < jn) {  // lane jj widens column j0 + jj of every checksum row of the unit
     const int j = j0 + lane;
 #pragma unroll
     for (int t = 0; t < kTcMaxUnitTiles; ++t) {
       if (t >= ntiles) break;
-      const uint32_t tb = bank + static_cast<uint32_t>(t * plan.tile_bank_bytes);
-      const uint32_t dst = wstg + static_cast<uint32_t>((t * (kTcMaxChecks + 1) * 32 + lane) * 8);
+      const uint32_t tb = bank + static_cast<uint32_t>(t * item.tile_bytes);
+      const uint32_t dst = wstg + static_cast<uint32_t>((t * kTcMaxChecks * 32 + lane) * 8);
 #pragma unroll
-      for (int r = 0; r <= kTcMaxChecks; ++r) {
-        if (r > K) break;
-        double v = 0.0;
-        if (j < jmax) {
-          if (r < K) {
-            v = static_cast<double>(__uint_as_float(lds32(tb + static_cast<uint32_t>(r * 256 + j * 4))));
-          } else {
-            const uint32_t w = lds32(tb + static_cast<uint32_t>(K * 256 + (j & ~1) * 2));
-            v = static_cast<double>((j & 1) ? bf16_hi(w) : bf16_lo(w));
-          }
-        }
+      for (int r = 0; r < kTcMaxChecks; ++r) {
+        if (r >= K) break;
+        const double v = j < jmax ? static_cast<double>(__uint_as_float(lds32(tb + static_cast<uint32_t>(r * 256 + j * 4))))
+                                  : 0.0;
         sts_f64(dst + static_cast<uint32_t>(r * 32 * 8), v);
       }
     }
   }
   __syncwarp();
   if (L.col[0] < 0) return;
-  const uint32_t xs = smem_addr(stage + plan.w_bytes);
+  const uint32_t xs = smem_addr(stage) + item.x_off;
   const bool two = L.col[1] >= 0;
   for (int ch = L.ch0; ch < L.ch1 && ch * 8 < jmax; ++ch) {  // jmax is a multiple of 8
-    double xv[2][8], ax[2][8];
+    double xv[2][8];
+    float ax[2][8];
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const int b = (c == 0 || two) ? L.col[c] : L.col[0];
@@ -391,32 +434,44 @@ __device__ __forceinline__ void bank_stage(const TcPlan& plan, const TcJob& jb, 
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
       for (int h = 0; h < 8; ++h) {
-        xv[c][h] = static_cast<double>((h & 1) ? bf16_hi(w[h >> 1]) : bf16_lo(w[h >> 1]));
-        ax[c][h] = fabs(xv[c][h]);
+        const float f = (h & 1) ? bf16_hi(w[h >> 1]) : bf16_lo(w[h >> 1]);
+        xv[c][h] = static_cast<double>(f);
+        ax[c][h] = fabsf(f);
       }
     }
 #pragma unroll
     for (int t = 0; t < kTcMaxUnitTiles; ++t) {
       if (t >= ntiles) break;
-      const uint32_t row0 = wstg + static_cast<uint32_t>((t * (kTcMaxChecks + 1) * 32 + (ch - L.ch0) * 8) * 8);
+      // binary64 checksums of this chunk: in the stage itself (row stride 512 bytes) or in the
+      // warp's widened copy (row stride 32 values)
+      const uint32_t row0 = c64 ? bank + static_cast<uint32_t>(t * item.tile_bytes + ch * 64)
+                                : wstg + static_cast<uint32_t>((t * kTcMaxChecks * 32 + (ch - L.ch0) * 8) * 8);
+      const uint32_t rstride = c64 ? 512u : 256u;
 #pragma unroll
-      for (int k = 0; k <= kTcMaxChecks; ++k) {
-        if (k > K) break;
+      for (int k = 0; k < kTcMaxChecks; ++k) {
+        if (k >= K) break;
         double v[8];
 #pragma unroll
-        for (int h = 0; h < 8; h += 2) lds_f64x2(row0 + static_cast<uint32_t>((k * 32 + h) * 8), v[h], v[h + 1]);
+        for (int h = 0; h < 8; h += 2) lds_f64x2(row0 + static_cast<uint32_t>(k) * rstride + static_cast<uint32_t>(h * 8), v[h], v[h + 1]);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           if (c == 1 && !two) break;
-          if (k < K) {
 #pragma unroll
-            for (int h = 0; h < 8; ++h) {
-              acc.cx[c][t][k][h % kPartials] = __fma_rn(v[h], xv[c][h], acc.cx[c][t][k][h % kPartials]);
-            }
-          } else {
-#pragma unroll
-            for (int h = 0; h < 8; ++h) acc.sx[c][t][h % kPartials] = __fma_ru(v[h], ax[c][h], acc.sx[c][t][h % kPartials]);
+          for (int h = 0; h < 8; ++h) {
+            acc.cx[c][t][k][h % kPartials] = __fma_rn(v[h], xv[c][h], acc.cx[c][t][k][h % kPartials]);
           }
+        }
+      }
+      // the bound row: 8 bfloat16 values of a for this chunk, one 16-byte load
+      const uint4 aq = lds128(bank + static_cast<uint32_t>(t * item.tile_bytes + K * cstride + ch * 16));
+      const uint32_t aw[4] = {aq.x, aq.y, aq.z, aq.w};
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if (c == 1 && !two) break;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const float a = (h & 1) ? bf16_hi(aw[h >> 1]) : bf16_lo(aw[h >> 1]);
+          acc.sx[c][t][h % kPartials] = __fmaf_ru(a, ax[c][h], acc.sx[c][t][h % kPartials]);
         }
       }
     }
@@ -436,9 +491,10 @@ __device__ __forceinline__ bool bank_finish(const TcJob& jb, const Work& wk, uin
   for (int c = 0; c < 2; ++c) {
 #pragma unroll
     for (int t = 0; t < kTcMaxUnitTiles; ++t) {
-      sx[c][t] = acc.sx[c][t][0];
+      float sf = acc.sx[c][t][0];
 #pragma unroll
-      for (int p = 1; p < kPartials; ++p) sx[c][t] = __dadd_ru(sx[c][t], acc.sx[c][t][p]);
+      for (int p = 1; p < kPartials; ++p) sf = __fadd_ru(sf, acc.sx[c][t][p]);
+      sx[c][t] = static_cast<double>(sf);  // exact
 #pragma unroll
       for (int k = 0; k < kTcMaxChecks; ++k) {
         cx[c][t][k] = acc.cx[c][t][k][0];
@@ -577,13 +633,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       const uint64_t keep_policy = policy_evict_last();
       WorkWalk walk = work_start(plan, kSplit);
       Work wk;
-      uint32_t it = 0;
+      Ring ring;
       bool ok = true;
       while (ok && work_next(plan, walk, wk)) {
         const TcJob& jb = plan.jobs[wk.job];
-        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++it) {
-          const int s = static_cast<int>(it % stages);
-          if (!mbar_wait_sleep(empty + s, ((it / stages) & 1u) ^ 1u)) {
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ring.next(stages)) {
+          const int s = ring.slot;
+          if (!mbar_wait_sleep(empty + s, ring.phase ^ 1u)) {
             ok = false;
             break;
           }
@@ -591,7 +647,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
           const int64_t col = static_cast<int64_t>(kb) * kTcTileK;
           const uint32_t jmax = static_cast<uint32_t>(min(static_cast<int64_t>(kTcTileK), jb.n - col));
           uint32_t bytes = static_cast<uint32_t>(wk.ntiles) * tile_w_bytes + static_cast<uint32_t>(plan.x_bytes);
-          if (jb.fused) bytes += static_cast<uint32_t>(wk.ntiles) * (static_cast<uint32_t>(jb.checks) * jmax * 4u + jmax * 2u);
+          const uint32_t csize = jb.c64 ? 8u : 4u;  // bytes of a checksum value in the bank rows
+          if (jb.fused) bytes += static_cast<uint32_t>(wk.ntiles) * (static_cast<uint32_t>(jb.checks) * jmax * csize + jmax * 2u);
           mbar_arrive_expect_tx(full + s, bytes);
           uint8_t* wdst = e4m3 ? st + plan.w_bytes + plan.x_bytes + plan.bank_bytes : st;
           for (int t = 0; t < wk.ntiles; ++t) {
@@ -603,11 +660,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
             for (int t = 0; t < wk.ntiles; ++t) {
               const int64_t beta = wk.tile + t;
               uint8_t* tb = st + plan.w_bytes + plan.x_bytes + t * plan.tile_bank_bytes;
+              const int cstride = jb.c64 ? 512 : 256;
               for (int k = 0; k < jb.checks; ++k) {
-                bulk_load(tb + k * 256, jb.c + (static_cast<int64_t>(k) * jb.nb + beta) * jb.n + col, jmax * 4u,
-                          full + s, stream_policy);
+                const int64_t off = (static_cast<int64_t>(k) * jb.nb + beta) * jb.n + col;
+                if (jb.c64) {
+                  bulk_load(tb + k * cstride, jb.c64 + off, jmax * 8u, full + s, stream_policy);
+                } else {
+                  bulk_load(tb + k * cstride, jb.c + off, jmax * 4u, full + s, stream_policy);
+                }
               }
-              bulk_load(tb + jb.checks * 256, jb.a + beta * jb.n + col, jmax * 2u, full + s, stream_policy);
+              bulk_load(tb + jb.checks * cstride, jb.a + beta * jb.n + col, jmax * 2u, full + s, stream_policy);
             }
           }
         }
@@ -618,16 +680,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
       const uint32_t idesc = instr_desc(plan.n_pad);
       WorkWalk walk = work_start(plan, kSplit);
       Work wk;
-      uint32_t it = 0, local = 0;
+      Ring ring;
+      uint32_t local = 0;
       bool ok = true;
       while (ok && work_next(plan, walk, wk)) {
         const uint32_t ab = kSplit ? 0u : local % static_cast<uint32_t>(plan.acc_bufs);
         const uint32_t use = kSplit ? 0u : local / static_cast<uint32_t>(plan.acc_bufs);
         if (!mbar_wait_sleep(tempty + ab, (use & 1u) ^ 1u)) break;
         tc_fence_after();
-        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++it) {
-          const int s = static_cast<int>(it % stages);
-          const uint32_t parity = (it / stages) & 1u;
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ring.next(stages)) {
+          const int s = ring.slot;
+          const uint32_t parity = ring.phase;
           if (!mbar_wait_sleep(full + s, parity) || (e4m3 && !mbar_wait_sleep(wready + s, parity))) {
             ok = false;
             break;
@@ -694,15 +757,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
     const uint32_t wstg = smem_addr(bank_area) + static_cast<uint32_t>((warp - 6) * kTcBankWarpStage * 8);
     WorkWalk walk = work_start(plan, kSplit);
     Work wk;
-    uint32_t it = 0, phase = 0;
+    Ring ring;
+    uint32_t phase = 0;
     bool ok = true;
     BankSums acc;
     while (ok && work_next(plan, walk, wk)) {
       const TcJob& jb = plan.jobs[wk.job];
+      const BankItem item = bank_item(plan, jb, wk);
       bank_zero(acc);
-      for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++it) {
-        const int s = static_cast<int>(it % stages);
-        if (!mbar_wait(full + s, (it / stages) & 1u)) {
+      for (int kb = wk.kb0; kb < wk.kb1; ++kb, ring.next(stages)) {
+        const int s = ring.slot;
+        if (!mbar_wait(full + s, ring.phase)) {
           ok = false;
           break;
         }
@@ -712,7 +777,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
           __syncwarp();
           if (lane == 0) mbar_arrive(wready + s);
         }
-        if (jb.fused) bank_stage(plan, jb, wk.ntiles, kb, st, wstg, L, lane, acc);
+        if (item.fused) bank_stage(item, kb == item.last_kb ? item.last_cols : kTcTileK, st, wstg, L, lane, acc);
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + s);
       }

@@ -37,6 +37,7 @@ struct TcJob {
   float* Y;           // (batch, m)
   // fused check (fused != 0): bank rows of block beta = row / 128
   const float* c;     // (checks, nb, n) binary32
+  const double* c64;  // the same widened to binary64, or NULL (then the bank warps widen c)
   const uint16_t* a;  // (nb, n) bfloat16, rounded up
   double* partial_cx;  // (batch, checks, nb, seg_alloc)
   double* partial_s;   // (batch, nb, seg_alloc)
@@ -63,7 +64,7 @@ struct alignas(64) TcPlan {
   int32_t w_bytes;      // bfloat16 W region of a stage: unit tiles * 16 KB
   int32_t x_bytes;      // X region: n_pad * 128
   int32_t bank_bytes;   // bank region: unit tiles * tile_bank_bytes (0 when nothing is fused)
-  int32_t tile_bank_bytes;  // per tile: checks * 256 (c) + 128 (a), 16-aligned
+  int32_t tile_bank_bytes;  // per tile: checks * 512 (c, binary64) or * 256 (binary32), + 128 (a)
   int32_t raw_bytes;    // E4M3 only: the raw weight bytes of a stage (unit tiles * 8 KB)
   int32_t acc_stride;   // tensor-memory columns per accumulator (n_pad up to 32s)
   int32_t acc_bufs;     // accumulator sets (1 or 2): the epilogue of one unit overlaps the next

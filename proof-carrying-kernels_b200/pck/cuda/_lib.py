@@ -37,7 +37,7 @@ class CheckDesc(ctypes.Structure):
         ("passed", _p), ("rho", _p), ("tau", _p),
         ("n", _i64), ("block", _i32), ("num_blocks", _i32), ("checks", _i32),
         ("segments", _i32), ("batch", _i32), ("reserved", _i32),
-        ("coef", _f64), ("geps", _f64), ("tau_floor", _f64),
+        ("coef", _f64), ("geps", _f64), ("tau_floor", _f64), ("c64", _p),
     ]  # fmt: skip
 
 

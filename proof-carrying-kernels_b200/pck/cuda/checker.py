@@ -118,8 +118,17 @@ class GpuBlockedChecker:
         self.geps = next_up(gh + g2 + gh * g2, 4)
         self.tau_floor = next_up(n * 2.0**-148, 2)
         self._scratch: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+        self._c64: torch.Tensor | None = None
         self._counters = torch.zeros((self.num_blocks,), dtype=torch.int32, device=W.device)
         self._partial_cx, self._partial_s = self.scratch(1)
+
+    @property
+    def c64(self) -> torch.Tensor:
+        """c widened to binary64 (exact), made on first use: the tensor-core GEMV's fused
+        reduction reads it instead of widening c in every stage."""
+        if self._c64 is None:
+            self._c64 = self.c.double()
+        return self._c64
 
     def scratch(self, batch: int) -> tuple[torch.Tensor, torch.Tensor]:
         """(partial_cx, partial_s) for a check of ``batch`` columns; batch 1 has no batch axis."""

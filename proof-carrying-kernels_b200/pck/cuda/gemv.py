@@ -97,5 +97,5 @@ def gemv_tc(W: torch.Tensor, X: torch.Tensor, checker=None, full_k: bool = False
     ps = ps.view(batch, checker.num_blocks, checker.segments)
     Y, passed, rho, tau = torch.ops.pck.gemv_tc_checked(W, X, checker.c, checker.a, checker.r, pcx, ps,
                                                         float(checker.coef), float(checker.geps),
-                                                        float(checker.tau_floor), full_k)  # fmt: skip
+                                                        float(checker.tau_floor), full_k, checker.c64)  # fmt: skip
     return Y, CheckResult(passed, rho, tau)

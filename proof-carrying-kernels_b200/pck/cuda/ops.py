@@ -15,7 +15,8 @@ reference rejects them, rather than by a missing dispatch key).
                                                       -> (passed, rho, tau)
     torch.ops.pck.gemv_checked(W, x, c, a, r, partial_cx!, partial_s!, coef, geps, tau_floor, threads)
                                                       -> (y, passed, rho, tau)
-    torch.ops.pck.gemv_tc_checked(W, X, c, a, r, partial_cx!, partial_s!, coef, geps, tau_floor, full_k=False)
+    torch.ops.pck.gemv_tc_checked(W, X, c, a, r, partial_cx!, partial_s!, coef, geps, tau_floor, full_k=False,
+                                  c64=None)
                                                       -> (Y, passed, rho, tau)
     torch.ops.pck.member_check(logits, tokens, top_k?, top_p?, greedy?, slack) -> (ok, above, mass_above)
     torch.ops.pck.sampling_check(logits, selected, lengths, k, top_p, p, temperature, slack, segments)
@@ -162,7 +163,8 @@ def _(W, x, c, a, r, partial_cx, partial_s, coef, geps, tau_floor, threads=256):
 @torch.library.custom_op("pck::gemv_tc_checked", mutates_args=("partial_cx", "partial_s"))
 def gemv_tc_checked(W: torch.Tensor, X: torch.Tensor, c: torch.Tensor, a: torch.Tensor, r: torch.Tensor,
                     partial_cx: torch.Tensor, partial_s: torch.Tensor, coef: float, geps: float,
-                    tau_floor: float, full_k: bool = False) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:  # fmt: skip
+                    tau_floor: float, full_k: bool = False,
+                    c64: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:  # fmt: skip
     Y = torch.empty((X.size(0), W.size(0)), dtype=_FLOAT, device=W.device)
     job = _tc_job(W, X, Y, full_k)
     desc = _lib.CheckDesc()
@@ -179,13 +181,17 @@ def gemv_tc_checked(W: torch.Tensor, X: torch.Tensor, c: torch.Tensor, a: torch.
     desc.n, desc.block, desc.num_blocks, desc.checks = W.size(1), r.size(2), c.size(1), c.size(0)
     desc.segments, desc.batch = partial_cx.size(-1), batch
     desc.coef, desc.geps, desc.tau_floor = float(coef), float(geps), float(tau_floor)
+    if c64 is not None:
+        if c64.dtype != torch.float64 or c64.shape != c.shape or not c64.is_contiguous() or c64.device != c.device:
+            raise RuntimeError("c64 must be a contiguous float64 tensor of c's shape and device")
+        desc.c64 = c64.data_ptr()
     job[0].check = ctypes.pointer(desc)
     _run_tc(job, W.device)
     return Y, passed, rho, tau
 
 
 @gemv_tc_checked.register_fake
-def _(W, X, c, a, r, partial_cx, partial_s, coef, geps, tau_floor, full_k=False):
+def _(W, X, c, a, r, partial_cx, partial_s, coef, geps, tau_floor, full_k=False, c64=None):
     shape = (X.size(0), c.size(0), c.size(1))
     return (X.new_empty((X.size(0), W.size(0)), dtype=_FLOAT), X.new_empty(shape, dtype=torch.bool),
             X.new_empty(shape, dtype=torch.float64), X.new_empty(shape, dtype=torch.float64))  # fmt: skip

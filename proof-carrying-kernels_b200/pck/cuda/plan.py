@@ -256,6 +256,7 @@ class TcLaunch:
             d.n, d.block, d.num_blocks, d.checks = W.size(1), ch.block, ch.num_blocks, ch.checks
             d.segments, d.batch = ch.segments, batch
             d.coef, d.geps, d.tau_floor = float(ch.coef), float(ch.geps), float(ch.tau_floor)
+            d.c64 = ch.c64.data_ptr()
             job.check = ctypes.pointer(d)
             self.results.append(CheckResult(*out))
 

@@ -37,6 +37,14 @@ def bound_ratio(W: torch.Tensor, X: torch.Tensor, Y: torch.Tensor) -> float:
     return float(ratio.max())
 
 
+def assert_tau_matches(fused: torch.Tensor, standalone: torch.Tensor, n: int) -> None:
+    """tau of a check reduced inside the tensor-core kernel against the standalone check's
+    (binary64 bank sums): the kernel sums the bound row a . |x| in binary32 rounded up, never
+    below the exact sum and above it by at most a relative (1 + 2^-23)^h - 1 for chains of
+    h <= n additions, so tau is never smaller and larger by at most about n * 2^-23."""
+    assert bool((fused >= standalone * (1 - 1e-12)).all())
+    assert bool((fused <= standalone * (1 + 1.01 * n * 2.0**-23) + 1e-300).all())
+
 @pytest.mark.parametrize(("m", "n", "batch"), [(128, 64, 16), (128, 4096, 64), (300, 1000, 50), (1024, 4096, 128),
                                                (512, 4096, 256), (128, 14336, 16), (640, 2048, 1)])  # fmt: skip
 def test_outputs_within_the_declared_bound(m: int, n: int, batch: int) -> None:
@@ -119,7 +127,7 @@ def test_checked_call_matches_the_standalone_check(m: int, n: int, batch: int, c
     for b0 in range(0, batch, 16):
         sep = checker.check(X[b0 : b0 + 16].contiguous(), Y[b0 : b0 + 16].contiguous())
         assert torch.equal(sep.passed, res.passed[b0 : b0 + 16])
-        torch.testing.assert_close(res.tau[b0 : b0 + 16], sep.tau, rtol=1e-12, atol=0)
+        assert_tau_matches(res.tau[b0 : b0 + 16], sep.tau, n)
         assert float(((res.rho[b0 : b0 + 16] - sep.rho).abs() / sep.tau).max()) < 1e-6
 
 
@@ -165,8 +173,8 @@ def test_e4m3_weights_within_the_declared_bound(m: int, n: int, batch: int) -> N
 def test_fused_bank_sums_match_the_standalone_check(m: int, n: int, batch: int, checks: int, fmt: str) -> None:
     """The checks whose bank rows the tensor-core kernel reduces itself (persistent units of
     two tiles and split-K clusters, every batch width) decide exactly as the standalone check
-    on the same outputs: every block passes, the bits are equal, tau agrees to binary64
-    rounding and rho far inside tau."""
+    on the same outputs: every block passes, the bits are equal, tau agrees within the
+    binary32 rounding of the bound row and rho is far inside tau."""
     from pck.cuda import GpuBlockedChecker, gemv_tc, tc_height
 
     if fmt == "e4m3":
@@ -183,7 +191,7 @@ def test_fused_bank_sums_match_the_standalone_check(m: int, n: int, batch: int, 
         b1 = min(batch, b0 + 16)
         sep = checker.check(X[b0:b1].contiguous(), Y[b0:b1].contiguous())
         assert torch.equal(sep.passed, res.passed[b0:b1])
-        torch.testing.assert_close(res.tau[b0:b1], sep.tau, rtol=1e-12, atol=0)
+        assert_tau_matches(res.tau[b0:b1], sep.tau, n)
         assert float(((res.rho[b0:b1] - sep.rho).abs() / sep.tau).max()) < 1e-6
 
 
@@ -226,4 +234,4 @@ def test_fused_bank_sums_with_zeros_and_subnormal_activations() -> None:
     for b0 in range(0, 64, 16):
         sep = checker.check(X[b0 : b0 + 16].contiguous(), Y[b0 : b0 + 16].contiguous())
         assert torch.equal(sep.passed, res.passed[b0 : b0 + 16])
-        torch.testing.assert_close(res.tau[b0 : b0 + 16], sep.tau, rtol=1e-12, atol=0)
+        assert_tau_matches(res.tau[b0 : b0 + 16], sep.tau, 4096)
