@@ -278,7 +278,7 @@ int pck_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t m,
  * so a checker of these outputs takes that accumulation's declared height
  * (pck.cuda.gemv.tc_height). `threads` and the exponent range are unused. A job's `check`
  * (optional; the job's own X, Y and shape, batch up to 256) is decided in the same call: for
- * 128-row blocks, at most 2 sign draws and batches up to 64 the GEMV kernel itself reduces
+ * 128-row blocks, at most 2 sign draws and batches up to 128 the GEMV kernel itself reduces
  * the bank rows against the staged X tiles in binary64 (exact products, the bound rounded
  * up); other checks take a bank launch of their own; a verdict launch follows. The reference
  * has no counterpart; its batched decode runs batch-1 GEMVs (harness/csrc/batched_gemv.cu:25-82

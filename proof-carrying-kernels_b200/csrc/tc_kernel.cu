@@ -338,12 +338,14 @@ __device__ __forceinline__ void widen_stage(const TcPlan& plan, int ntiles, uint
 // (1 + 2^-23)^h - 1 for a chain of h additions; an overflow gives +inf and fails the block).
 // Both bounds hold for any split of a sum.
 constexpr int kPartials = 2;
+template <int kK>  // checks per job reduced by the bank warps (1 or 2)
 struct BankSums {
-  double cx[2][kTcMaxUnitTiles][kTcMaxChecks][kPartials];
+  double cx[2][kTcMaxUnitTiles][kK][kPartials];
   float sx[2][kTcMaxUnitTiles][kPartials];
 };
 
-__device__ __forceinline__ void bank_zero(BankSums& a) {
+template <int kK>
+__device__ __forceinline__ void bank_zero(BankSums<kK>& a) {
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
 #pragma unroll
@@ -352,7 +354,7 @@ __device__ __forceinline__ void bank_zero(BankSums& a) {
       for (int p = 0; p < kPartials; ++p) {
         a.sx[c][t][p] = 0.0f;
 #pragma unroll
-        for (int k = 0; k < kTcMaxChecks; ++k) a.cx[c][t][k][p] = 0.0;
+        for (int k = 0; k < kK; ++k) a.cx[c][t][k][p] = 0.0;
       }
     }
   }
@@ -395,8 +397,9 @@ __device__ __forceinline__ BankItem bank_item(const TcPlan& plan, const TcJob& j
 // and per tile 4 two-value shared loads per check serving 8 binary64 FMAs per column, and one
 // 16-byte load of 8 bound values serving 8 binary32 FMAs per column. Only the warp
 // synchronizes; every access names the shared space.
+template <int kK>
 __device__ __forceinline__ void bank_stage(const BankItem& item, int jmax, const uint8_t* stage, uint32_t wstg,
-                                           const BankLanes& L, int lane, BankSums& acc) {
+                                           const BankLanes& L, int lane, BankSums<kK>& acc) {
   const int K = item.checks;
   const int ntiles = item.ntiles;
   const uint32_t bank = smem_addr(stage) + item.bank_off;
@@ -424,54 +427,72 @@ __device__ __forceinline__ void bank_stage(const BankItem& item, int jmax, const
   if (L.col[0] < 0) return;
   const uint32_t xs = smem_addr(stage) + item.x_off;
   const bool two = L.col[1] >= 0;
+  const uint32_t rstride = c64 ? 512u : 256u;  // bytes between checksum rows of a chunk
+  // tiles whose checksum loads are issued together (as many as the registers hold)
+  constexpr int kPre = kK == 1 ? kTcMaxUnitTiles : 1;
   for (int ch = L.ch0; ch < L.ch1 && ch * 8 < jmax; ++ch) {  // jmax is a multiple of 8
-    double xv[2][8];
-    float ax[2][8];
+    // The shared-memory loads first (the tensor core and TMA keep shared memory busy, so each
+    // round trip is long): the columns' 8 activations, and per tile the 8 binary64 checksums
+    // of each check (in the stage itself, or in the warp's widened copy) and the 8 bfloat16
+    // bound values.
+    uint4 xq[2];
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const int b = (c == 0 || two) ? L.col[c] : L.col[0];
-      const uint4 q = lds128(xs + static_cast<uint32_t>(b * 128 + ((ch ^ (b & 7)) << 4)));
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int h = 0; h < 8; ++h) {
-        const float f = (h & 1) ? bf16_hi(w[h >> 1]) : bf16_lo(w[h >> 1]);
-        xv[c][h] = static_cast<double>(f);
-        ax[c][h] = fabsf(f);
-      }
+      xq[c] = lds128(xs + static_cast<uint32_t>(b * 128 + ((ch ^ (b & 7)) << 4)));
     }
 #pragma unroll
-    for (int t = 0; t < kTcMaxUnitTiles; ++t) {
-      if (t >= ntiles) break;
-      // binary64 checksums of this chunk: in the stage itself (row stride 512 bytes) or in the
-      // warp's widened copy (row stride 32 values)
-      const uint32_t row0 = c64 ? bank + static_cast<uint32_t>(t * item.tile_bytes + ch * 64)
-                                : wstg + static_cast<uint32_t>((t * kTcMaxChecks * 32 + (ch - L.ch0) * 8) * 8);
-      const uint32_t rstride = c64 ? 512u : 256u;
+    for (int t0 = 0; t0 < kTcMaxUnitTiles; t0 += kPre) {
+      if (t0 >= ntiles) break;
+      double cv[kPre][kK][8];
+      uint4 aq[kPre];
 #pragma unroll
-      for (int k = 0; k < kTcMaxChecks; ++k) {
-        if (k >= K) break;
-        double v[8];
+      for (int u = 0; u < kPre; ++u) {
+        const int t = t0 + u;
+        if (t >= ntiles) break;
+        const uint32_t row0 = c64 ? bank + static_cast<uint32_t>(t * item.tile_bytes + ch * 64)
+                                  : wstg + static_cast<uint32_t>((t * kTcMaxChecks * 32 + (ch - L.ch0) * 8) * 8);
 #pragma unroll
-        for (int h = 0; h < 8; h += 2) lds_f64x2(row0 + static_cast<uint32_t>(k) * rstride + static_cast<uint32_t>(h * 8), v[h], v[h + 1]);
+        for (int k = 0; k < kK; ++k) {
+          if (k >= K) break;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          if (c == 1 && !two) break;
-#pragma unroll
-          for (int h = 0; h < 8; ++h) {
-            acc.cx[c][t][k][h % kPartials] = __fma_rn(v[h], xv[c][h], acc.cx[c][t][k][h % kPartials]);
+          for (int h = 0; h < 8; h += 2) {
+            lds_f64x2(row0 + static_cast<uint32_t>(k) * rstride + static_cast<uint32_t>(h * 8), cv[u][k][h],
+                      cv[u][k][h + 1]);
           }
         }
+        aq[u] = lds128(bank + static_cast<uint32_t>(t * item.tile_bytes + K * cstride + ch * 16));
       }
-      // the bound row: 8 bfloat16 values of a for this chunk, one 16-byte load
-      const uint4 aq = lds128(bank + static_cast<uint32_t>(t * item.tile_bytes + K * cstride + ch * 16));
-      const uint32_t aw[4] = {aq.x, aq.y, aq.z, aq.w};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         if (c == 1 && !two) break;
+        const uint32_t w[4] = {xq[c].x, xq[c].y, xq[c].z, xq[c].w};
+        double xv[8];
+        float ax[8];
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
-          const float a = (h & 1) ? bf16_hi(aw[h >> 1]) : bf16_lo(aw[h >> 1]);
-          acc.sx[c][t][h % kPartials] = __fmaf_ru(a, ax[c][h], acc.sx[c][t][h % kPartials]);
+          const float f = (h & 1) ? bf16_hi(w[h >> 1]) : bf16_lo(w[h >> 1]);
+          xv[h] = static_cast<double>(f);
+          ax[h] = fabsf(f);
+        }
+#pragma unroll
+        for (int u = 0; u < kPre; ++u) {
+          const int t = t0 + u;
+          if (t >= ntiles) break;
+#pragma unroll
+          for (int k = 0; k < kK; ++k) {
+            if (k >= K) break;
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+              acc.cx[c][t][k][h % kPartials] = __fma_rn(cv[u][k][h], xv[h], acc.cx[c][t][k][h % kPartials]);
+            }
+          }
+          const uint32_t aw[4] = {aq[u].x, aq[u].y, aq[u].z, aq[u].w};
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            const float a = (h & 1) ? bf16_hi(aw[h >> 1]) : bf16_lo(aw[h >> 1]);
+            acc.sx[c][t][h % kPartials] = __fmaf_ru(a, ax[h], acc.sx[c][t][h % kPartials]);
+          }
         }
       }
     }
@@ -483,10 +504,11 @@ __device__ __forceinline__ void bank_stage(const BankItem& item, int jmax, const
 // address; barrier `ready` three times: every warp is done with its staging, every sum is in
 // place, every sum is read) and stored as segment `seg` of the checks' partial sums.
 // `phase` counts the barrier's completions. False if a barrier wait gave up.
+template <int kK>
 __device__ __forceinline__ bool bank_finish(const TcJob& jb, const Work& wk, uint32_t comb, uint64_t* ready,
-                                            uint32_t& phase, const BankLanes& L, int bt, const BankSums& acc) {
+                                            uint32_t& phase, const BankLanes& L, int bt, const BankSums<kK>& acc) {
   const int K = jb.checks;
-  double cx[2][kTcMaxUnitTiles][kTcMaxChecks], sx[2][kTcMaxUnitTiles];
+  double cx[2][kTcMaxUnitTiles][kK], sx[2][kTcMaxUnitTiles];
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
 #pragma unroll
@@ -496,7 +518,7 @@ __device__ __forceinline__ bool bank_finish(const TcJob& jb, const Work& wk, uin
       for (int p = 1; p < kPartials; ++p) sf = __fadd_ru(sf, acc.sx[c][t][p]);
       sx[c][t] = static_cast<double>(sf);  // exact
 #pragma unroll
-      for (int k = 0; k < kTcMaxChecks; ++k) {
+      for (int k = 0; k < kK; ++k) {
         cx[c][t][k] = acc.cx[c][t][k][0];
 #pragma unroll
         for (int p = 1; p < kPartials; ++p) cx[c][t][k] = __dadd_rn(cx[c][t][k], acc.cx[c][t][k][p]);
@@ -520,7 +542,7 @@ __device__ __forceinline__ bool bank_finish(const TcJob& jb, const Work& wk, uin
       for (int t = 0; t < kTcMaxUnitTiles; ++t) {
         if (t >= wk.ntiles) break;
 #pragma unroll
-        for (int k = 0; k < kTcMaxChecks; ++k) {
+        for (int k = 0; k < kK; ++k) {
           if (k < K) sts_f64(at(t, k, c, bt), cx[c][t][k]);
         }
         sts_f64(at(t, kTcMaxChecks, c, bt), sx[c][t]);
@@ -537,7 +559,7 @@ __device__ __forceinline__ bool bank_finish(const TcJob& jb, const Work& wk, uin
             if (t >= wk.ntiles) break;
             double other;
 #pragma unroll
-            for (int k = 0; k < kTcMaxChecks; ++k) {
+            for (int k = 0; k < kK; ++k) {
               if (k < K) {
                 lds_f64x2_one(at(t, k, c, src), other);
                 cx[c][t][k] = __dadd_rn(cx[c][t][k], other);
@@ -561,7 +583,7 @@ __device__ __forceinline__ bool bank_finish(const TcJob& jb, const Work& wk, uin
       if (t >= wk.ntiles) break;
       const int64_t beta = wk.tile + t;
 #pragma unroll
-      for (int k = 0; k < kTcMaxChecks; ++k) {
+      for (int k = 0; k < kK; ++k) {
         if (k < K) jb.partial_cx[((static_cast<int64_t>(b) * K + k) * jb.nb + beta) * jb.seg_alloc + wk.seg] = cx[c][t][k];
       }
       jb.partial_s[(static_cast<int64_t>(b) * jb.nb + beta) * jb.seg_alloc + wk.seg] = sx[c][t];
@@ -571,9 +593,9 @@ __device__ __forceinline__ bool bank_finish(const TcJob& jb, const Work& wk, uin
 }
 
 // ---------------------------------------------------------------------------------------------
-// The kernel (kSplit: the cluster form)
+// The kernel (kSplit: the cluster form; kK: checks per job reduced by the bank warps, 1 or 2)
 
-template <bool kSplit>
+template <bool kSplit, int kK>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant__ TcPlan plan) {
   // A kernel launched after this one as its programmatic dependent reads nothing it writes
   // (the bank kernel for unfused checks), so it may start on the SMs this grid leaves free.
@@ -760,7 +782,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
     Ring ring;
     uint32_t phase = 0;
     bool ok = true;
-    BankSums acc;
+    BankSums<kK> acc;
     while (ok && work_next(plan, walk, wk)) {
       const TcJob& jb = plan.jobs[wk.job];
       const BankItem item = bank_item(plan, jb, wk);
@@ -914,7 +936,7 @@ cudaError_t configure(int* dev_out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    for (auto* fn : {tc_kernel<false>, tc_kernel<true>}) {
+    for (auto* fn : {tc_kernel<false, 1>, tc_kernel<true, 1>, tc_kernel<false, 2>, tc_kernel<true, 2>}) {
       const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemMax);
       if (err != cudaSuccess) return err;
     }
@@ -943,7 +965,7 @@ int tc_max_clusters(int splits) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, tc_kernel<true>, &cfg) != cudaSuccess || n < 1) {
+    if (cudaOccupancyMaxActiveClusters(&n, tc_kernel<true, 1>, &cfg) != cudaSuccess || n < 1) {
       (void)cudaGetLastError();
       n = -1;  // unknown: never chosen
     }
@@ -955,8 +977,13 @@ int tc_max_clusters(int splits) {
 cudaError_t launch_tc(const TcPlan& plan, int splits, int grid, size_t smem, cudaStream_t stream) {
   int dev = -1;
   if (const cudaError_t err = configure(&dev); err != cudaSuccess) return err;
+  const bool two = plan.max_checks > 1;
   if (splits <= 1) {
-    tc_kernel<false><<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(plan);
+    if (two) {
+      tc_kernel<false, 2><<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(plan);
+    } else {
+      tc_kernel<false, 1><<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(plan);
+    }
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
@@ -971,7 +998,7 @@ cudaError_t launch_tc(const TcPlan& plan, int splits, int grid, size_t smem, cud
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, tc_kernel<true>, plan);
+  return two ? cudaLaunchKernelEx(&cfg, tc_kernel<true, 2>, plan) : cudaLaunchKernelEx(&cfg, tc_kernel<true, 1>, plan);
 }
 
 }  // namespace pck

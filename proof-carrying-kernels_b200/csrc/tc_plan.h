@@ -19,7 +19,7 @@ constexpr int kTcMaxUnitTiles = 2;  // 128-row tiles sharing one staged X tile (
 constexpr int kTcBankWarps = 8;     // binary64 bank warps, two per SM sub-partition (also widen E4M3)
 constexpr int kTcThreads = 32 * (6 + kTcBankWarps);  // warp 0 TMA, 1 MMA, 2-5 epilogue, 6-13 bank
 constexpr int kTcMaxChecks = 2;   // checks per job reduced inside the kernel (more: bank kernel)
-constexpr int kTcFuseMaxBatch = 64;  // batches reduced inside the kernel (wider: bank kernel)
+constexpr int kTcFuseMaxBatch = 128;  // batches reduced inside the kernel (wider: bank kernel)
 constexpr int kTcMaxSplits = 8;   // CTAs of a tile's cluster (K ranges), the portable cluster size
 // Shared memory of the bank warps beyond the stages: per warp, the binary64 widening of the
 // bank values its columns need in a stage (also, at the end of a work item, the area where the

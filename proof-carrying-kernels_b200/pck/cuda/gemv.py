@@ -79,7 +79,7 @@ def gemv_tc(W: torch.Tensor, X: torch.Tensor, checker=None, full_k: bool = False
     With a ``checker`` (a GpuBlockedChecker of W, or of W widened to bfloat16 for E4M3 W,
     built with ``height=tc_height(n)``) the call also checks Y: the GEMV kernel reduces the
     bank rows against the staged X tiles in binary64 (128-row blocks, up to 2 checks, batches
-    up to 64; other checkers take a bank launch of their own), a verdict launch decides the blocks, and the
+    up to 128; other checkers take a bank launch of their own), a verdict launch decides the blocks, and the
     call returns (Y, CheckResult) with results of shape (B, checks, num_blocks).
 
     ``full_k``: every output accumulates its whole K range in one chain, so a row's value does
