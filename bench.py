@@ -10,8 +10,9 @@ next streaming launch (`pck_gemv_pipelined`: o's launch decides q/k/v's blocks, 
 layer's q/k/v launch decides down's), so a step still decides all seven checks, with no
 launch of its own; `--verdicts launch` instead ends the step with one verdict-kernel launch
 for all seven (the reference runs one checker launch per layer). Captured in a CUDA graph.
-With N GPUs every matrix is row-sharded by whole checker blocks and one NCCL all-gather
-per step assembles the outputs and verdict bits.
+With N GPUs every matrix is row-sharded by whole checker blocks and one all-gather per
+step assembles the outputs and verdict bits: by default this library's peer-memory kernel
+(each rank stores its slice into every peer over NVLink), `--gather nccl` for NCCL's.
 
 metric: checked-GEMV HBM throughput = algorithmic bytes of the step (weights, activations,
 outputs, checksum bank, verdicts) / device time, GB/s, over all ranks.
@@ -357,7 +358,7 @@ def gathered_layer_matches(groups, xs, ex, full, world: int, rank: int) -> bool 
 LM_VOCAB, LM_N, LM_BATCH = 128256, 4096, 64
 
 
-def lm_head_reading(rank: int, world: int, device, steps: int, warmup: int) -> dict:
+def lm_head_reading(rank: int, world: int, device, steps: int, warmup: int, gather: str = "peer") -> dict:
     """Config 5: the Llama-3 LM head W (128256, 4096) bfloat16 at decode batch 64, row-sharded
     by whole 128-row blocks over the ranks, each rank's slice checked in the same call as its
     tensor-core GEMV; one all-gather of logits and verdict bits; top-k 50 / top-p 0.9 sampling
@@ -377,6 +378,8 @@ def lm_head_reading(rank: int, world: int, device, steps: int, warmup: int) -> d
         del W_all
         W_all = None
     head = CheckedLMHead(W, X, LM_VOCAB, world=world, rank=rank, generator=torch.Generator().manual_seed(5001))
+    if world > 1 and gather == "peer":
+        head.exchange.use_peer_memory()
     torch.manual_seed(5002)  # the sampler's draws: the same on every rank
     sampler = TopKTopPSampler(LM_BATCH, LM_VOCAB, k=50, p=0.9, temperature=1.0, device=device, fault_rate=0.01)
     counts = torch.zeros(4, dtype=torch.int64, device=device)  # steps all passed, planted, caught, false alarms
@@ -420,10 +423,13 @@ def lm_head_reading(rank: int, world: int, device, steps: int, warmup: int) -> d
     gemv_gbs = float(total.item()) / t_gemv / 1e9
     peak = float(measured_peaks()["hbm_gbs"])
     del g_gemv, g_forward, g_member, g_full
+    if world > 1:
+        head.exchange.close()
     return {
         "workload": "Llama-3 LM head 128256x4096 bf16, batch 64, row-sharded checked tcgen05 GEMV + all-gather "
                     "+ top-k 50 / top-p 0.9 sampling + fused membership check (1% planted non-members)",
         "parallelism": f"row-shard x{world}" if world > 1 else "single",
+        "gather": gather if world > 1 else None,
         "ms_per_step": round(t_full * 1e3, 4), "tokens_per_s": round(LM_BATCH / t_full),
         "gemv_ms": round(t_gemv * 1e3, 4), "gemv_and_gather_ms": round(t_forward * 1e3, 4),
         "gather_ms": round((t_forward - t_gemv) * 1e3, 4) if world > 1 else 0.0,
@@ -608,6 +614,8 @@ def main() -> None:
     parser.add_argument("--no-lm-head", action="store_true", help="skip the LM-head (config 5) reading")
     parser.add_argument("--no-prefetch", action="store_true",
                         help="launches do not prefetch the next launch's first weight pieces into L2")
+    parser.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                        help="N > 1: the all-gather of the outputs (peer: pck_peer_all_gather over NVLink)")
     parser.add_argument("--verdicts", choices=sorted(VERDICTS), default="carried",
                         help="carried: each launch decides the previous launch's checks; launch: a verdict launch per step")
     args = parser.parse_args()
@@ -629,6 +637,9 @@ def main() -> None:
                                              device_id=device)  # fmt: skip
 
     groups, verdict, plain, xs, ex, ex_plain, full = build_layer(args, rank, world, device, keep_full=world > 1)
+    if world > 1 and args.gather == "peer":
+        ex.use_peer_memory()
+        ex_plain.use_peer_memory()
     x_all = build_layer.x_all
     vs = ex.parts[1]
     step_bytes_local = sum(g.algorithmic_bytes for g in groups)
@@ -661,8 +672,13 @@ def main() -> None:
         if world > 1:
             ex_plain.gather()
 
+    def local_step() -> None:  # the launches alone, without the gather (N > 1 breakdown)
+        for g in launches:
+            g.launch()
+
     graph_checked = cuda_graph(checked_step, per_graph)
     graph_plain = cuda_graph(plain_step, per_graph)
+    graph_local = cuda_graph(local_step, per_graph) if world > 1 else None
     # correctness of the timed path: every block of the honest layer passes on every rank,
     # and (N > 1) the gathered outputs equal the unsharded ones bit for bit
     graph_checked[0].replay()
@@ -682,6 +698,7 @@ def main() -> None:
         t_checked = timed(graph_checked, args.steps, args.warmup, world)
         t_plain = timed(graph_plain, args.steps, args.warmup, world)
         t_other = timed(graph_other, args.steps, args.warmup, world) if graph_other is not None else None
+        t_local = timed(graph_local, args.steps, args.warmup, world) if graph_local is not None else None
     clock = clocks.summary()
     side_steps = max(20, args.steps // 10)
     per_launch = launch_times([g.launch for g in launches] + ([ex.gather] if world > 1 else []), side_steps, world)
@@ -691,7 +708,7 @@ def main() -> None:
     if world == 1 and args.weights == "bf16" and args.batch == 1 and not args.no_e4m3:
         e4m3 = e4m3_reading(args, device, side_steps, args.warmup)
     if not args.no_lm_head:
-        lm_head = lm_head_reading(rank, world, device, side_steps, args.warmup)
+        lm_head = lm_head_reading(rank, world, device, side_steps, args.warmup, args.gather)
     t_e2e, h2d, d2h = e2e_step_time(launches, x_all, ex, side_steps, args.warmup, world)
 
     total_bytes = torch.tensor([float(step_bytes_local)], device=device)
@@ -736,8 +753,11 @@ def main() -> None:
             "verdict_launch_ms_per_step": round(t_other * 1e3, 5) if t_other is not None else None,
             "all_blocks_passed": all_passed,
             "gathered_outputs_equal_single_gpu": gathered_ok,
+            "gather": ex.transport if world > 1 else None,
+            "local_launches_ms_per_step": round(t_local * 1e3, 5) if t_local is not None else None,
+            "gather_ms_per_step": round((t_checked - t_local) * 1e3, 5) if t_local is not None else None,
             "launch_ms": {"launches": [f"stream_kernel:{'+'.join(grp)}" for grp in LLAMA3_GROUP_NAMES]
-                                      + (["nccl all_gather"] if world > 1 else []) + ([] if args.verdicts == "carried"
+                                      + ([f"{ex.transport} all_gather"] if world > 1 else []) + ([] if args.verdicts == "carried"
                                                                                      else ["verdict_kernel"]),
                           "ms": per_launch,
                           "how": "eager, a CUDA event between consecutive launches, mean over "
@@ -750,7 +770,7 @@ def main() -> None:
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"},
             "e2e": {"value": round(step_bytes / t_e2e / 1e9, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e * 1e3, 4)},
-            "gpu_launches": len(launches) * args.steps,
+            "gpu_launches": (len(launches) + (1 if world > 1 and ex.transport == "peer" else 0)) * args.steps,
             "clocks": clock,
             "cpu_baseline": cpu,
             "batch128": batch128,
@@ -758,8 +778,10 @@ def main() -> None:
             "lm_head": lm_head,
         }  # fmt: skip
         print(json.dumps(line), flush=True)
-    del graph_checked, graph_plain, graph_other
+    del graph_checked, graph_plain, graph_other, graph_local
     if world > 1:
+        ex.close()
+        ex_plain.close()
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 

@@ -26,6 +26,7 @@ cudaError_t launch_gemv_naive(const void* W, const void* x, float* y, int64_t m,
                               int threads, int sms, cudaStream_t stream);
 cudaError_t status_stream_bf16(unsigned int* value, bool clear);
 cudaError_t status_stream_e4m3(unsigned int* value, bool clear);
+cudaError_t peer_status(unsigned int* value, bool clear);
 cudaError_t launch_bank_build(const void* W, const int8_t* r, float* c, void* a, int64_t n,
                               int block, int num_blocks, int checks, double factor,
                               cudaStream_t stream);
@@ -644,7 +645,7 @@ int pck_device_status(unsigned int* status, int clear) {
   cudaError_t err = cudaDeviceSynchronize();
   if (err != cudaSuccess) return cuda_fail("device synchronize", err);
   unsigned int total = 0;
-  for (auto* reader : {pck::status_stream_bf16, pck::status_stream_e4m3, pck::tc_status}) {
+  for (auto* reader : {pck::status_stream_bf16, pck::status_stream_e4m3, pck::tc_status, pck::peer_status}) {
     unsigned int v = 0;
     err = reader(&v, clear != 0);
     if (err != cudaSuccess) return cuda_fail("status read", err);

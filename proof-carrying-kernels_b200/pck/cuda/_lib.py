@@ -52,6 +52,19 @@ class GemvJob(ctypes.Structure):
     ]  # fmt: skip
 
 
+PEER_MAX_RANKS = 8
+PEER_HANDLE_BYTES = 64
+
+
+class PeerGather(ctypes.Structure):
+    """pck_peer_gather."""
+
+    _fields_ = [
+        ("buffers", _p * PEER_MAX_RANKS), ("local", _p), ("gathered", _p),
+        ("slice_bytes", _i64), ("rank", _i32), ("world", _i32),
+    ]  # fmt: skip
+
+
 _SIGNATURES = {
     "pck_last_error": ([], ctypes.c_char_p),
     "pck_abi_version": ([], _int),
@@ -74,6 +87,13 @@ _SIGNATURES = {
                             _p, _p], _int),
     "pck_member_check": ([_p, _int, _i64, _i64, _i64, _p, _p, _p, _p, _f64, _p, _p, _p, _p], _int),
     "pck_bank_build": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _f64, _p], _int),
+    "pck_peer_buffer_bytes": ([_i64, _int], _i64),
+    "pck_peer_alloc": ([_i64, ctypes.POINTER(_p)], _int),
+    "pck_peer_free": ([_p], _int),
+    "pck_peer_export": ([_p, _p], _int),
+    "pck_peer_import": ([_p, ctypes.POINTER(_p)], _int),
+    "pck_peer_close": ([_p], _int),
+    "pck_peer_all_gather": ([ctypes.POINTER(PeerGather), _p], _int),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -2,10 +2,11 @@
 
 Every matrix is split by whole checker blocks: rank r owns the blocks
 [r*q, min((r+1)*q, nb)) with q = ceil(nb / world), so each block's check is local to one
-rank and needs nothing from the others. After the local launches, one NCCL
-all_gather_into_tensor assembles the outputs of all projections (and one the verdict
-bits) on every rank; a rank with fewer blocks pads its slice, so every rank sends the
-same count.
+rank and needs nothing from the others. After the local launches, one all-gather
+assembles the outputs of all projections (and the verdict bits) on every rank: NCCL's
+all_gather_into_tensor, or (`Exchange.use_peer_memory`) this library's kernel that stores
+each rank's slice straight into every peer's memory over NVLink (`pck_peer_all_gather`).
+A rank with fewer blocks pads its slice, so every rank sends the same count.
 """
 
 from __future__ import annotations
@@ -103,6 +104,77 @@ class PackedOutputs:
         return torch.cat(chunks, dim=-1, out=out)
 
 
+class PeerTransport:
+    """The all-gather of one (local, gathered) buffer pair over peer memory: an exchange
+    buffer per rank from the library (`pck_peer_alloc`), mapped into every other rank with
+    CUDA IPC, and one `pck_peer_all_gather` kernel per call on the current stream. Built
+    collectively (every rank at the same point, like a process group call); `close()` is
+    collective too."""
+
+    def __init__(self, local: torch.Tensor, gathered: torch.Tensor, world: int, rank: int, group=None) -> None:
+        import ctypes
+
+        import torch.distributed as dist
+
+        from pck.cuda import _lib
+
+        if not 2 <= world <= _lib.PEER_MAX_RANKS:
+            raise ValueError(f"peer memory serves 2 to {_lib.PEER_MAX_RANKS} ranks, got {world}")
+        slice_bytes = local.numel() * local.element_size()
+        if gathered.numel() * gathered.element_size() != world * slice_bytes or slice_bytes % 16:
+            raise ValueError("gathered must hold world slices of a multiple of 16 bytes")
+        self.lib, self.group, self.world, self.rank = _lib.library(), group, world, rank
+        self.device = local.device
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            size = self.lib.pck_peer_buffer_bytes(slice_bytes, world)
+            _lib.check(self.lib.pck_peer_alloc(size, ctypes.byref(own)), "peer buffer")
+            handle = (ctypes.c_ubyte * _lib.PEER_HANDLE_BYTES)()
+            _lib.check(self.lib.pck_peer_export(own, handle), "peer export")
+            handles: list[bytes | None] = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self.own, self.mapped = own, []
+            self.desc = _lib.PeerGather()
+            for r in range(world):
+                if r == rank:
+                    self.desc.buffers[r] = own.value
+                    continue
+                q = ctypes.c_void_p()
+                h = (ctypes.c_ubyte * _lib.PEER_HANDLE_BYTES).from_buffer_copy(handles[r])
+                _lib.check(self.lib.pck_peer_import(h, ctypes.byref(q)), "peer import")
+                self.mapped.append(q)
+                self.desc.buffers[r] = q.value
+        self.desc.local, self.desc.gathered = local.data_ptr(), gathered.data_ptr()
+        self.desc.slice_bytes, self.desc.rank, self.desc.world = slice_bytes, rank, world
+        self._keep = (local, gathered)
+
+    def gather(self) -> None:
+        import ctypes
+
+        from pck.cuda import _lib
+        from pck.cuda._ext import stream_handle
+
+        rc = self.lib.pck_peer_all_gather(ctypes.byref(self.desc), stream_handle(self.device))
+        _lib.check(rc, "peer all-gather")
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers, waits for every rank to do the same, frees this one's."""
+        import torch.distributed as dist
+
+        from pck.cuda import _lib
+
+        if self.own is None:
+            return
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            for q in self.mapped:
+                _lib.check(self.lib.pck_peer_close(q), "peer close")
+            self.mapped = []
+            dist.barrier(group=self.group)
+            _lib.check(self.lib.pck_peer_free(self.own), "peer free")
+        self.own = None
+
+
 class Exchange:
     """Several PackedOutputs (e.g. a layer's outputs and its verdict bits) in one byte buffer
     per rank, each section 16-byte aligned, so a single all-gather per step moves them all.
@@ -120,8 +192,28 @@ class Exchange:
         self.parts = [PackedOutputs(ms, block, world, rank, device, batch, dtype,
                                     buffers=(self.local, self.gathered, start, off))
                       for (ms, block, batch, dtype), start in zip(sections, starts, strict=True)]  # fmt: skip
+        self.world, self.rank = world, rank
+        self.peer: PeerTransport | None = None
+
+    def use_peer_memory(self, group=None) -> None:
+        """Gathers over peer memory from now on (collective: every rank calls it)."""
+        if self.peer is None:
+            self.peer = PeerTransport(self.local, self.gathered, self.world, self.rank, group)
+
+    @property
+    def transport(self) -> str:
+        return "peer" if self.peer is not None else "nccl"
 
     def gather(self, group=None) -> None:
         import torch.distributed as dist
 
+        if self.peer is not None:
+            self.peer.gather()
+            return
         dist.all_gather_into_tensor(self.gathered, self.local, group=group)
+
+    def close(self) -> None:
+        """Releases the peer-memory transport (collective), if any."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
