@@ -34,11 +34,12 @@ extern "C" {
 /*
  * Flag OR-ed into a job's weight_format: the weights were written before the kernel that
  * precedes this call on its stream began (e.g. loaded at start-up, followed by a
- * synchronize). The streaming kernel then requests its first weight pieces while that
- * kernel is still running (programmatic dependent launch); without the flag it waits for
- * the preceding kernel to complete before reading any weight, as it always does for the
- * checksum bank (c, a) and the activations. A caller that sets the flag while the
- * preceding kernel writes W can get stale weights and false alarms.
+ * synchronize). The streaming and tensor-core kernels then request their first weight
+ * pieces while that kernel is still running (programmatic dependent launch); without the
+ * flag they wait for the preceding kernel to complete before reading any weight, as they
+ * always do for the checksum bank (c, a) and the activations. A caller that sets the flag
+ * while the preceding kernel writes W can get stale weights and false alarms. (For
+ * pck_gemv_tc every job of the call must carry it.)
  */
 #define PCK_WEIGHTS_SETTLED 0x100
 /*
@@ -331,6 +332,25 @@ int pck_member_check(const void* logits, int logits_dtype, int64_t rows, int64_t
                      int64_t row_stride, const int64_t* tokens, const int64_t* top_k,
                      const double* top_p, const uint8_t* greedy, double slack, uint8_t* ok,
                      int64_t* above, double* mass_above, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Untrusted top-k / top-p sampler (checked afterwards by pck_member_check).              */
+
+/*
+ * For every row b of binary32 logits (rows, vocab) (row b at logits + b*row_stride): with
+ * l = logits / temperature, the k largest values (1 <= k <= 1024; ties at the k-th value by
+ * position), their binary32 softmax, the shortest prefix in descending order whose mass
+ * before each kept position is below p, and an inverse-CDF draw from it with draws[b]
+ * (uniform in [0, 1)): tokens[b]. When fault_draws is not NULL and fault_draws[b] <
+ * fault_rate, tokens[b] is the row's argmin instead and injected[b] = 1 (else 0; injected
+ * may be NULL). One launch, one CTA per row, no scratch memory. Not part of the trusted
+ * path: the reference samples with torch (vLLM's sampler, src/pck/vllm_plugin.py, and the
+ * untrusted samplers of src/pck/cuda/sampling.py:96-136), and every token is checked by the
+ * membership kernel.
+ */
+int pck_sample_topk_topp(const float* logits, int64_t rows, int64_t vocab, int64_t row_stride, int64_t k, double p,
+                         double temperature, const float* draws, const float* fault_draws, double fault_rate,
+                         int64_t* tokens, uint8_t* injected, void* stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* All-gather of row-sharded outputs over peer memory (one process per GPU of one node).  */

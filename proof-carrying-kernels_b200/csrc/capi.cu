@@ -869,7 +869,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
     return fail(PCK_ERR_ARGUMENT, "unknown weight format %d", jobs[0].weight_format);
   }
   const bool e4m3 = wfmt == PCK_WEIGHTS_E4M3;
-  bool full_k = false;
+  bool full_k = false, settled = true;
   const int n_pad = (batch + 15) / 16 * 16;
   int tiles = 0, nj = 0;
   const pck_check_desc* descs[pck::kTcMaxJobs] = {};
@@ -879,6 +879,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
       return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the weight format");
     }
     full_k = full_k || (jb.weight_format & PCK_TC_FULL_K) != 0;
+    settled = settled && (jb.weight_format & PCK_WEIGHTS_SETTLED) != 0;
     if (jb.batch != batch) return fail(PCK_ERR_ARGUMENT, "jobs in one launch must share the batch");
     if (int rc = check_gemv_args(jb.W, jb.X, jb.Y, jb.m, jb.n, 256, 1)) return rc;
     if (jb.m == 0) continue;
@@ -924,6 +925,7 @@ int pck_gemv_tc(const pck_gemv_job* jobs, int count, void* stream) {
   plan.batch = batch;
   plan.n_pad = n_pad;
   plan.weights = e4m3 ? pck::kTcWeightsE4m3 : pck::kTcWeightsBf16;
+  plan.settled = settled ? 1 : 0;
 
   // The form. Persistent: a CTA per SM over contiguous ranges of tiles, in units of two tiles
   // sharing each staged X tile. Split: a cluster of `splits` CTAs per unit of one or two

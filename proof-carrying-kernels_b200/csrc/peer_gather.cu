@@ -86,7 +86,9 @@ __device__ __forceinline__ uint4 ld_v4_volatile(const uint4* p) {
 // The flagged form. Payload word w (16 bytes) of a slice travels as two 16-byte units
 // {d0, e, d1, e} and {d2, e, d3, e} (e = the call number, never 0), at units 2w and 2w + 1 of
 // the sender's part of the receive region; each 8-byte half is written in one piece, so a
-// receiver that sees e beside a data word sees that word of this call.
+// receiver that sees e beside a data word sees that word of this call. Sends and receives
+// are spread over the (rank, word) pairs, one pair per thread where the grid allows, so the
+// polls of different words and peers overlap.
 __global__ void __launch_bounds__(kPeerThreads) peer_gather_flagged(const __grid_constant__ PeerParams p) {
   const int64_t slice_bytes = p.slice_words * 16;
   const int64_t region = region_bytes(slice_bytes, p.world);
@@ -101,40 +103,42 @@ __global__ void __launch_bounds__(kPeerThreads) peer_gather_flagged(const __grid
   const int64_t part = 2 * slice_bytes;  // bytes of one sender's part of a region
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kPeerThreads;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * kPeerThreads + threadIdx.x;
-  // send: this rank's slice, flagged, to every peer; its own part straight into `gathered`
-  for (int64_t w = first; w < p.slice_words; w += stride) {
+  const int64_t pairs = static_cast<int64_t>(p.world) * p.slice_words;
+  // send: pair (r, w) stores word w of this rank's slice, flagged, into rank r (its own part
+  // of `gathered` directly)
+  for (int64_t i = first; i < pairs; i += stride) {
+    const int r = static_cast<int>(i / p.slice_words);
+    const int64_t w = i - static_cast<int64_t>(r) * p.slice_words;
     const uint4 v = p.local[w];
-    p.gathered[p.rank * p.slice_words + w] = v;
-    const uint4 u0 = make_uint4(v.x, e, v.y, e), u1 = make_uint4(v.z, e, v.w, e);
-    for (int r = 0; r < p.world; ++r) {
-      if (r == p.rank) continue;
-      uint4* dst = reinterpret_cast<uint4*>(p.buffers[r] + base + p.rank * part) + 2 * w;
-      st_v4(dst, u0);
-      st_v4(dst + 1, u1);
+    if (r == p.rank) {
+      p.gathered[p.rank * p.slice_words + w] = v;
+      continue;
     }
+    uint4* dst = reinterpret_cast<uint4*>(p.buffers[r] + base + p.rank * part) + 2 * w;
+    st_v4(dst, make_uint4(v.x, e, v.y, e));
+    st_v4(dst + 1, make_uint4(v.z, e, v.w, e));
   }
-  // receive: every peer's words of this call, polled until their flags say so
+  // receive: pair (r, w) polls rank r's word w until its flags carry this call's number
   bool ok = true;
   const unsigned long long start = global_ns();
-  for (int r = 0; r < p.world && ok; ++r) {
+  for (int64_t i = first; i < pairs && ok; i += stride) {
+    const int r = static_cast<int>(i / p.slice_words);
     if (r == p.rank) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(self + base + r * part);
-    for (int64_t w = first; w < p.slice_words; w += stride) {
-      uint4 u0, u1;
-      int spins = 0;
-      while (true) {
-        u0 = ld_v4_volatile(src + 2 * w);
-        u1 = ld_v4_volatile(src + 2 * w + 1);
-        if (u0.y == e && u0.w == e && u1.y == e && u1.w == e) break;
-        if (++spins % 64 == 0 && global_ns() - start > kWaitLimitNs) {
-          report(kDevTimeout);
-          ok = false;
-          break;
-        }
+    const int64_t w = i - static_cast<int64_t>(r) * p.slice_words;
+    const uint4* src = reinterpret_cast<const uint4*>(self + base + r * part) + 2 * w;
+    uint4 u0, u1;
+    int spins = 0;
+    while (true) {
+      u0 = ld_v4_volatile(src);
+      u1 = ld_v4_volatile(src + 1);
+      if (u0.y == e && u0.w == e && u1.y == e && u1.w == e) break;
+      if (++spins % 64 == 0 && global_ns() - start > kWaitLimitNs) {
+        report(kDevTimeout);
+        ok = false;
+        break;
       }
-      if (!ok) break;
-      p.gathered[r * p.slice_words + w] = make_uint4(u0.x, u0.z, u1.x, u1.z);
     }
+    if (ok) p.gathered[r * p.slice_words + w] = make_uint4(u0.x, u0.z, u1.x, u1.z);
   }
   __syncthreads();
   if (threadIdx.x == 0) epochs[blockIdx.x] = e;
@@ -290,11 +294,13 @@ extern "C" int pck_peer_all_gather(const pck_peer_gather* g, void* stream) {
   p.slice_words = g->slice_bytes / 16;
   p.rank = g->rank;
   p.world = g->world;
-  // enough CTAs to spread the stores (about 4 words a thread), the same count on every rank
-  // (it depends on the slice only)
-  const int64_t want = (p.slice_words + pck::kPeerThreads * 4 - 1) / (pck::kPeerThreads * 4);
+  // The same grid on every rank (it depends on the slice and the world only): the flagged
+  // form one (rank, word) pair per thread, the counted form about 4 words a thread.
+  const bool flagged = pck::flagged_form(g->slice_bytes);
+  const int64_t want = flagged ? (p.world * p.slice_words + pck::kPeerThreads - 1) / pck::kPeerThreads
+                               : (p.slice_words + pck::kPeerThreads * 4 - 1) / (pck::kPeerThreads * 4);
   const int grid = static_cast<int>(want < 1 ? 1 : want > pck::kPeerMaxCtas ? pck::kPeerMaxCtas : want);
-  if (pck::flagged_form(g->slice_bytes)) {
+  if (flagged) {
     pck::peer_gather_flagged<<<grid, pck::kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
   } else {
     pck::peer_gather_kernel<<<grid, pck::kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);

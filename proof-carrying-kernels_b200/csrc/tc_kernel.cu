@@ -646,6 +646,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tile_w_bytes = e4m3 ? kTileE4m3Bytes : kTileBf16Bytes;
+  // Launched as the programmatic dependent of the kernel before it: every thread but the
+  // producer (which may first request settled weights) waits for that kernel here.
+  if (!(warp == 0 && lane == 0)) wait_for_producers();
   [[maybe_unused]] Work last{};  // the split form's one item, for its epilogue
   [[maybe_unused]] uint32_t last_it = 0;
 
@@ -653,13 +656,47 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
     if (lane == 0) {  // TMA producer
       const uint64_t stream_policy = policy_evict_first();
       const uint64_t keep_policy = policy_evict_last();
+      // The stage's bytes (W tiles, X tile, the fused checks' bank rows) and its W tiles.
+      auto stage_bytes_of = [&](const TcJob& jb, const Work& wk, int kb) {
+        const int64_t col = static_cast<int64_t>(kb) * kTcTileK;
+        const uint32_t jmax = static_cast<uint32_t>(min(static_cast<int64_t>(kTcTileK), jb.n - col));
+        uint32_t bytes = static_cast<uint32_t>(wk.ntiles) * tile_w_bytes + static_cast<uint32_t>(plan.x_bytes);
+        const uint32_t csize = jb.c64 ? 8u : 4u;  // bytes of a checksum value in the bank rows
+        if (jb.fused) bytes += static_cast<uint32_t>(wk.ntiles) * (static_cast<uint32_t>(jb.checks) * jmax * csize + jmax * 2u);
+        return bytes;
+      };
+      auto load_w = [&](const TcJob& jb, const Work& wk, int kb, uint8_t* st, uint64_t* bar) {
+        uint8_t* wdst = e4m3 ? st + plan.w_bytes + plan.x_bytes + plan.bank_bytes : st;
+        for (int t = 0; t < wk.ntiles; ++t) {
+          tma_load_2d(wdst + static_cast<size_t>(t) * tile_w_bytes, &jb.w_map, bar, kb * kTcTileK,
+                      (wk.tile + t) * kTcTileM, stream_policy);
+        }
+      };
+      // Settled weights: the first `stages` stages' W tiles before the producer wait (the ring
+      // starts empty), so they stream while the previous kernel finishes.
+      int pre = 0;
+      if (plan.settled) {
+        WorkWalk walk = work_start(plan, kSplit);
+        Work wk;
+        Ring ring;
+        while (pre < stages && work_next(plan, walk, wk)) {
+          const TcJob& jb = plan.jobs[wk.job];
+          for (int kb = wk.kb0; kb < wk.kb1 && pre < stages; ++kb, ++pre, ring.next(stages)) {
+            uint8_t* st = smem + static_cast<size_t>(ring.slot) * stage_bytes;
+            mbar_arrive_expect_tx(full + ring.slot, stage_bytes_of(jb, wk, kb));
+            load_w(jb, wk, kb, st, full + ring.slot);
+          }
+        }
+      }
+      wait_for_producers();  // X, the bank rows and the outputs belong to the kernels before
       WorkWalk walk = work_start(plan, kSplit);
       Work wk;
       Ring ring;
       bool ok = true;
+      int issued = 0;
       while (ok && work_next(plan, walk, wk)) {
         const TcJob& jb = plan.jobs[wk.job];
-        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ring.next(stages)) {
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ring.next(stages), ++issued) {
           const int s = ring.slot;
           if (!mbar_wait_sleep(empty + s, ring.phase ^ 1u)) {
             ok = false;
@@ -668,14 +705,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const __grid_constant
           uint8_t* st = smem + static_cast<size_t>(s) * stage_bytes;
           const int64_t col = static_cast<int64_t>(kb) * kTcTileK;
           const uint32_t jmax = static_cast<uint32_t>(min(static_cast<int64_t>(kTcTileK), jb.n - col));
-          uint32_t bytes = static_cast<uint32_t>(wk.ntiles) * tile_w_bytes + static_cast<uint32_t>(plan.x_bytes);
-          const uint32_t csize = jb.c64 ? 8u : 4u;  // bytes of a checksum value in the bank rows
-          if (jb.fused) bytes += static_cast<uint32_t>(wk.ntiles) * (static_cast<uint32_t>(jb.checks) * jmax * csize + jmax * 2u);
-          mbar_arrive_expect_tx(full + s, bytes);
-          uint8_t* wdst = e4m3 ? st + plan.w_bytes + plan.x_bytes + plan.bank_bytes : st;
-          for (int t = 0; t < wk.ntiles; ++t) {
-            tma_load_2d(wdst + static_cast<size_t>(t) * tile_w_bytes, &jb.w_map, full + s, kb * kTcTileK,
-                        (wk.tile + t) * kTcTileM, stream_policy);
+          if (issued >= pre) {
+            mbar_arrive_expect_tx(full + s, stage_bytes_of(jb, wk, kb));
+            load_w(jb, wk, kb, st, full + s);
           }
           tma_load_2d(st + plan.w_bytes, &jb.x_map, full + s, kb * kTcTileK, 0, keep_policy);
           if (jb.fused) {
@@ -978,26 +1010,23 @@ cudaError_t launch_tc(const TcPlan& plan, int splits, int grid, size_t smem, cud
   int dev = -1;
   if (const cudaError_t err = configure(&dev); err != cudaSuccess) return err;
   const bool two = plan.max_checks > 1;
-  if (splits <= 1) {
-    if (two) {
-      tc_kernel<false, 2><<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(plan);
-    } else {
-      tc_kernel<false, 1><<<static_cast<unsigned>(grid), kTcThreads, smem, stream>>>(plan);
-    }
-    return cudaGetLastError();
-  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));  // a cluster of `splits` CTAs per unit
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));  // split: a cluster of `splits` CTAs per unit
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // starts during the kernel before
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = splits > 1 ? 2 : 1;
+  if (splits <= 1) {
+    return two ? cudaLaunchKernelEx(&cfg, tc_kernel<false, 2>, plan) : cudaLaunchKernelEx(&cfg, tc_kernel<false, 1>, plan);
+  }
   return two ? cudaLaunchKernelEx(&cfg, tc_kernel<true, 2>, plan) : cudaLaunchKernelEx(&cfg, tc_kernel<true, 1>, plan);
 }
 

@@ -76,6 +76,8 @@ struct alignas(64) TcPlan {
   int32_t strided;      // persistent form: CTA c takes units c, c + grid, ... (else a contiguous
                         // range of tiles [c * total / grid, (c + 1) * total / grid), paired)
   int32_t total_units;
+  int32_t settled;      // every job's W was written before the preceding kernel began: the
+                        // first stages' W tiles are requested before the producer wait
 };
 
 // splits == 1: the persistent kernel over `grid` CTAs; else `grid` = total_units * splits CTAs

@@ -87,6 +87,7 @@ _SIGNATURES = {
                             _p, _p], _int),
     "pck_member_check": ([_p, _int, _i64, _i64, _i64, _p, _p, _p, _p, _f64, _p, _p, _p, _p], _int),
     "pck_bank_build": ([_p, _p, _p, _p, _i64, _i64, _int, _int, _f64, _p], _int),
+    "pck_sample_topk_topp": ([_p, _i64, _i64, _i64, _i64, _f64, _f64, _p, _p, _f64, _p, _p, _p], _int),
     "pck_peer_buffer_bytes": ([_i64, _int], _i64),
     "pck_peer_alloc": ([_i64, ctypes.POINTER(_p)], _int),
     "pck_peer_free": ([_p], _int),

@@ -91,12 +91,19 @@ class TopKTopPSampler:
     capturable): temperature, the ``k`` largest logits, the shortest prefix of them (in
     descending order) whose probability reaches ``p`` (binary32 softmax, running sum in
     binary32 as a fast sampler computes it), then an inverse-CDF draw. ``fault_rate``
-    replaces that share of the tokens (a per-row draw) with the row's lowest logit."""
+    replaces that share of the tokens (a per-row draw) with the row's lowest logit.
+
+    ``impl``: "kernel" runs `pck_sample_topk_topp` (one launch, one CTA per row; binary32
+    logits, k <= 1024), "torch" the same steps as torch operations (topk, softmax, cumsum,
+    searchsorted), as the reference's samplers are written."""
 
     def __init__(self, batch: int, vocab: int, k: int, p: float, temperature: float, device: torch.device,
-                 fault_rate: float = 0.0) -> None:  # fmt: skip
+                 fault_rate: float = 0.0, impl: str = "kernel") -> None:  # fmt: skip
         if not 1 <= k <= vocab or not 0 < p <= 1 or not temperature > 0:
             raise ValueError("need 1 <= k <= V, 0 < p <= 1 and temperature > 0")
+        if impl not in ("kernel", "torch") or (impl == "kernel" and k > 1024):
+            raise ValueError("impl is 'kernel' (k <= 1024) or 'torch'")
+        self.impl, self.vocab = impl, vocab
         self.k, self.p, self.temperature, self.fault_rate = k, p, temperature, fault_rate
         self.draw = torch.empty(batch, dtype=torch.float32, device=device)
         self.fault_draw = torch.empty(batch, dtype=torch.float32, device=device)
@@ -107,6 +114,8 @@ class TopKTopPSampler:
 
     def __call__(self, logits: torch.Tensor) -> torch.Tensor:
         self.draw.uniform_()
+        if self.impl == "kernel":
+            return self._kernel(logits)
         vals, idx = torch.topk(logits / self.temperature, self.k, dim=-1)  # descending
         probs = torch.softmax(vals, dim=-1)
         before = torch.cumsum(probs, dim=-1) - probs
@@ -122,6 +131,28 @@ class TopKTopPSampler:
             torch.lt(self.fault_draw, self.fault_rate, out=self.injected)
             tokens = torch.where(self.injected, logits.argmin(dim=-1), tokens)
         self.tokens.copy_(tokens)
+        return self.tokens
+
+    def _kernel(self, logits: torch.Tensor) -> torch.Tensor:
+        from pck.cuda import _lib
+        from pck.cuda._ext import on_device, stream_handle
+
+        if logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+            raise RuntimeError("logits must be float32 (B, V) with unit column stride")
+        if tuple(logits.shape) != (self.draw.numel(), self.vocab) or logits.device != self.draw.device:
+            raise RuntimeError("logits must be (batch, vocab) on the sampler's device")
+        faults = None
+        if self.fault_rate > 0:
+            self.fault_draw.uniform_()
+            faults = self.fault_draw.data_ptr()
+        else:
+            self.injected.zero_()
+        with on_device(logits.device):
+            rc = _lib.library().pck_sample_topk_topp(
+                logits.data_ptr(), logits.size(0), logits.size(1), logits.stride(0), self.k, float(self.p),
+                float(self.temperature), self.draw.data_ptr(), faults, float(self.fault_rate),
+                self.tokens.data_ptr(), self.injected.data_ptr() if faults else None, stream_handle(logits.device))
+        _lib.check(rc, "sampler kernel")
         return self.tokens
 
 

@@ -236,7 +236,9 @@ class TcLaunch:
             job = self._jobs[g]
             job.W, job.X, job.Y = W.data_ptr(), X.data_ptr(), y.data_ptr()
             job.m, job.n, job.batch, job.threads = W.size(0), W.size(1), batch, 256
-            job.weight_format = fmt | (_lib.PCK_TC_FULL_K if full_k else 0)
+            # the weights are final (synchronized below): the kernel may request its first
+            # tiles while the kernel before it still runs
+            job.weight_format = fmt | (_lib.PCK_TC_FULL_K if full_k else 0) | _lib.PCK_WEIGHTS_SETTLED
             if ch is None:
                 job.check = None
                 self.results.append(None)
@@ -259,6 +261,7 @@ class TcLaunch:
             d.c64 = ch.c64.data_ptr()
             job.check = ctypes.pointer(d)
             self.results.append(CheckResult(*out))
+        torch.cuda.synchronize(self.device)
 
     def launch(self) -> None:
         with on_device(self.device):

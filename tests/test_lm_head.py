@@ -110,3 +110,44 @@ def test_sharded_rows_reassemble_bitwise_on_one_gpu(head) -> None:
         full = torch.cat(parts, dim=-1)
         torch.cuda.synchronize()
         assert torch.equal(full.view(torch.int32), head.logits.view(torch.int32)), f"world {world}"
+
+
+def test_sampler_kernel_draws_as_the_torch_sampler(head) -> None:
+    """The fused sampler (`pck_sample_topk_topp`) against the torch sampler on the same logits
+    and the same uniform draws: every kernel token is one of the row's k largest logits and
+    inside the nucleus (probability mass before it, in descending order, below p, in binary64),
+    nearly every row picks the same token (the binary32 running sums may differ on a draw that
+    falls on a boundary), and the planted rows carry the row's argmin."""
+    from pck.cuda.lm_head import TopKTopPSampler
+
+    k, p = 50, 0.9
+    ker = TopKTopPSampler(BATCH, VOCAB, k, p, 1.0, head.device, fault_rate=0.05)
+    ref = TopKTopPSampler(BATCH, VOCAB, k, p, 1.0, head.device, fault_rate=0.05, impl="torch")
+    logits = head.logits
+    vals, idx = torch.topk(logits.double(), k, dim=-1)
+    probs = torch.softmax(vals, dim=-1)
+    before = torch.cumsum(probs, dim=-1) - probs
+    argmin = logits.argmin(dim=-1)
+    same = total = planted = 0
+    for step in range(20):
+        gen = torch.Generator(device=head.device).manual_seed(300 + step)
+        draws = torch.rand(BATCH, generator=gen, device=head.device)
+        faults = torch.rand(BATCH, generator=gen, device=head.device)
+        for s in (ker, ref):
+            s.draw.uniform_ = lambda d=draws, s=s: s.draw.copy_(d)  # noqa: B023 (fixed draws)
+            s.fault_draw.uniform_ = lambda f=faults, s=s: s.fault_draw.copy_(f)  # noqa: B023
+        t_ker = ker(logits).clone()
+        inj = ker.injected.clone()
+        t_ref = ref(logits).clone()
+        assert torch.equal(inj, ref.injected)
+        assert torch.equal(t_ker[inj], argmin[inj])
+        planted += int(inj.sum())
+        honest = ~inj
+        pos = (idx == t_ker.unsqueeze(-1))
+        assert bool(pos[honest].any(dim=-1).all()), "a token outside the top k"
+        b = (before * pos).sum(dim=-1)
+        assert bool((b[honest] < p).all()), "a token outside the nucleus"
+        same += int((t_ker == t_ref)[honest].sum())
+        total += int(honest.sum())
+    assert planted > 0
+    assert same >= 0.95 * total, f"{same} of {total} rows agree"
