@@ -96,6 +96,11 @@ __global__ void __launch_bounds__(kPeerThreads) peer_gather_flagged(const __grid
   unsigned int* epochs = reinterpret_cast<unsigned int*>(self + flags_offset(slice_bytes, p.world) +
                                                          PCK_PEER_MAX_RANKS * kCounterStride);
   __shared__ unsigned int s_epoch;
+  // Launched as the programmatic dependent of the kernel that wrote `local`: the next kernel
+  // may start now (it waits for this one before it writes anything), and this one waits for
+  // the previous before it reads.
+  allow_dependents();
+  wait_for_producers();
   if (threadIdx.x == 0) s_epoch = epochs[blockIdx.x] + 1;
   __syncthreads();
   const unsigned int e = s_epoch;
@@ -151,6 +156,8 @@ __global__ void __launch_bounds__(kPeerThreads) peer_gather_kernel(const __grid_
   unsigned int* epochs = reinterpret_cast<unsigned int*>(self + flags + PCK_PEER_MAX_RANKS * kCounterStride);
   __shared__ unsigned int s_epoch;
   __shared__ int s_ok;
+  allow_dependents();
+  wait_for_producers();
   if (threadIdx.x == 0) {
     s_epoch = epochs[blockIdx.x] + 1;
     s_ok = 1;
@@ -300,11 +307,16 @@ extern "C" int pck_peer_all_gather(const pck_peer_gather* g, void* stream) {
   const int64_t want = flagged ? (p.world * p.slice_words + pck::kPeerThreads - 1) / pck::kPeerThreads
                                : (p.slice_words + pck::kPeerThreads * 4 - 1) / (pck::kPeerThreads * 4);
   const int grid = static_cast<int>(want < 1 ? 1 : want > pck::kPeerMaxCtas ? pck::kPeerMaxCtas : want);
-  if (flagged) {
-    pck::peer_gather_flagged<<<grid, pck::kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  } else {
-    pck::peer_gather_kernel<<<grid, pck::kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  }
-  const cudaError_t err = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(pck::kPeerThreads);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // starts during the kernel before
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = flagged ? cudaLaunchKernelEx(&cfg, pck::peer_gather_flagged, p)
+                                  : cudaLaunchKernelEx(&cfg, pck::peer_gather_kernel, p);
   return err == cudaSuccess ? PCK_OK : peer_fail(PCK_ERR_CUDA, "peer gather kernel", err);
 }
