@@ -37,7 +37,8 @@ extern "C" {
  * synchronize). The streaming and tensor-core kernels then request their first weight
  * pieces while that kernel is still running (programmatic dependent launch); without the
  * flag they wait for the preceding kernel to complete before reading any weight, as they
- * always do for the checksum bank (c, a) and the activations. A caller that sets the flag
+ * do for the checksum bank (c, a) unless its check carries PCK_CHECK_BANK_SETTLED, and
+ * always for the activations. A caller that sets the flag
  * while the preceding kernel writes W can get stale weights and false alarms. (For
  * pck_gemv_tc every job of the call must carry it.)
  */
@@ -142,13 +143,22 @@ typedef struct pck_check_desc {
   int32_t checks;
   int32_t segments;     /* column segments per bank row, in [1, n]                        */
   int32_t batch;        /* columns of x and y, in [1, 16]                                 */
-  int32_t reserved;
+  int32_t flags;        /* 0 or PCK_CHECK_BANK_SETTLED                                    */
   double coef;          /* >= gamma_h + u32, rounded up                                   */
   double geps;          /* >= the checker's own rounding constant, rounded up             */
   double tau_floor;     /* >= n 2^-148, rounded up                                        */
   const double* c64;    /* optional: c widened to binary64, same shape (or NULL); the
                            tensor-core GEMV's fused reduction then reads it instead of c    */
 } pck_check_desc;
+
+/*
+ * Check flag: c and a were written before the kernel preceding this launch on the stream
+ * began (the bank is built at weight load), so the streaming kernel's bank CTAs may request
+ * their first bank pieces before that kernel completes, as PCK_WEIGHTS_SETTLED lets the row
+ * CTAs do for W (it takes effect in launches whose weights are all settled). A caller that
+ * sets it while the preceding kernel writes the bank can get false alarms.
+ */
+#define PCK_CHECK_BANK_SETTLED 0x1
 
 #define PCK_MAX_JOBS 16
 

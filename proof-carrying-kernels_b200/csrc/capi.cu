@@ -105,6 +105,7 @@ int validate_check(const pck_check_desc* d) {
   if (!(d->coef > 0) || !(d->geps > 0) || !(d->tau_floor > 0)) {
     return fail(PCK_ERR_ARGUMENT, "coef, geps and floor must be positive");
   }
+  if (d->flags & ~PCK_CHECK_BANK_SETTLED) return fail(PCK_ERR_ARGUMENT, "unknown check flags 0x%x", d->flags);
   return PCK_OK;
 }
 
@@ -114,8 +115,13 @@ constexpr int64_t kSegmentTarget = 2048;    // columns per checksum-bank segment
 // Time per byte of a bank segment (binary64 products and sums) relative to a weight row,
 // for the CTA split between the jobs of a launch.
 constexpr double kBankCost = 2.5;
-constexpr int kVerdictTasksPerWarp = 4;  // prior verdicts a warp decides, about
+constexpr int kVerdictTasksPerWarp = 4;  // prior verdicts a warp decides, about (long launches)
 constexpr int kMaxVerdictCtas = 8;
+// Weight bytes below which a launch is short enough that its prior verdicts, each task an
+// L2 round trip of about 1.5 us while the launch streams, would outlast its rows at 4 tasks
+// per warp: such launches get one task per warp (below the first) or two (below the second).
+constexpr int64_t kShortLaunchBytes = 64LL << 20;
+constexpr int64_t kMediumLaunchBytes = 128LL << 20;
 
 int64_t fill_verdicts(const pck_check_desc* const* descs, int count, const int32_t* fixed_segs,
                       pck::VerdictPlan& plan);
@@ -238,6 +244,7 @@ int plan_stream(const std::vector<Spec>& specs, const std::vector<const pck_chec
       pck::segment_split(d->n, d->segments, kSegmentTarget, &jb.seg_len, &jb.segs);
       jb.c = d->c;
       jb.a = static_cast<const uint16_t*>(d->a);
+      jb.bank_settled = (d->flags & PCK_CHECK_BANK_SETTLED) ? 1 : 0;
       jb.partial_cx = d->partial_cx;
       jb.partial_s = d->partial_s;
       jb.row_units = 0;
@@ -288,8 +295,8 @@ int plan_stream(const std::vector<Spec>& specs, const std::vector<const pck_chec
     plan.sum_bytes = static_cast<int32_t>(row_piece);
     bool checked = !prior.empty();
     for (const Spec* sp : live) checked = checked || sp->check != nullptr;
-    // Weight pieces before the producer wait only when every job's weights are settled (the
-    // bank CTAs never read before it: the bank may come from the kernel just before).
+    // Weight pieces before the producer wait only when every job's weights are settled; the
+    // bank CTAs take as many only for checks whose bank is settled too (PCK_CHECK_BANK_SETTLED).
     bool settled = true;
     for (const Spec* sp : live) settled = settled && (!sp->has_w || sp->settled);
     plan.pre_slots = !settled ? 0 : checked ? pck::kPreSlotsChecked : pck::kPreSlotsPlain;
@@ -298,12 +305,18 @@ int plan_stream(const std::vector<Spec>& specs, const std::vector<const pck_chec
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs
   // in proportion to their bytes, at least one each and never more than their units.
   // Prior verdicts: CTAs of their own past the streaming ones, about kVerdictTasksPerWarp
-  // tasks per warp (each a round trip to L2, so a few microseconds per CTA in all).
+  // tasks per warp (each a round trip to L2, so a few microseconds per CTA in all), fewer in
+  // short launches so that the verdicts end before the rows.
   int64_t prior_tasks = 0;
   int verdict_ctas = 0;
   if (!prior.empty()) {
     prior_tasks = fill_verdicts(prior.data(), static_cast<int>(prior.size()), nullptr, plan.prior);
-    const int64_t per_cta = static_cast<int64_t>(pck::kConsumerWarps) * kVerdictTasksPerWarp;
+    int64_t w_bytes = 0;
+    for (int j = 0; j < nj; ++j) w_bytes += plan.jobs[j].has_w ? plan.jobs[j].total_bytes : 0;
+    const int per_warp = w_bytes < kShortLaunchBytes    ? 1
+                         : w_bytes < kMediumLaunchBytes ? 2
+                                                        : kVerdictTasksPerWarp;
+    const int64_t per_cta = static_cast<int64_t>(pck::kConsumerWarps) * per_warp;
     verdict_ctas = static_cast<int>(std::min<int64_t>(kMaxVerdictCtas, (prior_tasks + per_cta - 1) / per_cta));
     verdict_ctas = std::max(verdict_ctas, 1);
   }

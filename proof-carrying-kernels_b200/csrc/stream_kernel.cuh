@@ -1415,9 +1415,11 @@ __global__ void __launch_bounds__(kPlainThreads, 1) stream_kernel(const __grid_c
       return jb.has_w && fma_is_exact<WFMT>(jb, xexp[0], xexp[1]) ? 1 : 0;
     };
     if (jb.has_check && !jb.has_w) {  // a bank CTA (uniform for the CTA)
-      // No bank piece before the producer wait: c and a may come from the kernel just before
-      // (pck_bank_build), whose writes are visible only after griddepcontrol.wait.
-      bank_warp(jb, u0, count, slots, 0, slot_bytes, ring, full, xs_addr, warp, lane, inputs);
+      // Bank pieces before the producer wait only for a settled bank: otherwise c and a may
+      // come from the kernel just before (pck_bank_build), whose writes are visible only
+      // after griddepcontrol.wait.
+      bank_warp(jb, u0, count, slots, jb.bank_settled ? plan.pre_slots : 0, slot_bytes, ring, full, xs_addr, warp,
+                lane, inputs);
     } else if (!jb.has_check && jb.rows == 1) {  // a row CTA
       row_warp<WFMT, NV, BG>(jb, u0, count, slots, plan.pre_slots, slot_bytes, row_piece, ring, full, xs_addr, warp,
                              lane, inputs);

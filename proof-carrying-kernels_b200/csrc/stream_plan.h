@@ -69,6 +69,7 @@ struct JobPlan {
   int32_t checks;
   int32_t seg_alloc;  // segment stride of the scratch arrays
   int32_t segs;       // effective segments (seg_len-aligned)
+  int32_t bank_settled;  // PCK_CHECK_BANK_SETTLED: bank pieces may be requested before the producer wait
   int64_t seg_len;    // columns per segment (multiple of 8)
   const float* c;
   const uint16_t* a;

@@ -16,6 +16,7 @@ PCK_OK = 0
 PCK_WEIGHTS_BF16 = 0
 PCK_WEIGHTS_E4M3 = 1
 PCK_WEIGHTS_SETTLED = 0x100  # weights written before the preceding kernel began
+PCK_CHECK_BANK_SETTLED = 0x1  # check flag: bank (c, a) written before the preceding kernel began
 PCK_TC_FULL_K = 0x200  # tensor-core GEMV: one accumulation chain over the whole K per output
 MAX_JOBS = 16  # PCK_MAX_JOBS
 MAX_BATCH = 16
@@ -36,7 +37,7 @@ class CheckDesc(ctypes.Structure):
         ("partial_cx", _p), ("partial_s", _p), ("counters", _p),
         ("passed", _p), ("rho", _p), ("tau", _p),
         ("n", _i64), ("block", _i32), ("num_blocks", _i32), ("checks", _i32),
-        ("segments", _i32), ("batch", _i32), ("reserved", _i32),
+        ("segments", _i32), ("batch", _i32), ("flags", _i32),
         ("coef", _f64), ("geps", _f64), ("tau_floor", _f64), ("c64", _p),
     ]  # fmt: skip
 

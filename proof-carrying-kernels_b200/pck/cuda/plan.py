@@ -91,12 +91,14 @@ class GemvLaunch:
                 out = (p.view(out[0].shape), out[1], out[2])
             self.results.append(CheckResult(*out))
             job.check = ctypes.pointer(self._descs[g])
-        # The weights are final from here on (a launch object is made at weight load), so the
-        # streaming kernel may request its first weight pieces before the preceding kernel on
-        # the stream has finished.
+        # The weights and the checkers' banks are final from here on (a launch object is made
+        # at weight load), so the streaming kernel may request its first weight and bank pieces
+        # before the preceding kernel on the stream has finished.
         torch.cuda.synchronize(self.device)
         for job in self._jobs:
             job.weight_format |= _lib.PCK_WEIGHTS_SETTLED
+        for desc in self._descs:
+            desc.flags |= _lib.PCK_CHECK_BANK_SETTLED
         self.prior: list[GemvLaunch] = []
         self._prior = None
         self.next: GemvLaunch | None = None

@@ -204,3 +204,47 @@ def test_chained_launches_with_next_prefetch_give_the_same_bits(fmt: str) -> Non
     for g, ref in zip(launches, refs, strict=True):
         assert torch.equal(g.ys[0].view(torch.int32), ref.view(torch.int32))
         assert bool(g.results[0].passed.all())
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")
+def test_settled_bank_gives_the_same_verdicts() -> None:
+    """Checks flagged PCK_CHECK_BANK_SETTLED (GemvLaunch's default: the bank CTAs request
+    their first pieces before the producer wait) decide every block as the same launches
+    without the flag, rho and tau bit for bit, with one planted fault caught either way;
+    unknown check flags are rejected."""
+    from pck.cuda import GpuBlockedChecker, _lib
+    from pck.cuda.plan import GemvLaunch
+    from pck.fp import tree_height
+
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    items = []
+    for i, (m, n) in enumerate([(1024, 4096), (512, 14336)]):
+        W = (torch.randn(m, n, generator=gen, device="cuda") * 0.02).bfloat16()
+        x = torch.randn(n, generator=gen, device="cuda").bfloat16()
+        ch = GpuBlockedChecker(W, 128, tree_height(n, 256, 8), generator=torch.Generator().manual_seed(40 + i))
+        items.append((W, x, ch))
+
+    def run(flags: int) -> list:
+        a = GemvLaunch([items[0]], 256, verdicts=False)
+        b = GemvLaunch([items[1]], 256, verdicts=False)
+        for g in (a, b):
+            for d in g._descs:
+                d.flags = flags
+        b.set_prior([a])
+        a.set_prior([b])
+        for _ in range(2):
+            a.launch()
+            b.launch()
+        b.ys[0][300] += 1.0  # a fault in block 2 of b's output, planted after b ran
+        a.launch()  # decides b's checks
+        torch.cuda.synchronize()
+        return [(r.passed.clone(), r.rho.clone(), r.tau.clone()) for g in (a, b) for r in g.results]
+
+    settled, plain = run(_lib.PCK_CHECK_BANK_SETTLED), run(0)
+    for (p1, r1, t1), (p0, r0, t0) in zip(settled, plain, strict=True):
+        assert torch.equal(p1, p0) and torch.equal(r1, r0) and torch.equal(t1, t0)
+    assert bool(settled[0][0].all())
+    assert not bool(settled[1][0][0, 2]) and int(settled[1][0].sum()) == settled[1][0].numel() - 1
+    with pytest.raises(RuntimeError, match="flags"):
+        run(0x2)
