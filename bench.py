@@ -137,31 +137,37 @@ def outlier_x(n: int, batch: int, gen: torch.Generator) -> torch.Tensor:
     return x.bfloat16()
 
 
-def build_layer(args, rank: int, world: int, device: torch.device, keep_full: bool = False):
+def build_layer(args, rank: int, world: int, device: torch.device, keep_full: bool = False, share=None):
     """Sharded weights, inputs, checkers and the launch objects of one decode layer. With
     ``keep_full``, also the unsharded weights of every projection (for the check that the
-    gathered outputs equal the single-GPU ones)."""
+    gathered outputs equal the single-GPU ones). With ``share`` (a layer built before), a
+    further copy of the layer in memory of its own (the same values) that writes the same
+    output, verdict and exchange buffers and reads the same activations, as the layers of a
+    model do."""
     from pck.cuda import GpuBlockedChecker
     from pck.cuda.plan import LLAMA3_8B_GROUPS, GemvLaunch, VerdictLaunch
     from pck.cuda.sharded import Exchange, shard_rows
     from pck.fp import tree_height
 
-    names = [p for g in LLAMA3_8B_GROUPS for p in g]
-    ms = [m for _, m, _ in names]
-    # one all-gather per step moves the outputs and the verdict bits of every projection
-    ex = Exchange([(ms, args.block, args.batch, torch.float32),
-                   ([m // args.block for m in ms], 1, args.checks, torch.bool)], world, rank, device)  # fmt: skip
-    ex_plain = Exchange([(ms, args.block, args.batch, torch.float32)], world, rank, device)
+    if share is None:
+        names = [p for g in LLAMA3_8B_GROUPS for p in g]
+        ms = [m for _, m, _ in names]
+        # one all-gather per step moves the outputs and the verdict bits of every projection
+        ex = Exchange([(ms, args.block, args.batch, torch.float32),
+                       ([m // args.block for m in ms], 1, args.checks, torch.bool)], world, rank, device)  # fmt: skip
+        ex_plain = Exchange([(ms, args.block, args.batch, torch.float32)], world, rank, device)
+        gen = torch.Generator().manual_seed(0)
+        # the layer's activations in one device buffer (each group's x a 16-byte aligned view),
+        # so a step's inputs arrive with one host-to-device copy
+        host_x = [outlier_x(group[0][2], args.batch, gen) for group in LLAMA3_8B_GROUPS]
+        x_all = torch.cat([h.reshape(-1) for h in host_x]).to(device)
+        views, off = [], 0
+        for h in host_x:
+            views.append(x_all[off : off + h.numel()].view(h.shape if args.batch > 1 else h.shape[1:]))
+            off += h.numel()
+    else:
+        ex, ex_plain, x_all, views = share
     ys, vs = ex.parts
-    gen = torch.Generator().manual_seed(0)
-    # the layer's activations in one device buffer (each group's x a 16-byte aligned view), so
-    # a step's inputs arrive with one host-to-device copy
-    host_x = [outlier_x(group[0][2], args.batch, gen) for group in LLAMA3_8B_GROUPS]
-    x_all = torch.cat([h.reshape(-1) for h in host_x]).to(device)
-    views, off = [], 0
-    for h in host_x:
-        views.append(x_all[off : off + h.numel()].view(h.shape if args.batch > 1 else h.shape[1:]))
-        off += h.numel()
     groups, plain, xs, full, j = [], [], [], [], 0
     for gi, group in enumerate(LLAMA3_8B_GROUPS):
         x = views[gi]
@@ -198,7 +204,31 @@ def build_layer(args, rank: int, world: int, device: torch.device, keep_full: bo
             g.set_next(plain[(i + 1) % len(plain)])
     torch.cuda.synchronize()
     build_layer.x_all = x_all  # the buffer behind xs (one copy per step in the end-to-end reading)
+    build_layer.share = (ex, ex_plain, x_all, views)
     return groups, verdict, plain, xs, ex, ex_plain, full
+
+
+def layer_copies(layer_bytes: int, steps: int) -> int:
+    """Copies of the layer a rank rotates through, one per step, so that the weights it reads
+    between two uses of the same bytes exceed L2 by half (a row shard at 4 or 8 GPUs fits in
+    L2 alone). The smallest count at least that for which some divisor of ``steps`` up to
+    GRAPH_STEPS is a multiple of it (the graphs then replay whole rotations)."""
+    need = max(1, -(-int(1.5 * L2_BYTES) // max(1, layer_bytes)))
+    for copies in range(need, GRAPH_STEPS + 1):
+        if any(steps % d == 0 and d % copies == 0 for d in range(copies, min(steps, GRAPH_STEPS) + 1)):
+            return copies
+    return max(1, graph_steps(steps))
+
+
+def rotation(fns):
+    """One call runs the next of ``fns`` in turn (a step of the next layer copy)."""
+    state = {"next": 0}
+
+    def step() -> None:
+        fns[state["next"] % len(fns)]()
+        state["next"] += 1
+
+    return step
 
 
 # Consecutive layer steps captured in one CUDA graph at most: a decode graph holds every
@@ -207,10 +237,13 @@ def build_layer(args, rank: int, world: int, device: torch.device, keep_full: bo
 GRAPH_STEPS = 32
 
 
-def graph_steps(steps: int) -> int:
-    """Steps per captured graph: the largest divisor of ``steps`` up to GRAPH_STEPS, so the
-    timed region replays whole graphs and holds exactly ``steps`` steps."""
-    return max(d for d in range(1, min(steps, GRAPH_STEPS) + 1) if steps % d == 0)
+def graph_steps(steps: int, copies: int = 1) -> int:
+    """Steps per captured graph: the largest divisor of ``steps`` up to GRAPH_STEPS (a multiple
+    of ``copies`` where one exists), so the timed region replays whole graphs and holds exactly
+    ``steps`` steps."""
+    ds = [d for d in range(1, min(steps, GRAPH_STEPS) + 1) if steps % d == 0]
+    whole = [d for d in ds if d % copies == 0]
+    return max(whole or ds)
 
 
 def cuda_graph(fn, steps: int = 1) -> tuple[torch.cuda.CUDAGraph, int]:
@@ -257,34 +290,38 @@ def timed(graph: tuple[torch.cuda.CUDAGraph, int], steps: int, warmup: int, worl
     return ms / 1e3 / steps
 
 
-def e2e_step_time(launches, x_all, ex, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
+def e2e_step_time(layers, x_all, ex, steps: int, warmup: int, world: int) -> tuple[float, int, int]:
     """The public API with host buffers (`pck.cuda.plan.CapturedStep`): every step copies the
-    layer's activations from pinned host memory, runs the layer's launches (and the gather),
-    and copies every output and verdict bit back to pinned host memory; one graph launch per
-    step. Device time per step, max over ranks."""
+    layer's activations from pinned host memory, runs the launches of the next layer copy in
+    ``layers`` (and the gather), and copies every output and verdict bit back to pinned host
+    memory; one graph launch per step. Device time per step, max over ranks."""
     from pck.cuda.plan import CapturedStep
 
     hx = [x_all.cpu().pin_memory()]  # x_all: the buffer the layer's activations are views of
     hout = torch.empty(ex.gathered.shape, dtype=ex.gathered.dtype, pin_memory=True)
 
-    def body() -> None:
-        for g in launches:
-            g.launch()
-        if world > 1:
-            ex.gather()
+    def body_of(launches):
+        def body() -> None:
+            for g in launches:
+                g.launch()
+            if world > 1:
+                ex.gather()
+
+        return body
 
     result = ex.gathered if world > 1 else ex.local
     hres = hout if world > 1 else torch.empty(ex.local.shape, dtype=ex.local.dtype, pin_memory=True)
-    step = CapturedStep(body, [(hx[0], x_all)], [(result, hres)])
-    for _ in range(warmup):
-        step.run()
+    captured = [CapturedStep(body_of(launches), [(hx[0], x_all)], [(result, hres)]) for launches in layers]
+    step = rotation([c.run for c in captured])
+    for _ in range(-(-warmup // len(captured)) * len(captured)):
+        step()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(steps):
-        step.run()
+        step()
     end.record()
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
@@ -292,23 +329,25 @@ def e2e_step_time(launches, x_all, ex, steps: int, warmup: int, world: int) -> t
         t = torch.tensor([ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
-    h2d, d2h = step.h2d_bytes, step.d2h_bytes
-    del step
+    h2d, d2h = captured[0].h2d_bytes, captured[0].d2h_bytes
+    del step, captured
     return ms / 1e3 / steps, h2d, d2h
 
 
-def launch_times(fns, steps: int, world: int) -> list[float]:
-    """Device time of each launch of a step, in ms: the step issued eagerly ``steps`` times
-    with a CUDA event between consecutive launches (on the launching stream), averaged. The
-    events keep each launch from overlapping its neighbour, so the sum is a little above the
-    graph's time per step."""
-    events = [torch.cuda.Event(enable_timing=True) for _ in range(len(fns) + 1)]
-    totals = [0.0] * len(fns)
-    for _ in range(3):
-        for f in fns:
+def launch_times(fn_sets, steps: int, world: int) -> list[float]:
+    """Device time of each launch of a step, in ms: the step (the launches of the next layer
+    copy in ``fn_sets``) issued eagerly ``steps`` times with a CUDA event between consecutive
+    launches (on the launching stream), averaged. The events keep each launch from overlapping
+    its neighbour, so the sum is a little above the graph's time per step."""
+    nf = len(fn_sets[0])
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(nf + 1)]
+    totals = [0.0] * nf
+    for s in range(3 * len(fn_sets)):
+        for f in fn_sets[s % len(fn_sets)]:
             f()
     torch.cuda.synchronize()
-    for _ in range(steps):
+    for s in range(steps):
+        fns = fn_sets[s % len(fn_sets)]
         events[0].record()
         for i, f in enumerate(fns):
             f()
@@ -464,7 +503,7 @@ def e4m3_reading(args, device, steps: int, warmup: int) -> dict:
     passed = bool(ex.parts[1].local.all())
     t_checked = timed(g_checked, steps, warmup, 1)
     t_plain = timed(g_plain, steps, warmup, 1)
-    per_launch = launch_times([g.launch for g in groups], max(10, steps), 1)
+    per_launch = launch_times([[g.launch for g in groups]], max(10, steps), 1)
     step_bytes = sum(g.algorithmic_bytes for g in groups)
     value = step_bytes / t_checked / 1e9
     peak = float(measured_peaks()["hbm_gbs"])
@@ -637,12 +676,20 @@ def main() -> None:
                                              device_id=device)  # fmt: skip
 
     groups, verdict, plain, xs, ex, ex_plain, full = build_layer(args, rank, world, device, keep_full=world > 1)
-    if world > 1 and args.gather == "peer":
-        ex.use_peer_memory()
-        ex_plain.use_peer_memory()
     x_all = build_layer.x_all
     vs = ex.parts[1]
     step_bytes_local = sum(g.algorithmic_bytes for g in groups)
+    # Layer copies in rotation, one per step, so that a rank's weights exceed L2 between reuses
+    # (each copy its own memory, the same values, writing the same output buffers).
+    copies = layer_copies(step_bytes_local, args.steps)
+    layers = [(groups, verdict, plain)]
+    share = build_layer.share
+    for _ in range(copies - 1):
+        g2, v2, p2, *_ = build_layer(args, rank, world, device, share=share)
+        layers.append((g2, v2, p2))
+    if world > 1 and args.gather == "peer":
+        ex.use_peer_memory()
+        ex_plain.use_peer_memory()
 
     def step_of(launches):
         def checked_step() -> None:
@@ -654,27 +701,43 @@ def main() -> None:
         return checked_step
 
     # the other verdict form, for comparison (captured before the launches are re-planned)
-    per_graph = graph_steps(args.steps)
-    graph_other = cuda_graph(step_of([*groups, verdict]), per_graph) if args.verdicts == "carried" else None
+    per_graph = graph_steps(args.steps, copies)
+    graph_other = (cuda_graph(rotation([step_of([*g, v]) for g, v, _ in layers]), per_graph)
+                   if args.verdicts == "carried" else None)  # fmt: skip
+    chain = [g for gs, _, _ in layers for g in gs]  # every launch of the rotation, in order
     if args.verdicts == "carried":  # each launch decides the previous one's checks
-        for i, g in enumerate(groups):
-            g.set_prior([groups[i - 1]])
+        for i, g in enumerate(chain):
+            g.set_prior([chain[i - 1]])
             if not args.no_prefetch:  # and prefetches the next one's first weight pieces
-                g.set_next(groups[(i + 1) % len(groups)])
-        launches = list(groups)
+                g.set_next(chain[(i + 1) % len(chain)])
+        layer_launches = [list(gs) for gs, _, _ in layers]
     else:
-        launches = [*groups, verdict]
-    checked_step = step_of(launches)
+        layer_launches = [[*gs, v] for gs, v, _ in layers]
+    launches = layer_launches[0]
+    checked_step = rotation([step_of(ls) for ls in layer_launches])
+    plain_chain = [g for _, _, ps in layers for g in ps]
+    if not args.no_prefetch:
+        for i, g in enumerate(plain_chain):
+            g.set_next(plain_chain[(i + 1) % len(plain_chain)])
 
-    def plain_step() -> None:
-        for g in plain:
-            g.launch()
-        if world > 1:
-            ex_plain.gather()
+    def plain_of(ps):
+        def plain_step() -> None:
+            for g in ps:
+                g.launch()
+            if world > 1:
+                ex_plain.gather()
 
-    def local_step() -> None:  # the launches alone, without the gather (N > 1 breakdown)
-        for g in launches:
-            g.launch()
+        return plain_step
+
+    def local_of(ls):
+        def local_step() -> None:  # the launches alone, without the gather (N > 1 breakdown)
+            for g in ls:
+                g.launch()
+
+        return local_step
+
+    plain_step = rotation([plain_of(ps) for _, _, ps in layers])
+    local_step = rotation([local_of(ls) for ls in layer_launches])
 
     graph_checked = cuda_graph(checked_step, per_graph)
     graph_plain = cuda_graph(plain_step, per_graph)
@@ -701,7 +764,8 @@ def main() -> None:
         t_local = timed(graph_local, args.steps, args.warmup, world) if graph_local is not None else None
     clock = clocks.summary()
     side_steps = max(20, args.steps // 10)
-    per_launch = launch_times([g.launch for g in launches] + ([ex.gather] if world > 1 else []), side_steps, world)
+    per_launch = launch_times([[g.launch for g in ls] + ([ex.gather] if world > 1 else []) for ls in layer_launches],
+                              side_steps, world)  # fmt: skip
     batch128 = e4m3 = lm_head = None
     if world == 1 and args.weights == "bf16" and args.batch == 1 and not args.no_batch128:
         batch128 = batch128_reading(args, groups, device, side_steps, args.warmup)
@@ -709,7 +773,7 @@ def main() -> None:
         e4m3 = e4m3_reading(args, device, side_steps, args.warmup)
     if not args.no_lm_head:
         lm_head = lm_head_reading(rank, world, device, side_steps, args.warmup, args.gather)
-    t_e2e, h2d, d2h = e2e_step_time(launches, x_all, ex, side_steps, args.warmup, world)
+    t_e2e, h2d, d2h = e2e_step_time(layer_launches, x_all, ex, side_steps, args.warmup, world)
 
     total_bytes = torch.tensor([float(step_bytes_local)], device=device)
     if world > 1:
@@ -743,7 +807,9 @@ def main() -> None:
                 "batch": args.batch, "block": args.block, "checks": args.checks, "threads": args.threads,
                 "launches_per_step": len(launches),
                 "verdicts": VERDICTS[args.verdicts], "parallelism": f"row-shard x{world}" if world > 1 else "single",
-                "l2": "inputs larger than L2 (436 MB of weights per step, 126 MB L2)",
+                "l2": f"inputs larger than L2: {copies} layer cop{'y' if copies == 1 else 'ies'} in rotation, one per "
+                      f"step, {copies * step_bytes_local / 1e6:.0f} MB of weights per rank between reuses, 126 MB L2",
+                "layer_copies": copies,
                 "graph": f"CUDA graph of {per_graph} consecutive steps, replayed",
                 "prefetch": "none" if args.no_prefetch else
                             "each launch's CTAs prefetch the next launch's first weight pieces into L2 as they finish",

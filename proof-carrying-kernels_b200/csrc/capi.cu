@@ -113,15 +113,21 @@ constexpr int64_t kPieceTarget = 4 * 1024;  // row piece size the staged path ai
 constexpr int kMaxSlots = 4;                // ring slots per warp
 constexpr int64_t kSegmentTarget = 2048;    // columns per checksum-bank segment
 // Time per byte of a bank segment (binary64 products and sums) relative to a weight row,
-// for the CTA split between the jobs of a launch.
-constexpr double kBankCost = 2.5;
-constexpr int kVerdictTasksPerWarp = 4;  // prior verdicts a warp decides, about (long launches)
+// for the CTA split between the jobs of a launch: bfloat16 rows, and E4M3 rows (twice the
+// weights per byte, so the bank costs less against them). Measured: the CTAs of both kinds
+// end together.
+constexpr double kBankCostBf16 = 2.5;
+constexpr double kBankCostE4m3 = 1.8;
 constexpr int kMaxVerdictCtas = 8;
-// Weight bytes below which a launch is short enough that its prior verdicts, each task an
-// L2 round trip of about 1.5 us while the launch streams, would outlast its rows at 4 tasks
-// per warp: such launches get one task per warp (below the first) or two (below the second).
-constexpr int64_t kShortLaunchBytes = 64LL << 20;
-constexpr int64_t kMediumLaunchBytes = 128LL << 20;
+// Prior verdicts: a warp's tasks run one after another, each an L2 round trip while the
+// launch saturates HBM. A verdict CTA ends about kVerdictBaseUs + kVerdictTaskUs per task
+// after the producer wait, the rows about their bytes over the per-format streaming rate
+// (bytes per microsecond) after it; a warp takes 4, 2 or 1 tasks, the most that still end
+// before the rows.
+constexpr double kVerdictBaseUs = 2.5;
+constexpr double kVerdictTaskUs = 1.5;
+constexpr double kRowBytesPerUsBf16 = 6.0e6;
+constexpr double kRowBytesPerUsE4m3 = 5.0e6;
 
 int64_t fill_verdicts(const pck_check_desc* const* descs, int count, const int32_t* fixed_segs,
                       pck::VerdictPlan& plan);
@@ -254,7 +260,8 @@ int plan_stream(const std::vector<Spec>& specs, const std::vector<const pck_chec
       jb.total_bytes = jb.period_bytes * d->num_blocks;
       x_bytes = std::max<int64_t>(x_bytes, static_cast<int64_t>(jb.batch) * jb.n * 2);
       plan.jobs[nj++] = jb;
-      bytes.push_back(static_cast<double>(jb.total_bytes) * kBankCost);
+      bytes.push_back(static_cast<double>(jb.total_bytes) *
+                      (wfmt == pck::kWeightsBf16 ? kBankCostBf16 : kBankCostE4m3));
     }
   }
 
@@ -304,18 +311,23 @@ int plan_stream(const std::vector<Spec>& specs, const std::vector<const pck_chec
 
   // CTAs: one per SM in total (two without shared-memory staging), split between the jobs
   // in proportion to their bytes, at least one each and never more than their units.
-  // Prior verdicts: CTAs of their own past the streaming ones, about kVerdictTasksPerWarp
-  // tasks per warp (each a round trip to L2, so a few microseconds per CTA in all), fewer in
-  // short launches so that the verdicts end before the rows.
+  // Prior verdicts: CTAs of their own past the streaming ones, 4, 2 or 1 tasks per warp by
+  // the launch's length (kVerdictBaseUs above).
   int64_t prior_tasks = 0;
   int verdict_ctas = 0;
   if (!prior.empty()) {
     prior_tasks = fill_verdicts(prior.data(), static_cast<int>(prior.size()), nullptr, plan.prior);
     int64_t w_bytes = 0;
     for (int j = 0; j < nj; ++j) w_bytes += plan.jobs[j].has_w ? plan.jobs[j].total_bytes : 0;
-    const int per_warp = w_bytes < kShortLaunchBytes    ? 1
-                         : w_bytes < kMediumLaunchBytes ? 2
-                                                        : kVerdictTasksPerWarp;
+    const double rows_us =
+        static_cast<double>(w_bytes) / (wfmt == pck::kWeightsBf16 ? kRowBytesPerUsBf16 : kRowBytesPerUsE4m3);
+    int per_warp = 1;
+    for (int t : {4, 2}) {
+      if (kVerdictBaseUs + kVerdictTaskUs * t <= rows_us) {
+        per_warp = t;
+        break;
+      }
+    }
     const int64_t per_cta = static_cast<int64_t>(pck::kConsumerWarps) * per_warp;
     verdict_ctas = static_cast<int>(std::min<int64_t>(kMaxVerdictCtas, (prior_tasks + per_cta - 1) / per_cta));
     verdict_ctas = std::max(verdict_ctas, 1);
@@ -373,8 +385,22 @@ int plan_stream(const std::vector<Spec>& specs, const std::vector<const pck_chec
     return fail(PCK_ERR_ARGUMENT, "streaming grid of %lld CTAs exceeds %d", static_cast<long long>(begin + verdict_ctas),
                 pck::kMaxCtas);
   }
-  begin = 0;
+  // Bank jobs take the grid's first CTAs. A dependent launch's CTAs start in index order on
+  // the SMs the previous launch frees, and a CTA's prologue (its share of the launch
+  // parameters, read through the constant cache while HBM is saturated) takes over a
+  // microsecond; the row CTAs that start last hide it behind little work, the bank CTAs,
+  // whose segment sums take longest after the producer wait, would not.
+  int order[pck::kMaxPlanJobs];
+  int no = 0;
   for (int j = 0; j < nj; ++j) {
+    if (!plan.jobs[j].has_w) order[no++] = j;
+  }
+  for (int j = 0; j < nj; ++j) {
+    if (plan.jobs[j].has_w) order[no++] = j;
+  }
+  begin = 0;
+  for (int oi = 0; oi < nj; ++oi) {
+    const int j = order[oi];
     pck::JobPlan& jb = plan.jobs[j];
     jb.cta_begin = static_cast<int32_t>(begin);
     jb.cta_count = static_cast<int32_t>(cnt[j]);

@@ -693,21 +693,35 @@ __device__ __forceinline__ void load_activations(const JobPlan& jb, uint8_t* xs,
   const bool split = WFMT == kWeightsE4m3 && jb.has_w;  // n % 16 == 0 on the staged path
   const uint32_t cw = static_cast<uint32_t>(jb.n / 8);  // 16-byte words per column
   unsigned mn = 1000, mx = 0;
-  for (int64_t i = tid; i < words; i += kPlainThreads) {
-    const uint4 v = __ldcg(src + i);
-    if (split) {
-      const uint32_t b = static_cast<uint32_t>(i) / cw, w = static_cast<uint32_t>(i) - b * cw;
-      dst[b * cw + (w & 1u) * (cw / 2) + (w >> 1)] = v;
-    } else {
-      dst[i] = v;
-    }
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  // Up to kXLoads loads of a thread in flight before any store: the activations come after
+  // the producer wait, while HBM traffic makes every L2 round trip long.
+  constexpr int kXLoads = 4;
+  for (int64_t base = tid; base < words; base += kXLoads * kPlainThreads) {
+    uint4 vs[kXLoads];
 #pragma unroll
-    for (int h = 0; h < 8; ++h) {
-      const unsigned mag = (h & 1 ? w[h / 2] >> 16 : w[h / 2]) & 0x7fffu;
-      const unsigned e = mag >> 7;
-      mx = max(mx, e);
-      if (mag) mn = min(mn, max(e, 1u));
+    for (int u = 0; u < kXLoads; ++u) {
+      const int64_t i = base + static_cast<int64_t>(u) * kPlainThreads;
+      if (i < words) vs[u] = __ldcg(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kXLoads; ++u) {
+      const int64_t i = base + static_cast<int64_t>(u) * kPlainThreads;
+      if (i >= words) break;
+      const uint4 v = vs[u];
+      if (split) {
+        const uint32_t b = static_cast<uint32_t>(i) / cw, w = static_cast<uint32_t>(i) - b * cw;
+        dst[b * cw + (w & 1u) * (cw / 2) + (w >> 1)] = v;
+      } else {
+        dst[i] = v;
+      }
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        const unsigned mag = (h & 1 ? w[h / 2] >> 16 : w[h / 2]) & 0x7fffu;
+        const unsigned e = mag >> 7;
+        mx = max(mx, e);
+        if (mag) mn = min(mn, max(e, 1u));
+      }
     }
   }
   if (jb.has_w) {
