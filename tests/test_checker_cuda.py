@@ -292,9 +292,10 @@ def test_an_overflowing_threshold_fails_closed() -> None:
 def test_bank_built_just_before_a_checked_launch(settled: bool) -> None:
     """pck_bank_build directly followed, on the same stream and with no synchronization, by a
     checked launch that reads the new bank: the launch waits for the bank kernel before it
-    reads c and a (the bank CTAs never prefetch), so the verdicts equal those of the same
-    launch run after a synchronize. Settled weights (PCK_WEIGHTS_SETTLED) change nothing
-    here: only W, written long before, is read early."""
+    reads c and a (the bank CTAs prefetch only for checks flagged PCK_CHECK_BANK_SETTLED, which
+    this one is not), so the verdicts equal those of the same launch run after a synchronize.
+    Settled weights (PCK_WEIGHTS_SETTLED) change nothing here: only W, written long before, is
+    read early."""
     import ctypes
 
     from pck.cuda import _lib
