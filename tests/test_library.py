@@ -85,6 +85,19 @@ def test_blocked_check_rejects_bad_batches(lib) -> None:
     assert lib.pck_blocked_check(descs, 1, None) == 1 and "segments" in _err(lib)
     d.segments, d.geps = 1, 0.0
     assert lib.pck_blocked_check(descs, 1, None) == 1 and "positive" in _err(lib)
+    d.geps, d.flags = 1e-12, 0x2
+    assert lib.pck_blocked_check(descs, 1, None) == 1 and "flags" in _err(lib)
+
+
+def test_check_flag_constants_match_the_header() -> None:
+    """The ctypes binding's flag values and the CheckDesc field are the header's."""
+    from pck.cuda import _lib
+
+    text = HEADER.read_text()
+    for name in ("PCK_CHECK_BANK_SETTLED", "PCK_WEIGHTS_SETTLED", "PCK_TC_FULL_K"):
+        m = re.search(rf"#define {name} (0x[0-9a-fA-F]+|\d+)", text)
+        assert m and int(m.group(1), 0) == getattr(_lib, name), name
+    assert "int32_t flags;" in text and "flags" in dict(_lib.CheckDesc._fields_)
 
 
 def test_fused_check_must_cover_its_job(lib) -> None:
