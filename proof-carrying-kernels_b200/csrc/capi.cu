@@ -387,9 +387,10 @@ int plan_stream(const std::vector<Spec>& specs, const std::vector<const pck_chec
   }
   // Bank jobs take the grid's first CTAs. A dependent launch's CTAs start in index order on
   // the SMs the previous launch frees, and a CTA's prologue (its share of the launch
-  // parameters, read through the constant cache while HBM is saturated) takes over a
-  // microsecond; the row CTAs that start last hide it behind little work, the bank CTAs,
-  // whose segment sums take longest after the producer wait, would not.
+  // parameters, read through the constant cache while HBM is saturated, then its first
+  // requests) takes over a microsecond. The CTAs that start first have it done, and their
+  // first pieces in flight, before the producer wait returns; the bank CTAs, whose segment
+  // sums take longest after the wait, go first.
   int order[pck::kMaxPlanJobs];
   int no = 0;
   for (int j = 0; j < nj; ++j) {
